@@ -1,0 +1,483 @@
+#!/usr/bin/env python
+"""Benchmark: fused mHC layer forward + backward on B200.
+
+Workload (BASELINE.json target): MHCLayer(n=4, C=4096), T = 65,536 tokens
+per GPU, one training step = parameter kernel + fused forward + fused
+backward + finalize (+ one NCCL all-reduce of the mHC parameter gradients
+when N > 1) + an SGD update of the mHC parameters.  Synthetic N(0, 1)
+activations and upstream gradients, H_* logits ~ N(0, 0.1), rms_weight = 1
+(BASELINE config 2 distributions).  Inputs (4 GiB fp32 per tensor) are far
+larger than the 126 MB L2, so no flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                  [--io-dtype f32|bf16] [--tokens T]
+
+Under torchrun (N > 1) each rank processes T tokens (weak scaling); the
+reported time is the max over ranks of CUDA-event time.  `--impl reference`
+times the reference's CPU algorithm (the oracle restatement of
+mhc_mlx/reference.py with autograd) on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "mhc-mlx_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "mHC fwd+bwd tokens/s (n=4, C=4096, 64K tokens/GPU)"
+UNIT = "tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--io-dtype", choices=["f32", "bf16"], default="f32")
+    ap.add_argument("--tokens", type=int, default=65536)
+    ap.add_argument("--n", type=int, default=4)
+    ap.add_argument("--C", type=int, default=4096)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-latency", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    return ap.parse_args()
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_bench_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sms, maxs, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxs.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
+        return {"sm_mhz": statistics.median(sms) if sms else None,
+                "sm_max_mhz": max(maxs) if maxs else None, "samples": len(sms),
+                "reasons": sorted(reasons)}
+
+
+# --------------------------------------------------------------- workload --
+def algo_bytes(T, n, C, s_x, s_out, s_dout, s_dx):
+    """Algorithmic HBM bytes per launch (one read of every input, one write of
+    every output; the O(C) parameter traffic added per call)."""
+    fwd = T * n * C * (s_x + s_out) + 4 * C
+    bwd = T * n * C * (s_x + s_dout + s_dx) + 8 * C
+    return fwd, bwd
+
+
+def make_layer(n, C, dev):
+    import mhc_b200
+
+    layer = mhc_b200.MHCLayer(n=n, C=C, identity_init=False).to(dev)
+    g = torch.Generator().manual_seed(2024)  # same parameters on every rank
+    with torch.no_grad():
+        layer.H_pre_raw.copy_(0.1 * torch.randn(n, generator=g))
+        layer.H_post_raw.copy_(0.1 * torch.randn(n, generator=g))
+        layer.H_res_raw.copy_(0.1 * torch.randn(n, n, generator=g))
+        layer.rms_weight.fill_(1.0)
+    return layer
+
+
+def make_step(layer, x, d, rdt, world):
+    from mhc_b200 import dist as mdist
+
+    params = list(layer.parameters())
+
+    def step():
+        for p in params:
+            p.grad = None
+        x.grad = None
+        out = layer(x, return_dtype=rdt)
+        out.backward(d)
+        if world > 1:
+            mdist.allreduce_grads(params)
+        with torch.no_grad():
+            torch._foreach_add_(params, [p.grad for p in params], alpha=-1e-3)
+        return out
+
+    return step
+
+
+def timed_loop(step, steps, warmup, world, dev):
+    """W untimed steps, then K steps between CUDA events (barrier + sync on
+    both sides); returns (max-over-ranks ms, per-kernel event stats, launches)."""
+    import torch.distributed as dist
+
+    from mhc_b200 import _capi, _kernels
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    st = torch.cuda.current_stream(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _kernels.TIMING = {}
+    calls0 = _capi.CALLS
+    a.record(st)
+    for _ in range(steps):
+        step()
+    b.record(st)
+    torch.cuda.synchronize(dev)
+    launches = _capi.CALLS - calls0
+    timing, _kernels.TIMING = _kernels.TIMING, None
+    if world > 1:
+        dist.barrier()
+    ms = a.elapsed_time(b)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t)
+    kstats = {k: {"launches": len(v), "avg_us": 1e3 * statistics.mean(e0.elapsed_time(e1) for e0, e1 in v)}
+              for k, v in timing.items()}
+    return ms, kstats, launches
+
+
+def e2e_measure(layer, T, n, C, iodt, rdt, dev, steps, world, chunks=8):
+    """Same step through the public API with host buffers: pinned host x and
+    d_out are copied in, out and dx copied back every step, pipelined in
+    token chunks (H2D of chunk i+1 and D2H of chunk i-1 overlap compute)."""
+    import torch.distributed as dist
+
+    from mhc_b200 import dist as mdist
+
+    odt = rdt or torch.float32
+    Tc = T // chunks
+    x_h = torch.empty(chunks, Tc, n, C, dtype=iodt, pin_memory=True)
+    d_h = torch.empty(chunks, Tc, n, C, dtype=odt, pin_memory=True)
+    out_h = torch.empty(chunks, Tc, n, C, dtype=odt, pin_memory=True)
+    dx_h = torch.empty(chunks, Tc, n, C, dtype=iodt, pin_memory=True)
+    g = torch.Generator(device=dev).manual_seed(7)
+    for i in range(chunks):
+        x_h[i].copy_(torch.randn(Tc, n, C, device=dev, generator=g).to(iodt))
+        d_h[i].copy_(torch.randn(Tc, n, C, device=dev, generator=g).to(odt))
+    xd = [torch.empty(Tc, n, C, dtype=iodt, device=dev) for _ in range(2)]
+    dd = [torch.empty(Tc, n, C, dtype=odt, device=dev) for _ in range(2)]
+    params = list(layer.parameters())
+    comp = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_free = [torch.cuda.Event() for _ in range(2)]
+    for e in ev_free:
+        e.record(comp)
+
+    def step():
+        for p in params:
+            p.grad = None
+        for i in range(chunks):
+            bsel = i % 2
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(ev_free[bsel])
+                xd[bsel].copy_(x_h[i], non_blocking=True)
+                dd[bsel].copy_(d_h[i], non_blocking=True)
+                ev_in[bsel].record(s_in)
+            comp.wait_event(ev_in[bsel])
+            xg = xd[bsel].detach().requires_grad_(True)
+            out = layer(xg, return_dtype=rdt)
+            out.backward(dd[bsel])
+            dx = xg.grad
+            ev_free[bsel].record(comp)
+            s_out.wait_stream(comp)
+            with torch.cuda.stream(s_out):
+                out_h[i].copy_(out, non_blocking=True)
+                dx_h[i].copy_(dx, non_blocking=True)
+            out.record_stream(s_out)
+            dx.record_stream(s_out)
+        if world > 1:
+            mdist.allreduce_grads(params)
+        with torch.no_grad():
+            torch._foreach_add_(params, [p.grad for p in params], alpha=-1e-3)
+        comp.wait_stream(s_out)
+
+    step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(comp)
+    for _ in range(steps):
+        step()
+    b.record(comp)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t)
+    s_x, s_o = x_h.element_size(), out_h.element_size()
+    return {"value": world * T / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms,
+            "h2d_bytes_per_step": T * n * C * (s_x + s_o),
+            "d2h_bytes_per_step": T * n * C * (s_o + s_x),
+            "path": f"MHCLayer forward+backward on pinned host tensors, {chunks} token chunks, "
+                    "H2D/compute/D2H overlapped on 3 streams"}
+
+
+def cpu_oracle_step(T, n, C, iters, dtype=torch.float32, seed=0):
+    from oracle import mhc_oracle as O
+
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(T, n, C, generator=g)
+    d = torch.randn(T, n, C, generator=g)
+    params = [0.1 * torch.randn(n, generator=g), 0.1 * torch.randn(n, generator=g),
+              0.1 * torch.randn(n, n, generator=g), torch.ones(C)]
+    t0 = time.perf_counter()
+    O.layer_grads(x, *params, d, iters, 1e-5, dtype=dtype)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(n, C, seconds, iters=20):
+    """The oracle restatement of reference.py (torch CPU, fp32, autograd
+    backward) on all host cores, on a bounded token sample."""
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    t_probe = cpu_oracle_step(64, n, C, iters)
+    per_tok = t_probe / 64
+    T = int(max(64, min(65536, (seconds / 3) / per_tok)))
+    times = [cpu_oracle_step(T, n, C, iters, seed=k) for k in range(3)]
+    med = statistics.median(times)
+    return {"value": T / med, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{T} of the 65536 tokens per step, fwd+bwd fp32 (oracle restatement of "
+                      f"mhc_mlx/reference.py + torch autograd), median of 3, {torch.get_num_threads()} threads"}
+
+
+def latency_b1(layer, n, C, dev, iters=1000):
+    """T = 1 latency per call (CUDA events around each call, median/p10/p90)."""
+    x = torch.randn(1, n, C, device=dev, requires_grad=True)
+    d = torch.randn(1, n, C, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def measure(fn):
+        for _ in range(20):
+            fn()
+        torch.cuda.synchronize(dev)
+        ts = []
+        for _ in range(iters):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            fn()
+            b.record(st)
+            ts.append((a, b))
+        torch.cuda.synchronize(dev)
+        v = sorted(1e3 * a.elapsed_time(b) for a, b in ts)
+        return {"median_us": v[len(v) // 2], "p10_us": v[len(v) // 10], "p90_us": v[9 * len(v) // 10]}
+
+    def fwd():
+        with torch.no_grad():
+            layer(x)
+
+    def fwd_bwd():
+        x.grad = None
+        for p in layer.parameters():
+            p.grad = None
+        layer(x).backward(d)
+
+    return {"fwd": measure(fwd), "fwd_bwd": measure(fwd_bwd)}
+
+
+def traffic_from_profile(name):
+    p = ROOT / "profiles" / "roofline_traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return d.get(name)
+
+
+# ------------------------------------------------------------------- arms --
+def run_b200(args):
+    import torch.distributed as dist
+
+    rank, local, world = env_rank()
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    T, n, C = args.tokens, args.n, args.C
+    peak, peak_kind = load_peaks()
+
+    def measure(io: str, steps: int, clocks: bool):
+        iodt = torch.float32 if io == "f32" else torch.bfloat16
+        rdt = None if io == "f32" else torch.bfloat16  # bf16 I/O end to end
+        odt = rdt or torch.float32
+        layer = make_layer(n, C, dev)
+        g = torch.Generator(device=dev).manual_seed(1234 + rank)
+        x = torch.randn(T, n, C, device=dev, generator=g).to(iodt).requires_grad_(True)
+        d = torch.randn(T, n, C, device=dev, generator=g).to(odt)
+        step = make_step(layer, x, d, rdt, world)
+        sampler = ClockSampler(local) if clocks else None
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize(dev)
+        if sampler:
+            sampler.start()
+            time.sleep(0.3)
+        ms, kstats, launches = timed_loop(step, steps, args.warmup, world, dev)
+        clk = sampler.stop() if sampler else None
+        sx, so = x.element_size(), d.element_size()
+        fwd_b, bwd_b = algo_bytes(T, n, C, sx, so, so, sx)
+        del x, d, step
+        torch.cuda.empty_cache()
+        return layer, ms / steps, kstats, launches, clk, fwd_b, bwd_b
+
+    layer, ms, kstats, launches, clk, fwd_b, bwd_b = measure(args.io_dtype, args.steps, True)
+    value = world * T / (ms * 1e-3)
+    dom = "mhc_bwd"
+    bwd_us = kstats.get(dom, {}).get("avg_us")
+    achieved = bwd_b / (bwd_us * 1e-6) / 1e9 if bwd_us else None
+    fwd_us = kstats.get("mhc_fwd", {}).get("avg_us")
+    res = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"MHCLayer fwd+bwd (+grad all-reduce, SGD) T={T} tokens/GPU, n={n}, "
+                               f"C={C}, {args.io_dtype} I/O, fp32 math, 20 Sinkhorn iters",
+                   "tokens_per_gpu": T, "n": n, "C": C, "io_dtype": args.io_dtype,
+                   "sinkhorn_iters": 20, "parallelism": f"dp{world}",
+                   "l2": "inputs larger than L2 (T*n*C elements per tensor); no flush"},
+        "roofline": {"bound": "hbm", "kernel": dom,
+                     "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak if achieved else None,
+                     "traffic": traffic_from_profile(f"{dom}:{args.io_dtype}:T{T}:n{n}:C{C}"),
+                     "algorithmic_bytes_per_launch": bwd_b, "peak_source": f"{peak_kind} hbm_gbs",
+                     "fwd_achieved": fwd_b / (fwd_us * 1e-6) / 1e9 if fwd_us else None,
+                     "step_achieved": (fwd_b + bwd_b) / (ms * 1e-3) / 1e9},
+        "kernels": kstats,
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if args.io_dtype == "f32" and args.steps >= 10:
+        _, ms2, ks2, _, _, f2, b2 = measure("bf16", max(10, args.steps // 2), False)
+        bu = ks2.get(dom, {}).get("avg_us")
+        res["secondary_bf16_io"] = {"value": world * T / (ms2 * 1e-3), "ms_per_step": ms2,
+                                    "bwd_achieved_gbs": b2 / (bu * 1e-6) / 1e9 if bu else None,
+                                    "step_achieved_gbs": (f2 + b2) / (ms2 * 1e-3) / 1e9,
+                                    "kernels": ks2}
+    if not args.no_e2e:
+        iodt = torch.float32 if args.io_dtype == "f32" else torch.bfloat16
+        rdt = None if args.io_dtype == "f32" else torch.bfloat16
+        res["e2e"] = e2e_measure(layer, T, n, C, iodt, rdt, dev, args.e2e_steps, world)
+    if rank == 0 and world == 1 and not args.no_latency:
+        res["latency_b1"] = latency_b1(make_layer(n, C, dev), n, C, dev)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        res["cpu_baseline"] = cpu_baseline(n, C, args.cpu_seconds)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+def run_reference(args):
+    """The reference's CPU algorithm (oracle port of reference.py, autograd
+    backward) on all host cores, same metric/config, bounded token sample."""
+    rank, _, world = env_rank()
+    if rank != 0:
+        return
+    n, C = args.n, args.C
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    per_tok = cpu_oracle_step(64, n, C, 20) / 64
+    budget = 150.0 / max(1, args.steps + args.warmup)  # whole run within a few minutes
+    Ts = int(max(8, min(args.tokens, budget / per_tok)))
+    for k in range(args.warmup):
+        cpu_oracle_step(Ts, n, C, 20, seed=k)
+    times = [cpu_oracle_step(Ts, n, C, 20, seed=100 + k) for k in range(args.steps)]
+    sec = sum(times)
+    value = Ts * args.steps / sec
+    sample = (f"{Ts} tokens per step of the {args.tokens}-token workload, fwd+bwd fp32 "
+              f"(oracle restatement of mhc_mlx/reference.py, torch autograd), {cores} threads")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sec / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"MHCLayer fwd+bwd T={args.tokens} tokens/GPU, n={n}, C={C}, "
+                               f"{args.io_dtype} I/O, fp32 math, 20 Sinkhorn iters",
+                   "tokens_per_gpu": args.tokens, "n": n, "C": C, "io_dtype": args.io_dtype,
+                   "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

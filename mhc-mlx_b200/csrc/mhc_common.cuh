@@ -1,0 +1,189 @@
+// Shared device helpers for the mHC sm_100a kernels: dtype conversion,
+// 16-byte vector loads/stores, warp/block reductions.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "mhc_b200.h"
+
+namespace mhc {
+
+using bf16 = __nv_bfloat16;
+using f16 = __half;
+
+constexpr int kMaxN = 64;  // reference metal.py:71 _MAX_N_ALLOWED
+
+// ---------------------------------------------------------------- dtypes --
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(f16 v) { return __half2float(v); }
+__device__ __forceinline__ float to_f(bf16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ f16 from_f<f16>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ bf16 from_f<bf16>(float v) { return __float2bfloat16_rn(v); }
+
+// Elements per 16-byte vector.
+template <typename T> struct VecOf { static constexpr int value = 16 / sizeof(T); };
+
+// ------------------------------------------------------ vector load/store --
+// Load V consecutive elements starting at p into fp32 registers.  V is either
+// 1 (scalar path, any alignment) or the 16-byte width of T (p 16B-aligned).
+// `Stream` selects the evict-first cache policy for data touched once.
+template <bool Stream>
+__device__ __forceinline__ float4 ld4(const float4* p) {
+  if constexpr (Stream) return __ldcs(p);
+  else return __ldg(p);
+}
+template <bool Stream>
+__device__ __forceinline__ uint4 ldu4(const uint4* p) {
+  if constexpr (Stream) return __ldcs(p);
+  else return __ldg(p);
+}
+
+template <typename T, int V, bool Stream = true>
+__device__ __forceinline__ void load_vec(const T* __restrict__ p, float (&o)[V]) {
+  if constexpr (V == 1) {
+    o[0] = to_f(p[0]);
+  } else if constexpr (sizeof(T) == 4) {
+    static_assert(V % 4 == 0, "fp32 vector width is a multiple of 4");
+#pragma unroll
+    for (int k = 0; k < V; k += 4) {
+      float4 v = ld4<Stream>(reinterpret_cast<const float4*>(p) + k / 4);
+      o[k] = v.x; o[k + 1] = v.y; o[k + 2] = v.z; o[k + 3] = v.w;
+    }
+  } else if constexpr (V == 4) {
+    uint2 u = *reinterpret_cast<const uint2*>(p);  // 8-byte aligned
+    const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = to_f(h[k]);
+  } else {
+    static_assert(V == 8, "16-bit vector width is 4 or 8");
+    uint4 u = ldu4<Stream>(reinterpret_cast<const uint4*>(p));
+    const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = to_f(h[k]);
+  }
+}
+
+// Store V fp32 values as T.  For T = float with V = 8 (half input, fp32
+// output) two float4 stores are issued.
+template <typename T, int V, bool Stream = true>
+__device__ __forceinline__ void store_vec(T* __restrict__ p, const float (&v)[V]) {
+  if constexpr (V == 1) {
+    p[0] = from_f<T>(v[0]);
+  } else if constexpr (sizeof(T) == 4) {
+    static_assert(V % 4 == 0, "fp32 store width");
+#pragma unroll
+    for (int k = 0; k < V; k += 4) {
+      float4 f = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
+      if constexpr (Stream) __stcs(reinterpret_cast<float4*>(p) + k / 4, f);
+      else reinterpret_cast<float4*>(p)[k / 4] = f;
+    }
+  } else if constexpr (V == 4) {
+    uint2 u;
+    T* h = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) h[k] = from_f<T>(v[k]);
+    *reinterpret_cast<uint2*>(p) = u;
+  } else {
+    static_assert(V == 8, "16-bit store width is 4 or 8");
+    uint4 u;
+    T* h = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) h[k] = from_f<T>(v[k]);
+    if constexpr (Stream) __stcs(reinterpret_cast<uint4*>(p), u);
+    else *reinterpret_cast<uint4*>(p) = u;
+  }
+}
+
+// Plain fp32 vector load for parameter vectors (w) of width V.
+template <int V>
+__device__ __forceinline__ void load_f32(const float* __restrict__ p, float (&o)[V]) {
+  if constexpr (V % 4 == 0) {
+#pragma unroll
+    for (int k = 0; k < V; k += 4) {
+      float4 f = __ldg(reinterpret_cast<const float4*>(p) + k / 4);
+      o[k] = f.x; o[k + 1] = f.y; o[k + 2] = f.z; o[k + 3] = f.w;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < V; ++k) o[k] = __ldg(p + k);
+  }
+}
+
+// ------------------------------------------------------------ reductions --
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide sum of one value.  `red` is a 32-float shared slot; the caller
+// alternates between two slots on consecutive calls so one barrier per call
+// suffices.  Every thread gets the same bits (fixed order over warps).
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  float s = 0.f;
+  for (int w = 0; w < nw; ++w) s += red[w];
+  return s;
+}
+
+// Two sums with one barrier; `red` holds 64 floats.
+__device__ __forceinline__ float2 block_sum2(float a, float b, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  a = warp_sum(a);
+  b = warp_sum(b);
+  if (lane == 0) { red[warp] = a; red[32 + warp] = b; }
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  float sa = 0.f, sb = 0.f;
+  for (int w = 0; w < nw; ++w) { sa += red[w]; sb += red[32 + w]; }
+  return make_float2(sa, sb);
+}
+
+// Sum over a group of G consecutive lanes (G divides 32, G a power of two).
+// Butterfly order: every lane of the group gets identical bits.
+template <int G>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Reference numerics (reference.py:40,45,104):
+//   row scale = row_sum > eps ? 1/row_sum : 1
+//   col scale = col_sum > eps ? 1/col_sum : 0
+//   inv_rms  = 1 / sqrt(mean + eps)
+__device__ __forceinline__ float row_scale(float s, float eps) { return s > eps ? 1.0f / s : 1.0f; }
+__device__ __forceinline__ float col_scale(float s, float eps) { return s > eps ? 1.0f / s : 0.0f; }
+__device__ __forceinline__ float inv_rms(float sumsq, int C, float eps) {
+  return 1.0f / sqrtf(sumsq / (float)C + eps);
+}
+__device__ __forceinline__ float sigmoidf_(float v) { return 1.0f / (1.0f + expf(-v)); }
+
+// Layout of the workspace written by the backward kernels:
+//   [0, 256)            header: int32 number of partial rows G
+//   params partials     G x P floats (P = n*n + 2n: dM row-major, dH_pre, dH_post)
+//   column partials     G x C floats (d_rms_weight)
+struct WsLayout {
+  static constexpr size_t kHeader = 256;
+  static __host__ __device__ size_t P(int n) { return (size_t)n * n + 2 * (size_t)n; }
+  static __host__ __device__ size_t params_off() { return kHeader; }
+  static __host__ __device__ size_t cols_off(int G, int n) {
+    size_t b = kHeader + (size_t)G * P(n) * sizeof(float);
+    return (b + 255) & ~size_t(255);
+  }
+  static __host__ __device__ size_t bytes(int G, int n, int C) {
+    return cols_off(G, n) + (size_t)G * (size_t)C * sizeof(float);
+  }
+};
+
+}  // namespace mhc

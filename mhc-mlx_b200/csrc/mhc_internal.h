@@ -1,0 +1,83 @@
+// Host-side internals shared by the .cu files: error reporting, device
+// queries and the launcher declarations that mhc_capi.cu validates and calls.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include "mhc_b200.h"
+
+namespace mhc {
+
+// Thread-local last-error text (returned by mhc_last_error()).
+int set_error(int code, const char* fmt, ...);
+// Checks cudaGetLastError() after a launch; returns MHC_OK or MHC_ERR_CUDA.
+int check_launch(const char* what);
+
+// Current device's SM count (cached per device).
+int sm_count();
+// Max dynamic shared memory per block (opt-in) of the current device.
+int max_smem_optin();
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline int dtype_size(int dt) { return dt == MHC_F32 ? 4 : 2; }
+inline bool dtype_ok(int dt) { return dt == MHC_F32 || dt == MHC_F16 || dt == MHC_BF16; }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Upper bound of partial rows a backward launch may use; sizes workspaces.
+int max_partial_rows(int64_t T);
+
+// ---- Sinkhorn / parameters (mhc_sinkhorn.cu) ----------------------------
+size_t sk_tape_floats(int n, int iters);
+int launch_params_fwd(const float* hpre_raw, const float* hpost_raw, const float* hres_raw,
+                      int n, int iters, float eps, float* hpre, float* hpost, float* M,
+                      float* tape, cudaStream_t st);
+int launch_params_bwd(const float* hpre_raw, const float* hpost_raw, const float* hres_raw,
+                      const float* tape, int n, int iters, float eps, const float* dhpre,
+                      const float* dhpost, const float* dM, float* dhpre_raw,
+                      float* dhpost_raw, float* dhres_raw, cudaStream_t st);
+size_t sk_batched_ws_bytes(int64_t batch, int n, int iters);
+int launch_sk_batched_fwd(const float* H, int64_t batch, int n, int iters, float eps, float* M,
+                          void* ws, size_t ws_bytes, cudaStream_t st);
+int launch_sk_batched_bwd(const float* H, const float* dM, int64_t batch, int n, int iters,
+                          float eps, float* dH, void* ws, size_t ws_bytes, cudaStream_t st);
+
+// ---- layer forward / backward (mhc_layer.cu) ------------------------------
+int launch_fwd(const void* x, int xdt, const float* M, const float* hpre, const float* hpost,
+               const float* w, void* out, int odt, int64_t T, int n, int C, float eps,
+               cudaStream_t st);
+size_t bwd_ws_bytes(int64_t T, int n, int C);
+int launch_bwd(const void* x, int xdt, const void* dout, int ddt, const float* M,
+               const float* hpre, const float* hpost, const float* w, void* dx, int dxdt,
+               int64_t T, int n, int C, float eps, void* ws, size_t ws_bytes, cudaStream_t st);
+int launch_finalize(const void* ws, int n, int C, float* dM, float* dhpre, float* dhpost,
+                    float* dw, const float* hpre_raw, const float* hpost_raw,
+                    const float* hres_raw, const float* tape, int iters, float eps,
+                    float* dhpre_raw, float* dhpost_raw, float* dhres_raw, cudaStream_t st);
+
+// ---- mix / rewire / prescale / residual (mhc_mix.cu) ------------------------
+int launch_mix_add_fwd(const void* x, int xdt, const float* M, const void* y, int ydt, void* out,
+                       int odt, int64_t T, int n, int C, cudaStream_t st);
+size_t mix_ws_bytes(int64_t T, int n, int C);
+int launch_mix_add_bwd(const void* x, int xdt, const float* M, const void* dout, int ddt,
+                       void* dx, int dxdt, float* dM, int64_t T, int n, int C, void* ws,
+                       size_t ws_bytes, cudaStream_t st);
+int launch_rewire_fwd(const void* x, int xdt, const void* y, int ydt, const float* M,
+                      const float* hpre, const float* hpost, void* out, int odt, int64_t T,
+                      int n, int C, cudaStream_t st);
+int launch_rewire_bwd(const void* x, int xdt, const void* y, int ydt, const void* dout, int ddt,
+                      const float* M, const float* hpre, const float* hpost, void* dx, int dxdt,
+                      void* dy, int dydt, float* dM, float* dhpre, float* dhpost, int64_t T,
+                      int n, int C, void* ws, size_t ws_bytes, cudaStream_t st);
+int launch_prescale_fwd(const void* x, int xdt, const float* hpre, void* xo, int odt, int64_t T,
+                        int n, int C, cudaStream_t st);
+int launch_prescale_bwd(const void* x, int xdt, const void* d, int ddt, const float* hpre,
+                        void* dx, int dxdt, float* dhpre, int64_t T, int n, int C, void* ws,
+                        size_t ws_bytes, cudaStream_t st);
+int launch_residual_add_agg(const void* x, int xdt, const void* res, int rdt, const float* hpre,
+                            void* out, int odt, float* yagg, int64_t T, int n, int C,
+                            cudaStream_t st);
+
+}  // namespace mhc

@@ -1,0 +1,803 @@
+// Fused mHC layer kernels for sm_100a: forward (aggregate + RMSNorm + mix +
+// residual add), backward (dx plus per-CTA partials of every parameter
+// gradient) and the finalize reduction (+ Sinkhorn / sigmoid chain).
+//
+// Reference math: reference.py:72-161.  Reference launch structure being
+// replaced: metal.py:1823-1975 (forward strategy selector: 1 or 3 kernels)
+// and metal.py:2787-2857 (backward: 7 kernels, dM/dH reductions on n^2 / n
+// threadgroups).  Here the forward is one pass (x read once, out written
+// once) and the backward is one pass (x, d_out read once, dx written once)
+// followed by a small deterministic reduction.
+//
+// Mapping ("fast" kernels, n in {1,2,4,8[,16,32]}): persistent CTAs, one token
+// row [n, C] at a time per CTA.  Thread t owns the column groups
+// g = t + k*blockDim (k < ITEMS), VEC columns each, for all n streams, so the
+// whole row sits in registers between the load and the store; the RMS sum
+// (and in the backward the RMS-gradient dot product) is one block reduction.
+// The "generic" kernels cover any n <= 64 and any C with two passes per row.
+#include <cstdlib>
+
+#include "mhc_common.cuh"
+#include "mhc_sinkhorn.cuh"
+#include "mhc_internal.h"
+
+namespace mhc {
+
+// ===================================================================== fwd ==
+template <int N, typename InT, typename OutT, int VEC, int ITEMS, int MAXT>
+__global__ void __launch_bounds__(MAXT)
+k_fwd_fast(const InT* __restrict__ x, const float* __restrict__ Mg,
+           const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
+           const float* __restrict__ w, OutT* __restrict__ out, int64_t T, int C, float eps) {
+  constexpr bool kMReg = N <= 8;
+  __shared__ float sM[N * N];
+  __shared__ float red[2][32];
+  for (int e = threadIdx.x; e < N * N; e += blockDim.x) sM[e] = Mg[e];
+  float hpre[N], hpost[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) { hpre[i] = __ldg(hpre_g + i); hpost[i] = __ldg(hpost_g + i); }
+  __syncthreads();
+  float Mr[kMReg ? N : 1][kMReg ? N : 1];
+  if constexpr (kMReg) {
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+#pragma unroll
+      for (int j = 0; j < N; ++j) Mr[i][j] = sM[i * N + j];
+  }
+
+  int col[ITEMS];
+  bool ok[ITEMS];
+  float wv[ITEMS][VEC];
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) {
+    col[it] = (threadIdx.x + it * blockDim.x) * VEC;
+    ok[it] = col[it] < C;
+    if (ok[it]) load_f32<VEC>(w + col[it], wv[it]);
+    else
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) wv[it][v] = 0.f;
+  }
+
+  const int64_t rs = (int64_t)N * C;
+  int par = 0;
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    const InT* xt = x + t * rs;
+    float xr[ITEMS][N][VEC];
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it)
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        if (ok[it]) load_vec<InT, VEC>(xt + (int64_t)i * C + col[it], xr[it][i]);
+        else
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) xr[it][i][v] = 0.f;
+      }
+    float y[ITEMS][VEC];
+    float ss = 0.f;
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it)
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        float a = 0.f;
+#pragma unroll
+        for (int i = 0; i < N; ++i) a = fmaf(hpre[i], xr[it][i][v], a);
+        y[it][v] = a;
+        ss = fmaf(a, a, ss);
+      }
+    ss = block_sum(ss, red[par]);
+    par ^= 1;
+    const float inv = inv_rms(ss, C, eps);
+    OutT* ot = out + t * rs;
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it) {
+      if (!ok[it]) continue;
+      float yn[VEC];
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) yn[v] = (y[it][v] * inv) * wv[it][v];
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        float o[VEC];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          float m = 0.f;
+#pragma unroll
+          for (int j = 0; j < N; ++j) {
+            const float mij = kMReg ? Mr[kMReg ? i : 0][kMReg ? j : 0] : sM[i * N + j];
+            m = fmaf(mij, xr[it][j][v], m);
+          }
+          o[v] = m + hpost[i] * yn[v];
+        }
+        store_vec<OutT, VEC>(ot + (int64_t)i * C + col[it], o);
+      }
+    }
+  }
+}
+
+// Generic forward: any n <= MAXN, any C, any alignment.  Pass 1 computes the
+// row's sum of squares, pass 2 re-reads the row (L2-resident) and writes out.
+template <int MAXN, typename InT, typename OutT>
+__global__ void __launch_bounds__(256)
+k_fwd_generic(const InT* __restrict__ x, const float* __restrict__ Mg,
+              const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
+              const float* __restrict__ w, OutT* __restrict__ out, int64_t T, int n, int C,
+              float eps) {
+  __shared__ float sM[MAXN * MAXN];
+  __shared__ float shpre[MAXN], shpost[MAXN];
+  __shared__ float red[2][32];
+  for (int e = threadIdx.x; e < n * n; e += blockDim.x) sM[e] = Mg[e];
+  for (int e = threadIdx.x; e < n; e += blockDim.x) { shpre[e] = hpre_g[e]; shpost[e] = hpost_g[e]; }
+  __syncthreads();
+  const int64_t rs = (int64_t)n * C;
+  int par = 0;
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    const InT* xt = x + t * rs;
+    float ss = 0.f;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+      float a = 0.f;
+      for (int i = 0; i < n; ++i) a = fmaf(shpre[i], to_f(xt[(int64_t)i * C + c]), a);
+      ss = fmaf(a, a, ss);
+    }
+    ss = block_sum(ss, red[par]);
+    par ^= 1;
+    const float inv = inv_rms(ss, C, eps);
+    OutT* ot = out + t * rs;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+      float xc[MAXN];
+      float a = 0.f;
+#pragma unroll
+      for (int j = 0; j < MAXN; ++j) {
+        xc[j] = j < n ? to_f(xt[(int64_t)j * C + c]) : 0.f;
+        if (j < n) a = fmaf(shpre[j], xc[j], a);
+      }
+      const float yn = (a * inv) * __ldg(w + c);
+      for (int i = 0; i < n; ++i) {
+        float m = 0.f;
+#pragma unroll
+        for (int j = 0; j < MAXN; ++j)
+          if (j < n) m = fmaf(sM[i * n + j], xc[j], m);
+        ot[(int64_t)i * C + c] = from_f<OutT>(m + shpost[i] * yn);
+      }
+    }
+  }
+}
+
+// ===================================================================== bwd ==
+// Per token (y = sum_i hpre_i x_i, dyn = sum_i hpost_i d_i, both per column):
+//   ss = sum_c y^2, pd = sum_c dyn w y, inv = 1/sqrt(ss/C + eps)
+//   dya = dyn w inv - (pd inv^3 / C) y
+//   dx_j = sum_i M_ij d_i + hpre_j dya
+// Accumulated over tokens and columns (per CTA, then finalize):
+//   dM_ij += d_i x_j, dHpre_j += dya x_j, dHpost_i += d_i (y inv w),
+//   dw_c += dyn (y inv)
+template <int N, typename XT, typename DT, typename DXT, int VEC, int ITEMS, int MAXT>
+__global__ void __launch_bounds__(MAXT)
+k_bwd_fast(const XT* __restrict__ x, const DT* __restrict__ dout, const float* __restrict__ Mg,
+           const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
+           const float* __restrict__ w, DXT* __restrict__ dx, int64_t T, int C, float eps,
+           float* __restrict__ ws_p, float* __restrict__ ws_c, int* __restrict__ ws_hdr) {
+  constexpr int P = N * N + 2 * N;
+  __shared__ float sM[N * N];
+  __shared__ float red[2][64];
+  __shared__ float sacc[32 * P];
+  for (int e = threadIdx.x; e < N * N; e += blockDim.x) sM[e] = Mg[e];
+  float hpre[N], hpost[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) { hpre[i] = __ldg(hpre_g + i); hpost[i] = __ldg(hpost_g + i); }
+  __syncthreads();
+
+  int col[ITEMS];
+  bool ok[ITEMS];
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) {
+    col[it] = (threadIdx.x + it * blockDim.x) * VEC;
+    ok[it] = col[it] < C;
+  }
+  float aM[N][N], aPre[N], aPost[N], aW[ITEMS][VEC];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    aPre[i] = 0.f; aPost[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) aM[i][j] = 0.f;
+  }
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it)
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) aW[it][v] = 0.f;
+
+  const int64_t rs = (int64_t)N * C;
+  const float invC = 1.0f / (float)C;
+  int par = 0;
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    const XT* xt = x + t * rs;
+    const DT* dt = dout + t * rs;
+    float xr[ITEMS][N][VEC], dr[ITEMS][N][VEC];
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it)
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        if (ok[it]) {
+          load_vec<XT, VEC>(xt + (int64_t)i * C + col[it], xr[it][i]);
+          load_vec<DT, VEC>(dt + (int64_t)i * C + col[it], dr[it][i]);
+        } else {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) { xr[it][i][v] = 0.f; dr[it][i][v] = 0.f; }
+        }
+      }
+    float ss = 0.f, pd = 0.f;
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it) {
+      float wv[VEC];
+      if (ok[it]) load_f32<VEC>(w + col[it], wv);
+      else
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) wv[v] = 0.f;
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        float y = 0.f, dyn = 0.f;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          y = fmaf(hpre[i], xr[it][i][v], y);
+          dyn = fmaf(hpost[i], dr[it][i][v], dyn);
+        }
+        ss = fmaf(y, y, ss);
+        pd = fmaf(dyn * wv[v], y, pd);
+      }
+    }
+    const float2 red2 = block_sum2(ss, pd, red[par]);
+    par ^= 1;
+    const float inv = inv_rms(red2.x, C, eps);
+    const float k2 = (red2.y * (inv * inv * inv)) * invC;
+
+    float dya[ITEMS][VEC];
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it) {
+      float wv[VEC];
+      if (ok[it]) load_f32<VEC>(w + col[it], wv);
+      else
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) wv[v] = 0.f;
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        float y = 0.f, dyn = 0.f;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          y = fmaf(hpre[i], xr[it][i][v], y);
+          dyn = fmaf(hpost[i], dr[it][i][v], dyn);
+        }
+        const float yi = y * inv;
+        const float yn = yi * wv[v];
+        aW[it][v] = fmaf(dyn, yi, aW[it][v]);
+        const float g = (dyn * wv[v]) * inv - k2 * y;
+        dya[it][v] = g;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          aPost[i] = fmaf(dr[it][i][v], yn, aPost[i]);
+          aPre[i] = fmaf(g, xr[it][i][v], aPre[i]);
+#pragma unroll
+          for (int j = 0; j < N; ++j) aM[i][j] = fmaf(dr[it][i][v], xr[it][j][v], aM[i][j]);
+        }
+      }
+    }
+    DXT* dxt = dx + t * rs;
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it) {
+      if (!ok[it]) continue;
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float o[VEC];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) o[v] = hpre[j] * dya[it][v];
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          const float mij = sM[i * N + j];
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) o[v] = fmaf(mij, dr[it][i][v], o[v]);
+        }
+        store_vec<DXT, VEC>(dxt + (int64_t)j * C + col[it], o);
+      }
+    }
+  }
+
+  // ---- per-CTA partials: fixed-order warp butterfly + ordered warp sum ----
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float v = warp_sum(aM[i][j]);
+      if (lane == 0) sacc[warp * P + i * N + j] = v;
+    }
+    const float a = warp_sum(aPre[i]);
+    const float b = warp_sum(aPost[i]);
+    if (lane == 0) { sacc[warp * P + N * N + i] = a; sacc[warp * P + N * N + N + i] = b; }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < P; e += blockDim.x) {
+    float s = 0.f;
+    for (int q = 0; q < nw; ++q) s += sacc[q * P + e];
+    ws_p[(size_t)blockIdx.x * P + e] = s;
+  }
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it)
+    if (ok[it]) store_vec<float, VEC, false>(ws_c + (size_t)blockIdx.x * C + col[it], aW[it]);
+  if (blockIdx.x == 0 && threadIdx.x == 0) ws_hdr[0] = gridDim.x;
+}
+
+// Generic backward: any n <= 64, any C.  Pass 1 reduces ss and pd for the
+// row; pass 2 walks the row in tiles of blockDim columns: each thread stages
+// its column of x and d_out in shared memory (plus two extra rows: y inv w
+// and dya), writes dx, and the CTA accumulates the (n+1) x (n+1) outer
+// product D_aug X_aug^T with 4x4 register blocks:
+//   [i<n, j<n] -> dM_ij,  [i<n, j=n] -> dHpost_i,  [i=n, j<n] -> dHpre_j.
+// d_rms_weight accumulates in the CTA's own row of the column partials.
+constexpr int kGenBD = 128;   // threads per CTA (= tile width)
+constexpr int kGenLD = kGenBD + 1;
+constexpr int kGenRB = 4;     // register block edge
+constexpr int kGenMaxBlk = 3; // ceil(ceil(65/4)^2 / 128)
+
+template <typename XT, typename DT, typename DXT>
+__global__ void __launch_bounds__(kGenBD)
+k_bwd_generic(const XT* __restrict__ x, const DT* __restrict__ dout, const float* __restrict__ Mg,
+              const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
+              const float* __restrict__ w, DXT* __restrict__ dx, int64_t T, int n, int C,
+              float eps, float* __restrict__ ws_p, float* __restrict__ ws_c,
+              int* __restrict__ ws_hdr) {
+  extern __shared__ float smem[];
+  const int na = n + 1;
+  float* sM = smem;                       // n*n
+  float* shpre = sM + n * n;              // n
+  float* shpost = shpre + n;              // n
+  float* sx = shpost + n;                 // na x kGenLD  (row n = y inv w)
+  float* sd = sx + na * kGenLD;           // na x kGenLD  (row n = dya)
+  __shared__ float red[2][64];
+  const int tid = threadIdx.x;
+  for (int e = tid; e < n * n; e += kGenBD) sM[e] = Mg[e];
+  for (int e = tid; e < n; e += kGenBD) { shpre[e] = hpre_g[e]; shpost[e] = hpost_g[e]; }
+  float* wc = ws_c + (size_t)blockIdx.x * C;
+  for (int c = tid; c < C; c += kGenBD) wc[c] = 0.f;
+
+  const int nb = (na + kGenRB - 1) / kGenRB;  // blocks per edge
+  const int nblk = nb * nb;
+  float acc[kGenMaxBlk][kGenRB][kGenRB];
+#pragma unroll
+  for (int q = 0; q < kGenMaxBlk; ++q)
+#pragma unroll
+    for (int a = 0; a < kGenRB; ++a)
+#pragma unroll
+      for (int b = 0; b < kGenRB; ++b) acc[q][a][b] = 0.f;
+  __syncthreads();
+
+  const int64_t rs = (int64_t)n * C;
+  const float invC = 1.0f / (float)C;
+  int par = 0;
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    const XT* xt = x + t * rs;
+    const DT* dt = dout + t * rs;
+    float ss = 0.f, pd = 0.f;
+    for (int c = tid; c < C; c += kGenBD) {
+      float y = 0.f, dyn = 0.f;
+      for (int i = 0; i < n; ++i) {
+        y = fmaf(shpre[i], to_f(xt[(int64_t)i * C + c]), y);
+        dyn = fmaf(shpost[i], to_f(dt[(int64_t)i * C + c]), dyn);
+      }
+      ss = fmaf(y, y, ss);
+      pd = fmaf(dyn * __ldg(w + c), y, pd);
+    }
+    const float2 red2 = block_sum2(ss, pd, red[par]);
+    par ^= 1;
+    const float inv = inv_rms(red2.x, C, eps);
+    const float k2 = (red2.y * (inv * inv * inv)) * invC;
+    DXT* dxt = dx + t * rs;
+    for (int c0 = 0; c0 < C; c0 += kGenBD) {
+      const int c = c0 + tid;
+      const bool ok = c < C;
+      float y = 0.f, dyn = 0.f;
+      for (int i = 0; i < n; ++i) {
+        const float xv = ok ? to_f(xt[(int64_t)i * C + c]) : 0.f;
+        const float dv = ok ? to_f(dt[(int64_t)i * C + c]) : 0.f;
+        sx[i * kGenLD + tid] = xv;
+        sd[i * kGenLD + tid] = dv;
+        y = fmaf(shpre[i], xv, y);
+        dyn = fmaf(shpost[i], dv, dyn);
+      }
+      const float wv = ok ? __ldg(w + c) : 0.f;
+      const float yi = y * inv;
+      const float g = (dyn * wv) * inv - k2 * y;
+      sx[n * kGenLD + tid] = yi * wv;
+      sd[n * kGenLD + tid] = ok ? g : 0.f;
+      if (ok) {
+        wc[c] = fmaf(dyn, yi, wc[c]);
+        for (int j = 0; j < n; ++j) {
+          float o = shpre[j] * g;
+          for (int i = 0; i < n; ++i) o = fmaf(sM[i * n + j], sd[i * kGenLD + tid], o);
+          dxt[(int64_t)j * C + c] = from_f<DXT>(o);
+        }
+      }
+      __syncthreads();
+      const int width = min(kGenBD, C - c0);
+#pragma unroll
+      for (int q = 0; q < kGenMaxBlk; ++q) {
+        const int blk = tid + q * kGenBD;
+        if (blk >= nblk) break;
+        const int i0 = (blk / nb) * kGenRB, j0 = (blk % nb) * kGenRB;
+        for (int cc = 0; cc < width; ++cc) {
+          float dv[kGenRB], xv[kGenRB];
+#pragma unroll
+          for (int a = 0; a < kGenRB; ++a) {
+            dv[a] = (i0 + a < na) ? sd[(i0 + a) * kGenLD + cc] : 0.f;
+            xv[a] = (j0 + a < na) ? sx[(j0 + a) * kGenLD + cc] : 0.f;
+          }
+#pragma unroll
+          for (int a = 0; a < kGenRB; ++a)
+#pragma unroll
+            for (int b = 0; b < kGenRB; ++b) acc[q][a][b] = fmaf(dv[a], xv[b], acc[q][a][b]);
+        }
+      }
+      __syncthreads();
+    }
+  }
+  // scatter the owned blocks into this CTA's partial row
+  const int P = n * n + 2 * n;
+  float* pr = ws_p + (size_t)blockIdx.x * P;
+#pragma unroll
+  for (int q = 0; q < kGenMaxBlk; ++q) {
+    const int blk = tid + q * kGenBD;
+    if (blk >= nblk) break;
+    const int i0 = (blk / nb) * kGenRB, j0 = (blk % nb) * kGenRB;
+#pragma unroll
+    for (int a = 0; a < kGenRB; ++a)
+#pragma unroll
+      for (int b = 0; b < kGenRB; ++b) {
+        const int i = i0 + a, j = j0 + b;
+        if (i < n && j < n) pr[i * n + j] = acc[q][a][b];
+        else if (i == n && j < n) pr[n * n + j] = acc[q][a][b];      // dHpre_j
+        else if (i < n && j == n) pr[n * n + n + i] = acc[q][a][b];  // dHpost_i
+      }
+  }
+  if (blockIdx.x == 0 && tid == 0) ws_hdr[0] = gridDim.x;
+}
+
+// ================================================================ finalize ==
+// Blocks [0, nbc) reduce d_rms_weight columns; the last block reduces the
+// n*n + 2n parameter partials and optionally runs the parameter chain
+// (Sinkhorn backward + sigmoid derivatives).  Summation is sequential over
+// partial rows: deterministic for a given partial count.
+constexpr int kFinBD = 256;
+
+__global__ void __launch_bounds__(kFinBD)
+k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
+           float* __restrict__ dhpre, float* __restrict__ dhpost, float* __restrict__ dw,
+           const float* __restrict__ hpre_raw, const float* __restrict__ hpost_raw,
+           const float* __restrict__ hres_raw, const float* __restrict__ tape, int iters,
+           float eps, float* __restrict__ dhpre_raw, float* __restrict__ dhpost_raw,
+           float* __restrict__ dhres_raw) {
+  const int G = *reinterpret_cast<const int*>(ws);
+  const int P = n * n + 2 * n;
+  const float* wp = reinterpret_cast<const float*>(ws + WsLayout::params_off());
+  const float* wc = reinterpret_cast<const float*>(ws + WsLayout::cols_off(G, n));
+  const int nbc = (C + kFinBD - 1) / kFinBD;
+  if ((int)blockIdx.x < nbc) {
+    const int c = blockIdx.x * kFinBD + threadIdx.x;
+    if (c < C && dw) {
+      float s = 0.f;
+      for (int g = 0; g < G; ++g) s += wc[(size_t)g * C + c];
+      dw[c] = s;
+    }
+    return;
+  }
+  __shared__ float sP[kMaxN * kMaxN + 2 * kMaxN];
+  __shared__ float D[kMaxN * (kMaxN + 1)];
+  for (int e = threadIdx.x; e < P; e += kFinBD) {
+    float s = 0.f;
+    for (int g = 0; g < G; ++g) s += wp[(size_t)g * P + e];
+    sP[e] = s;
+    if (e < n * n) { if (dM) dM[e] = s; }
+    else if (e < n * n + n) { if (dhpre) dhpre[e - n * n] = s; }
+    else if (dhpost) dhpost[e - n * n - n] = s;
+  }
+  __syncthreads();
+  const int tid = threadIdx.x;
+  if (tid < n) {
+    if (hpre_raw && dhpre_raw) {
+      const float s = sigmoidf_(hpre_raw[tid]);
+      dhpre_raw[tid] = sP[n * n + tid] * (1.0f - s) * s;
+    }
+    if (hpost_raw && dhpost_raw) {
+      const float s = sigmoidf_(hpost_raw[tid]);
+      dhpost_raw[tid] = (2.0f * sP[n * n + n + tid]) * (1.0f - s) * s;
+    }
+  }
+  if (hres_raw && dhres_raw && (tape || iters == 0)) {
+    const int ld = sk_ld(n);
+    for (int e = tid; e < n * n; e += kFinBD) D[(e / n) * ld + e % n] = sP[e];
+    __syncthreads();
+    sk_backward_block(hres_raw, tape, n, iters, eps, D, dhres_raw);
+  }
+}
+
+// ================================================================= launch ==
+// Environment overrides for tuning sweeps (unset in normal use):
+//   MHC_B200_FWD_ITEMS / MHC_B200_BWD_ITEMS  force the ITEMS of the fast path
+//   MHC_B200_GENERIC=1                       force the generic kernels
+static int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return v && *v ? atoi(v) : dflt;
+}
+
+int max_partial_rows(int64_t T) {
+  int64_t g = (int64_t)sm_count() * 4;
+  if (g > T) g = T;
+  return (int)(g < 1 ? 1 : g);
+}
+
+template <typename K>
+static int persistent_grid(K kernel, int threads, size_t smem, int64_t T, int cap) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  int64_t g = (int64_t)per_sm * sm_count();
+  if (g > cap) g = cap;
+  if (g > T) g = T;
+  return (int)(g < 1 ? 1 : g);
+}
+
+// Threads per CTA ceiling for a fast instantiation holding `d` fp32 row
+// values per thread.
+constexpr int fast_maxt(int d) { return d <= 16 ? 1024 : (d <= 64 ? 512 : 256); }
+
+static int round32(int v) { return (v + 31) & ~31; }
+
+// ---- forward dispatch -------------------------------------------------------
+template <int N, typename InT, typename OutT, int VEC, int ITEMS>
+static int try_fwd_items(const InT* x, const float* M, const float* hpre, const float* hpost,
+                         const float* w, OutT* out, int64_t T, int C, float eps, cudaStream_t st) {
+  constexpr int d = N * VEC * ITEMS;
+  if constexpr (d > 64) {
+    return -1;
+  } else {
+    constexpr int MAXT = fast_maxt(d);
+    const int groups = (C + VEC - 1) / VEC;
+    const int threads = round32((groups + ITEMS - 1) / ITEMS);
+    if (threads > MAXT) return -1;
+    auto kern = k_fwd_fast<N, InT, OutT, VEC, ITEMS, MAXT>;
+    const int grid = persistent_grid(kern, threads, 0, T, 1 << 30);
+    kern<<<grid, threads, 0, st>>>(x, M, hpre, hpost, w, out, T, C, eps);
+    return check_launch("mhc_fwd");
+  }
+}
+
+template <int N, typename InT, typename OutT, int VEC>
+static int try_fwd_vec(const InT* x, const float* M, const float* hpre, const float* hpost,
+                       const float* w, OutT* out, int64_t T, int C, float eps, cudaStream_t st) {
+  const int forced = env_int("MHC_B200_FWD_ITEMS", 0);
+  const int groups = (C + VEC - 1) / VEC;
+  // Default: the fewest ITEMS whose block is at most 512 threads.
+  const int order[4] = {1, 2, 4, 8};
+  for (int k = 0; k < 4; ++k) {
+    const int items = order[k];
+    if (forced && items != forced) continue;
+    if (!forced && round32((groups + items - 1) / items) > 512 && items != 8) continue;
+    int r = -1;
+    switch (items) {
+      case 1: r = try_fwd_items<N, InT, OutT, VEC, 1>(x, M, hpre, hpost, w, out, T, C, eps, st); break;
+      case 2: r = try_fwd_items<N, InT, OutT, VEC, 2>(x, M, hpre, hpost, w, out, T, C, eps, st); break;
+      case 4: r = try_fwd_items<N, InT, OutT, VEC, 4>(x, M, hpre, hpost, w, out, T, C, eps, st); break;
+      case 8: r = try_fwd_items<N, InT, OutT, VEC, 8>(x, M, hpre, hpost, w, out, T, C, eps, st); break;
+    }
+    if (r >= 0) return r;
+  }
+  return -1;
+}
+
+template <int N, typename InT, typename OutT>
+static int fwd_fast(const InT* x, const float* M, const float* hpre, const float* hpost,
+                    const float* w, OutT* out, int64_t T, int C, float eps, cudaStream_t st) {
+  constexpr int VV = VecOf<InT>::value;
+  const bool vec_ok = (C % VV == 0) && aligned16(x) && aligned16(out) && aligned16(w);
+  if (vec_ok) {
+    const int r = try_fwd_vec<N, InT, OutT, VV>(x, M, hpre, hpost, w, out, T, C, eps, st);
+    if (r >= 0) return r;
+  }
+  return try_fwd_vec<N, InT, OutT, 1>(x, M, hpre, hpost, w, out, T, C, eps, st);
+}
+
+template <typename InT, typename OutT>
+static int fwd_generic(const InT* x, const float* M, const float* hpre, const float* hpost,
+                       const float* w, OutT* out, int64_t T, int n, int C, float eps,
+                       cudaStream_t st) {
+  if (n <= 16) {
+    auto kern = k_fwd_generic<16, InT, OutT>;
+    const int grid = persistent_grid(kern, 256, 0, T, 1 << 30);
+    kern<<<grid, 256, 0, st>>>(x, M, hpre, hpost, w, out, T, n, C, eps);
+  } else {
+    auto kern = k_fwd_generic<64, InT, OutT>;
+    const int grid = persistent_grid(kern, 256, 0, T, 1 << 30);
+    kern<<<grid, 256, 0, st>>>(x, M, hpre, hpost, w, out, T, n, C, eps);
+  }
+  return check_launch("mhc_fwd(generic)");
+}
+
+template <typename InT, typename OutT>
+static int fwd_typed(const void* xv, const float* M, const float* hpre, const float* hpost,
+                     const float* w, void* ov, int64_t T, int n, int C, float eps,
+                     cudaStream_t st) {
+  const InT* x = static_cast<const InT*>(xv);
+  OutT* out = static_cast<OutT*>(ov);
+  if (!env_int("MHC_B200_GENERIC", 0)) {
+    int r = -1;
+    switch (n) {
+      case 1: r = fwd_fast<1, InT, OutT>(x, M, hpre, hpost, w, out, T, C, eps, st); break;
+      case 2: r = fwd_fast<2, InT, OutT>(x, M, hpre, hpost, w, out, T, C, eps, st); break;
+      case 4: r = fwd_fast<4, InT, OutT>(x, M, hpre, hpost, w, out, T, C, eps, st); break;
+      case 8: r = fwd_fast<8, InT, OutT>(x, M, hpre, hpost, w, out, T, C, eps, st); break;
+      case 16: r = fwd_fast<16, InT, OutT>(x, M, hpre, hpost, w, out, T, C, eps, st); break;
+      case 32: r = fwd_fast<32, InT, OutT>(x, M, hpre, hpost, w, out, T, C, eps, st); break;
+      default: break;
+    }
+    if (r >= 0) return r;
+  }
+  return fwd_generic<InT, OutT>(x, M, hpre, hpost, w, out, T, n, C, eps, st);
+}
+
+int launch_fwd(const void* x, int xdt, const float* M, const float* hpre, const float* hpost,
+               const float* w, void* out, int odt, int64_t T, int n, int C, float eps,
+               cudaStream_t st) {
+  if (T == 0) return MHC_OK;
+  if (xdt == MHC_F32 && odt == MHC_F32)
+    return fwd_typed<float, float>(x, M, hpre, hpost, w, out, T, n, C, eps, st);
+  if (xdt == MHC_BF16 && odt == MHC_F32)
+    return fwd_typed<bf16, float>(x, M, hpre, hpost, w, out, T, n, C, eps, st);
+  if (xdt == MHC_BF16 && odt == MHC_BF16)
+    return fwd_typed<bf16, bf16>(x, M, hpre, hpost, w, out, T, n, C, eps, st);
+  if (xdt == MHC_F16 && odt == MHC_F32)
+    return fwd_typed<f16, float>(x, M, hpre, hpost, w, out, T, n, C, eps, st);
+  if (xdt == MHC_F16 && odt == MHC_F16)
+    return fwd_typed<f16, f16>(x, M, hpre, hpost, w, out, T, n, C, eps, st);
+  return set_error(MHC_ERR_UNSUPPORTED, "mhc_fwd: unsupported dtype pair x=%d out=%d", xdt, odt);
+}
+
+// ---- backward dispatch ------------------------------------------------------
+size_t bwd_ws_bytes(int64_t T, int n, int C) {
+  return WsLayout::bytes(max_partial_rows(T), n, C);
+}
+
+struct BwdPtrs {
+  float* p;
+  float* c;
+  int* hdr;
+};
+
+static BwdPtrs ws_ptrs(void* ws, int G, int n) {
+  char* b = static_cast<char*>(ws);
+  return {reinterpret_cast<float*>(b + WsLayout::params_off()),
+          reinterpret_cast<float*>(b + WsLayout::cols_off(G, n)), reinterpret_cast<int*>(b)};
+}
+
+template <int N, typename XT, typename DT, typename DXT, int VEC, int ITEMS>
+static int try_bwd_items(const XT* x, const DT* d, const float* M, const float* hpre,
+                         const float* hpost, const float* w, DXT* dx, int64_t T, int C, float eps,
+                         void* ws, cudaStream_t st) {
+  constexpr int d2 = 2 * N * VEC * ITEMS;
+  if constexpr (d2 > 64) {
+    return -1;
+  } else {
+    constexpr int MAXT = d2 <= 16 ? 1024 : 512;
+    const int groups = (C + VEC - 1) / VEC;
+    const int threads = round32((groups + ITEMS - 1) / ITEMS);
+    if (threads > MAXT) return -1;
+    auto kern = k_bwd_fast<N, XT, DT, DXT, VEC, ITEMS, MAXT>;
+    const int G = persistent_grid(kern, threads, 0, T, max_partial_rows(T));
+    BwdPtrs p = ws_ptrs(ws, G, N);
+    kern<<<G, threads, 0, st>>>(x, d, M, hpre, hpost, w, dx, T, C, eps, p.p, p.c, p.hdr);
+    return check_launch("mhc_bwd");
+  }
+}
+
+template <int N, typename XT, typename DT, typename DXT, int VEC>
+static int try_bwd_vec(const XT* x, const DT* d, const float* M, const float* hpre,
+                       const float* hpost, const float* w, DXT* dx, int64_t T, int C, float eps,
+                       void* ws, cudaStream_t st) {
+  const int forced = env_int("MHC_B200_BWD_ITEMS", 0);
+  const int groups = (C + VEC - 1) / VEC;
+  const int order[4] = {1, 2, 4, 8};
+  for (int k = 0; k < 4; ++k) {
+    const int items = order[k];
+    if (forced && items != forced) continue;
+    if (!forced && round32((groups + items - 1) / items) > 512 && items != 8) continue;
+    int r = -1;
+    switch (items) {
+      case 1: r = try_bwd_items<N, XT, DT, DXT, VEC, 1>(x, d, M, hpre, hpost, w, dx, T, C, eps, ws, st); break;
+      case 2: r = try_bwd_items<N, XT, DT, DXT, VEC, 2>(x, d, M, hpre, hpost, w, dx, T, C, eps, ws, st); break;
+      case 4: r = try_bwd_items<N, XT, DT, DXT, VEC, 4>(x, d, M, hpre, hpost, w, dx, T, C, eps, ws, st); break;
+      case 8: r = try_bwd_items<N, XT, DT, DXT, VEC, 8>(x, d, M, hpre, hpost, w, dx, T, C, eps, ws, st); break;
+    }
+    if (r >= 0) return r;
+  }
+  return -1;
+}
+
+template <int N, typename XT, typename DT, typename DXT>
+static int bwd_fast(const XT* x, const DT* d, const float* M, const float* hpre,
+                    const float* hpost, const float* w, DXT* dx, int64_t T, int C, float eps,
+                    void* ws, cudaStream_t st) {
+  constexpr int VX = VecOf<XT>::value, VD = VecOf<DT>::value;
+  // one vector width for both streams: the wider element count is used
+  // only if both dtypes share it (f32/f32 -> 4, 16-bit/16-bit -> 8)
+  if constexpr (VX == VD && VecOf<DXT>::value == VX) {
+    const bool vec_ok = (C % VX == 0) && aligned16(x) && aligned16(d) && aligned16(dx) &&
+                        aligned16(w);
+    if (vec_ok) {
+      const int r = try_bwd_vec<N, XT, DT, DXT, VX>(x, d, M, hpre, hpost, w, dx, T, C, eps, ws, st);
+      if (r >= 0) return r;
+    }
+  }
+  return try_bwd_vec<N, XT, DT, DXT, 1>(x, d, M, hpre, hpost, w, dx, T, C, eps, ws, st);
+}
+
+template <typename XT, typename DT, typename DXT>
+static int bwd_typed(const void* xv, const void* dv, const float* M, const float* hpre,
+                     const float* hpost, const float* w, void* dxv, int64_t T, int n, int C,
+                     float eps, void* ws, cudaStream_t st) {
+  const XT* x = static_cast<const XT*>(xv);
+  const DT* d = static_cast<const DT*>(dv);
+  DXT* dx = static_cast<DXT*>(dxv);
+  if (!env_int("MHC_B200_GENERIC", 0)) {
+    int r = -1;
+    switch (n) {
+      case 1: r = bwd_fast<1, XT, DT, DXT>(x, d, M, hpre, hpost, w, dx, T, C, eps, ws, st); break;
+      case 2: r = bwd_fast<2, XT, DT, DXT>(x, d, M, hpre, hpost, w, dx, T, C, eps, ws, st); break;
+      case 4: r = bwd_fast<4, XT, DT, DXT>(x, d, M, hpre, hpost, w, dx, T, C, eps, ws, st); break;
+      case 8: r = bwd_fast<8, XT, DT, DXT>(x, d, M, hpre, hpost, w, dx, T, C, eps, ws, st); break;
+      default: break;
+    }
+    if (r >= 0) return r;
+  }
+  const int na = n + 1;
+  const size_t smem = ((size_t)n * n + 2 * n + 2 * (size_t)na * kGenLD) * sizeof(float);
+  auto kern = k_bwd_generic<XT, DT, DXT>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_bwd(generic): %s", cudaGetErrorString(e));
+  }
+  const int G = persistent_grid(kern, kGenBD, smem, T, max_partial_rows(T));
+  BwdPtrs p = ws_ptrs(ws, G, n);
+  kern<<<G, kGenBD, smem, st>>>(x, d, M, hpre, hpost, w, dx, T, n, C, eps, p.p, p.c, p.hdr);
+  return check_launch("mhc_bwd(generic)");
+}
+
+int launch_bwd(const void* x, int xdt, const void* dout, int ddt, const float* M,
+               const float* hpre, const float* hpost, const float* w, void* dx, int dxdt,
+               int64_t T, int n, int C, float eps, void* ws, size_t ws_bytes, cudaStream_t st) {
+  const size_t need = bwd_ws_bytes(T, n, C);
+  if (ws_bytes < need || !ws)
+    return set_error(MHC_ERR_WORKSPACE, "mhc_bwd: workspace %zu < %zu bytes", ws_bytes, need);
+  if (dxdt != xdt)
+    return set_error(MHC_ERR_UNSUPPORTED, "mhc_bwd: dx dtype must equal x dtype");
+  if (ddt != MHC_F32 && ddt != xdt)
+    return set_error(MHC_ERR_UNSUPPORTED, "mhc_bwd: d_out dtype must be fp32 or x's dtype");
+  // T == 0 still launches one CTA so that the workspace holds zero partials.
+  const int64_t Te = T;
+  if (xdt == MHC_F32)
+    return bwd_typed<float, float, float>(x, dout, M, hpre, hpost, w, dx, Te, n, C, eps, ws, st);
+  if (xdt == MHC_BF16 && ddt == MHC_F32)
+    return bwd_typed<bf16, float, bf16>(x, dout, M, hpre, hpost, w, dx, Te, n, C, eps, ws, st);
+  if (xdt == MHC_BF16)
+    return bwd_typed<bf16, bf16, bf16>(x, dout, M, hpre, hpost, w, dx, Te, n, C, eps, ws, st);
+  if (xdt == MHC_F16 && ddt == MHC_F32)
+    return bwd_typed<f16, float, f16>(x, dout, M, hpre, hpost, w, dx, Te, n, C, eps, ws, st);
+  return bwd_typed<f16, f16, f16>(x, dout, M, hpre, hpost, w, dx, Te, n, C, eps, ws, st);
+}
+
+int launch_finalize(const void* ws, int n, int C, float* dM, float* dhpre, float* dhpost,
+                    float* dw, const float* hpre_raw, const float* hpost_raw,
+                    const float* hres_raw, const float* tape, int iters, float eps,
+                    float* dhpre_raw, float* dhpost_raw, float* dhres_raw, cudaStream_t st) {
+  const int nbc = (C + kFinBD - 1) / kFinBD;
+  k_finalize<<<nbc + 1, kFinBD, 0, st>>>(static_cast<const char*>(ws), n, C, dM, dhpre, dhpost,
+                                          dw, hpre_raw, hpost_raw, hres_raw, tape, iters, eps,
+                                          dhpre_raw, dhpost_raw, dhres_raw);
+  return check_launch("mhc_bwd_finalize");
+}
+
+}  // namespace mhc

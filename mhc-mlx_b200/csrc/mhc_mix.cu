@@ -1,0 +1,773 @@
+// MHCRewire-side kernels for sm_100a: stream mix + add (reference
+// stream_mix_add.metal, metal.py:954-1014), its backward (reference
+// stream_mix_backward_dx.metal + mhc_backward_dM.metal, metal.py:2661-2690),
+// the fused post-combine of layer.py:302-337 (H_pre/H_post folded in-kernel),
+// the input pre-scale of layer.py:478-480, and residual_add_agg
+// (reference residual_add_agg.metal, metal.py:1673-1731, utils.py:4-24).
+//
+// All of these are elementwise over columns with an n x n mix across the
+// streams of one token: thread = (token, VEC consecutive columns), the n
+// stream values of those columns in registers, one read of every input and
+// one write of every output.  Parameter gradients are reduced per CTA into a
+// partial row and summed in a fixed order by a one-CTA finalize.
+//
+// Combined forward (rewire form; the plain mix is hpre = hpost = 1):
+//   out_i = hpost_i * (y_i + sum_j M_ij (hpre_j x_j))
+// Combined backward:
+//   dz_i = hpost_i d_i,  dy_i = dz_i,  dx_j = hpre_j sum_i M_ij dz_i
+//   Q_ij = sum d_i x_j,  R_i = sum d_i y_i          (partials)
+//   dM_ij = hpost_i hpre_j Q_ij
+//   dhpre_j = sum_i hpost_i M_ij Q_ij
+//   dhpost_i = R_i + sum_j M_ij hpre_j Q_ij
+#include <cstdlib>
+
+#include "mhc_common.cuh"
+#include "mhc_internal.h"
+
+namespace mhc {
+
+constexpr int kMixBD = 256;
+
+// Loop helper: with EXACT the stream count is the compile-time MAXN, else a
+// runtime n <= MAXN handled with predicated, fully unrolled loops (the
+// register arrays stay in registers).
+#define MHC_FOR_N(j) _Pragma("unroll") for (int j = 0; j < MAXN; ++j) if (EXACT || j < n)
+
+template <typename T, int V>
+__device__ __forceinline__ void load_or_zero(const T* p, bool ok, float (&o)[V]) {
+  if (ok) load_vec<T, V>(p, o);
+  else
+#pragma unroll
+    for (int v = 0; v < V; ++v) o[v] = 0.f;
+}
+
+// ------------------------------------------------------------ combine fwd --
+template <int MAXN, bool EXACT, typename XT, typename YT, typename OT, int VEC>
+__global__ void __launch_bounds__(kMixBD)
+k_combine_fwd(const XT* __restrict__ x, const YT* __restrict__ y, const float* __restrict__ Mg,
+              const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
+              OT* __restrict__ out, int64_t T, int n, int C) {
+  __shared__ float sM[MAXN * MAXN];
+  __shared__ float shpre[MAXN], shpost[MAXN];
+  const int nr = EXACT ? MAXN : n;
+  for (int e = threadIdx.x; e < nr * nr; e += blockDim.x) sM[e] = Mg[e];
+  for (int e = threadIdx.x; e < nr; e += blockDim.x) {
+    shpre[e] = hpre_g ? hpre_g[e] : 1.0f;
+    shpost[e] = hpost_g ? hpost_g[e] : 1.0f;
+  }
+  __syncthreads();
+  const int groups = (C + VEC - 1) / VEC;
+  const int64_t items = T * groups;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < items;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = q / groups;
+    const int col = (int)(q - t * groups) * VEC;
+    const int64_t base = t * (int64_t)nr * C + col;
+    float xs[MAXN][VEC];
+    MHC_FOR_N(j) {
+      load_vec<XT, VEC>(x + base + (int64_t)j * C, xs[j]);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) xs[j][v] *= shpre[j];
+    }
+    MHC_FOR_N(i) {
+      float yv[VEC], o[VEC];
+      load_vec<YT, VEC>(y + base + (int64_t)i * C, yv);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) o[v] = 0.f;
+      MHC_FOR_N(j) {
+        const float mij = sM[i * nr + j];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) o[v] = fmaf(mij, xs[j][v], o[v]);
+      }
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) o[v] = shpost[i] * (yv[v] + o[v]);
+      store_vec<OT, VEC>(out + base + (int64_t)i * C, o);
+    }
+  }
+}
+
+// ----------------------------------------------------------- prescale fwd --
+template <int MAXN, bool EXACT, typename XT, typename OT, int VEC>
+__global__ void __launch_bounds__(kMixBD)
+k_prescale_fwd(const XT* __restrict__ x, const float* __restrict__ hpre_g, OT* __restrict__ xo,
+               int64_t T, int n, int C) {
+  __shared__ float shpre[MAXN];
+  const int nr = EXACT ? MAXN : n;
+  for (int e = threadIdx.x; e < nr; e += blockDim.x) shpre[e] = hpre_g[e];
+  __syncthreads();
+  const int groups = (C + VEC - 1) / VEC;
+  const int64_t items = T * groups;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < items;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = q / groups;
+    const int col = (int)(q - t * groups) * VEC;
+    const int64_t base = t * (int64_t)nr * C + col;
+    MHC_FOR_N(i) {
+      float v_[VEC];
+      load_vec<XT, VEC>(x + base + (int64_t)i * C, v_);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) v_[v] *= shpre[i];
+      store_vec<OT, VEC>(xo + base + (int64_t)i * C, v_);
+    }
+  }
+}
+
+// ------------------------------------------------------- residual add agg --
+// out = x + res (fp32 add, stored as OT); y_agg = sum_i hpre_i (x + res)_i in
+// fp32 from the unrounded sums, as residual_add_agg.metal does.
+template <int MAXN, bool EXACT, typename XT, typename RT, typename OT, int VEC>
+__global__ void __launch_bounds__(kMixBD)
+k_residual_add_agg(const XT* __restrict__ x, const RT* __restrict__ res,
+                   const float* __restrict__ hpre_g, OT* __restrict__ out,
+                   float* __restrict__ yagg, int64_t T, int n, int C) {
+  __shared__ float shpre[MAXN];
+  const int nr = EXACT ? MAXN : n;
+  for (int e = threadIdx.x; e < nr; e += blockDim.x) shpre[e] = hpre_g[e];
+  __syncthreads();
+  const int groups = (C + VEC - 1) / VEC;
+  const int64_t items = T * groups;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < items;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = q / groups;
+    const int col = (int)(q - t * groups) * VEC;
+    const int64_t base = t * (int64_t)nr * C + col;
+    float agg[VEC];
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) agg[v] = 0.f;
+    MHC_FOR_N(i) {
+      float a[VEC], b[VEC];
+      load_vec<XT, VEC>(x + base + (int64_t)i * C, a);
+      load_vec<RT, VEC>(res + base + (int64_t)i * C, b);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        a[v] += b[v];
+        agg[v] = fmaf(a[v], shpre[i], agg[v]);
+      }
+      store_vec<OT, VEC>(out + base + (int64_t)i * C, a);
+    }
+    // y_agg rows are C fp32 values; VEC is 1, 4 or 8 and C % VEC == 0
+    store_vec<float, VEC>(yagg + t * C + col, agg);
+  }
+}
+
+// ------------------------------------------------------- combine bwd (fast) --
+// Thread-per-(token, VEC columns) with the Q / R partials in registers
+// (n <= 8).  HAS_Y: accumulate R_i = sum d_i y_i (rewire mode).
+template <int N, typename XT, typename YT, typename DT, typename DXT, typename DYT, int VEC,
+          bool HAS_Y>
+__global__ void __launch_bounds__(kMixBD)
+k_combine_bwd_fast(const XT* __restrict__ x, const YT* __restrict__ y,
+                   const DT* __restrict__ dout, const float* __restrict__ Mg,
+                   const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
+                   DXT* __restrict__ dx, DYT* __restrict__ dy, int64_t T, int C,
+                   float* __restrict__ ws_p, int* __restrict__ ws_hdr) {
+  constexpr int P = N * N + 2 * N;
+  __shared__ float sM[N * N];
+  __shared__ float sacc[(kMixBD / 32) * P];
+  for (int e = threadIdx.x; e < N * N; e += blockDim.x) sM[e] = Mg[e];
+  float hpre[N], hpost[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    hpre[i] = hpre_g ? __ldg(hpre_g + i) : 1.0f;
+    hpost[i] = hpost_g ? __ldg(hpost_g + i) : 1.0f;
+  }
+  __syncthreads();
+  float aQ[N][N], aR[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    aR[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) aQ[i][j] = 0.f;
+  }
+  const int groups = (C + VEC - 1) / VEC;
+  const int64_t items = T * groups;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < items;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = q / groups;
+    const int col = (int)(q - t * groups) * VEC;
+    const int64_t base = t * (int64_t)N * C + col;
+    float xr[N][VEC], dr[N][VEC];
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      load_vec<XT, VEC>(x + base + (int64_t)i * C, xr[i]);
+      load_vec<DT, VEC>(dout + base + (int64_t)i * C, dr[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      if constexpr (HAS_Y) {
+        float yv[VEC];
+        load_vec<YT, VEC>(y + base + (int64_t)i * C, yv);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) aR[i] = fmaf(dr[i][v], yv[v], aR[i]);
+      }
+#pragma unroll
+      for (int j = 0; j < N; ++j)
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) aQ[i][j] = fmaf(dr[i][v], xr[j][v], aQ[i][j]);
+    }
+    // dz overwrites d; dy = dz
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) dr[i][v] *= hpost[i];
+      if (dy) store_vec<DYT, VEC>(dy + base + (int64_t)i * C, dr[i]);
+    }
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      float o[VEC];
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) o[v] = 0.f;
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const float mij = sM[i * N + j];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) o[v] = fmaf(mij, dr[i][v], o[v]);
+      }
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) o[v] *= hpre[j];
+      store_vec<DXT, VEC>(dx + base + (int64_t)j * C, o);
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float v = warp_sum(aQ[i][j]);
+      if (lane == 0) sacc[warp * P + i * N + j] = v;
+    }
+    const float r = warp_sum(aR[i]);
+    if (lane == 0) { sacc[warp * P + N * N + i] = r; sacc[warp * P + N * N + N + i] = 0.f; }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < P; e += blockDim.x) {
+    float s = 0.f;
+    for (int w = 0; w < nw; ++w) s += sacc[w * P + e];
+    ws_p[(size_t)blockIdx.x * P + e] = s;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) ws_hdr[0] = gridDim.x;
+}
+
+// ---------------------------------------------------- combine bwd (generic) --
+// Any n <= 64: a tile of kMixGenBD columns of d and x is staged in shared
+// memory (plus the products d_i y_i when y is given); each thread writes
+// dx / dy for its column, then the CTA accumulates Q = D X^T with 4x4
+// register blocks and thread i (< n) sums the product row i into R_i.
+constexpr int kMixGenBD = 128;
+constexpr int kMixGenLD = kMixGenBD + 1;
+constexpr int kMixRB = 4;
+constexpr int kMixMaxBlk = 2;  // ceil(16 * 16 / 128)
+
+__host__ __device__ inline size_t mix_gen_smem(int n) {
+  return ((size_t)n * n + 2 * (size_t)n + 3 * (size_t)n * kMixGenLD) * sizeof(float);
+}
+
+template <typename XT, typename YT, typename DT, typename DXT, typename DYT>
+__global__ void __launch_bounds__(kMixGenBD)
+k_combine_bwd_generic(const XT* __restrict__ x, const YT* __restrict__ y,
+                      const DT* __restrict__ dout, const float* __restrict__ Mg,
+                      const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
+                      DXT* __restrict__ dx, DYT* __restrict__ dy, int64_t T, int n, int C,
+                      float* __restrict__ ws_p, int* __restrict__ ws_hdr) {
+  extern __shared__ float smem[];
+  float* sM = smem;
+  float* shpre = sM + n * n;
+  float* shpost = shpre + n;
+  float* sx = shpost + n;            // n x LD
+  float* sd = sx + n * kMixGenLD;    // n x LD
+  float* sp = sd + n * kMixGenLD;    // n x LD  (d_i * y_i)
+  const int tid = threadIdx.x;
+  for (int e = tid; e < n * n; e += kMixGenBD) sM[e] = Mg[e];
+  for (int e = tid; e < n; e += kMixGenBD) {
+    shpre[e] = hpre_g ? hpre_g[e] : 1.0f;
+    shpost[e] = hpost_g ? hpost_g[e] : 1.0f;
+  }
+  const int nb = (n + kMixRB - 1) / kMixRB;
+  const int nblk = nb * nb;
+  float acc[kMixMaxBlk][kMixRB][kMixRB];
+#pragma unroll
+  for (int q = 0; q < kMixMaxBlk; ++q)
+#pragma unroll
+    for (int a = 0; a < kMixRB; ++a)
+#pragma unroll
+      for (int b = 0; b < kMixRB; ++b) acc[q][a][b] = 0.f;
+  float accR = 0.f;
+  __syncthreads();
+  const int tiles = (C + kMixGenBD - 1) / kMixGenBD;
+  const int64_t ntile = T * tiles;
+  for (int64_t tt = blockIdx.x; tt < ntile; tt += gridDim.x) {
+    const int64_t t = tt / tiles;
+    const int c0 = (int)(tt - t * tiles) * kMixGenBD;
+    const int c = c0 + tid;
+    const bool ok = c < C;
+    const int64_t base = t * (int64_t)n * C + c;
+    for (int i = 0; i < n; ++i) {
+      const float dv = ok ? to_f(dout[base + (int64_t)i * C]) : 0.f;
+      sx[i * kMixGenLD + tid] = ok ? to_f(x[base + (int64_t)i * C]) : 0.f;
+      sd[i * kMixGenLD + tid] = dv;
+      if (y) sp[i * kMixGenLD + tid] = ok ? dv * to_f(y[base + (int64_t)i * C]) : 0.f;
+    }
+    if (ok) {
+      for (int j = 0; j < n; ++j) {
+        float o = 0.f;
+        for (int i = 0; i < n; ++i)
+          o = fmaf(sM[i * n + j], shpost[i] * sd[i * kMixGenLD + tid], o);
+        dx[base + (int64_t)j * C] = from_f<DXT>(o * shpre[j]);
+      }
+      if (dy)
+        for (int i = 0; i < n; ++i)
+          dy[base + (int64_t)i * C] = from_f<DYT>(shpost[i] * sd[i * kMixGenLD + tid]);
+    }
+    __syncthreads();
+    const int width = min(kMixGenBD, C - c0);
+#pragma unroll
+    for (int q = 0; q < kMixMaxBlk; ++q) {
+      const int blk = tid + q * kMixGenBD;
+      if (blk >= nblk) break;
+      const int i0 = (blk / nb) * kMixRB, j0 = (blk % nb) * kMixRB;
+      for (int cc = 0; cc < width; ++cc) {
+        float dv[kMixRB], xv[kMixRB];
+#pragma unroll
+        for (int a = 0; a < kMixRB; ++a) {
+          dv[a] = (i0 + a < n) ? sd[(i0 + a) * kMixGenLD + cc] : 0.f;
+          xv[a] = (j0 + a < n) ? sx[(j0 + a) * kMixGenLD + cc] : 0.f;
+        }
+#pragma unroll
+        for (int a = 0; a < kMixRB; ++a)
+#pragma unroll
+          for (int b = 0; b < kMixRB; ++b) acc[q][a][b] = fmaf(dv[a], xv[b], acc[q][a][b]);
+      }
+    }
+    if (y && tid < n)
+      for (int cc = 0; cc < width; ++cc) accR += sp[tid * kMixGenLD + cc];
+    __syncthreads();
+  }
+  const int P = n * n + 2 * n;
+  float* pr = ws_p + (size_t)blockIdx.x * P;
+  if (tid < n) { pr[n * n + tid] = accR; pr[n * n + n + tid] = 0.f; }
+#pragma unroll
+  for (int q = 0; q < kMixMaxBlk; ++q) {
+    const int blk = tid + q * kMixGenBD;
+    if (blk >= nblk) break;
+    const int i0 = (blk / nb) * kMixRB, j0 = (blk % nb) * kMixRB;
+#pragma unroll
+    for (int a = 0; a < kMixRB; ++a)
+#pragma unroll
+      for (int b = 0; b < kMixRB; ++b) {
+        const int i = i0 + a, j = j0 + b;
+        if (i < n && j < n) pr[i * n + j] = acc[q][a][b];
+      }
+  }
+  if (blockIdx.x == 0 && tid == 0) ws_hdr[0] = gridDim.x;
+}
+
+// ----------------------------------------------------------- prescale bwd --
+// dx_i = hpre_i d_i;  R_i = sum d_i x_i  (-> dH_pre_act)
+template <int MAXN, bool EXACT, typename XT, typename DT, typename DXT, int VEC>
+__global__ void __launch_bounds__(kMixBD)
+k_prescale_bwd(const XT* __restrict__ x, const DT* __restrict__ dout,
+               const float* __restrict__ hpre_g, DXT* __restrict__ dx, int64_t T, int n, int C,
+               float* __restrict__ ws_p, int* __restrict__ ws_hdr) {
+  __shared__ float shpre[MAXN];
+  __shared__ float sacc[(kMixBD / 32) * MAXN];
+  const int nr = EXACT ? MAXN : n;
+  for (int e = threadIdx.x; e < nr; e += blockDim.x) shpre[e] = hpre_g[e];
+  __syncthreads();
+  float aR[MAXN];
+#pragma unroll
+  for (int i = 0; i < MAXN; ++i) aR[i] = 0.f;
+  const int groups = (C + VEC - 1) / VEC;
+  const int64_t items = T * groups;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < items;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = q / groups;
+    const int col = (int)(q - t * groups) * VEC;
+    const int64_t base = t * (int64_t)nr * C + col;
+    MHC_FOR_N(i) {
+      float a[VEC], d[VEC];
+      load_vec<XT, VEC>(x + base + (int64_t)i * C, a);
+      load_vec<DT, VEC>(dout + base + (int64_t)i * C, d);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        aR[i] = fmaf(d[v], a[v], aR[i]);
+        d[v] *= shpre[i];
+      }
+      store_vec<DXT, VEC>(dx + base + (int64_t)i * C, d);
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  MHC_FOR_N(i) {
+    const float v = warp_sum(aR[i]);
+    if (lane == 0) sacc[warp * MAXN + i] = v;
+  }
+  __syncthreads();
+  const int P = nr * nr + 2 * nr;
+  float* pr = ws_p + (size_t)blockIdx.x * P;
+  for (int e = threadIdx.x; e < P; e += blockDim.x) {
+    float s = 0.f;
+    if (e >= nr * nr && e < nr * nr + nr)
+      for (int w = 0; w < nw; ++w) s += sacc[w * MAXN + (e - nr * nr)];
+    pr[e] = s;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) ws_hdr[0] = gridDim.x;
+}
+
+// --------------------------------------------------------------- finalize --
+// One CTA: sums the partial rows (fixed order) into Q (n*n) and R (n), then
+//   mode 0 (mix):      dM = Q
+//   mode 1 (rewire):   dM_ij = hpost_i hpre_j Q_ij, dhpre_j = sum_i hpost_i M_ij Q_ij,
+//                      dhpost_i = R_i + sum_j M_ij hpre_j Q_ij
+//   mode 2 (prescale): dhpre = R
+__global__ void __launch_bounds__(256)
+k_combine_finalize(const char* __restrict__ ws, int n, const float* __restrict__ M,
+                   const float* __restrict__ hpre, const float* __restrict__ hpost, int mode,
+                   float* __restrict__ dM, float* __restrict__ dhpre, float* __restrict__ dhpost) {
+  __shared__ float sQ[kMaxN * kMaxN + kMaxN];
+  const int G = *reinterpret_cast<const int*>(ws);
+  const int P = n * n + 2 * n;
+  const float* wp = reinterpret_cast<const float*>(ws + WsLayout::params_off());
+  for (int e = threadIdx.x; e < n * n + n; e += blockDim.x) {
+    float s = 0.f;
+    for (int g = 0; g < G; ++g) s += wp[(size_t)g * P + e];
+    sQ[e] = s;
+  }
+  __syncthreads();
+  const float* sR = sQ + n * n;
+  if (mode == 0) {
+    for (int e = threadIdx.x; e < n * n; e += blockDim.x) dM[e] = sQ[e];
+  } else if (mode == 2) {
+    for (int e = threadIdx.x; e < n; e += blockDim.x) dhpre[e] = sR[e];
+  } else {
+    for (int e = threadIdx.x; e < n * n; e += blockDim.x) {
+      const int i = e / n, j = e % n;
+      if (dM) dM[e] = (hpost[i] * hpre[j]) * sQ[e];
+    }
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+      float s = 0.f;
+      for (int i = 0; i < n; ++i) s = fmaf(hpost[i] * M[i * n + j], sQ[i * n + j], s);
+      if (dhpre) dhpre[j] = s;
+    }
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      float s = sR[i];
+      for (int j = 0; j < n; ++j) s = fmaf(M[i * n + j] * hpre[j], sQ[i * n + j], s);
+      if (dhpost) dhpost[i] = s;
+    }
+  }
+}
+
+// ================================================================= launch ==
+static int mix_rows_cap() { return sm_count() * 4; }
+
+static int elem_grid(int64_t items, int cap) {
+  int64_t b = (items + kMixBD - 1) / kMixBD;
+  if (b > cap) b = cap;
+  return (int)(b < 1 ? 1 : b);
+}
+
+static bool all_aligned(std::initializer_list<const void*> ps) {
+  for (const void* p : ps)
+    if (p && !aligned16(p)) return false;
+  return true;
+}
+
+// ---- combine forward (plain mix: hpre = hpost = NULL) ----------------------
+template <typename XT, typename YT, typename OT>
+static int combine_fwd_t(const void* xv, const void* yv, const float* M, const float* hpre,
+                         const float* hpost, void* ov, int64_t T, int n, int C,
+                         cudaStream_t st) {
+  constexpr int VX = VecOf<XT>::value;
+  const XT* x = static_cast<const XT*>(xv);
+  const YT* y = static_cast<const YT*>(yv);
+  OT* o = static_cast<OT*>(ov);
+  const bool vec = (C % VX == 0) && all_aligned({xv, yv, ov});
+  const int cap = sm_count() * 8;
+  const int gv = elem_grid(T * (C / VX), cap), g1 = elem_grid(T * C, cap);
+#define MHC_CF(NN, EX, V, G) \
+  k_combine_fwd<NN, EX, XT, YT, OT, V><<<G, kMixBD, 0, st>>>(x, y, M, hpre, hpost, o, T, n, C)
+  switch (n) {
+    case 1: if (vec) MHC_CF(1, true, VX, gv); else MHC_CF(1, true, 1, g1); break;
+    case 2: if (vec) MHC_CF(2, true, VX, gv); else MHC_CF(2, true, 1, g1); break;
+    case 4: if (vec) MHC_CF(4, true, VX, gv); else MHC_CF(4, true, 1, g1); break;
+    case 8: if (vec) MHC_CF(8, true, VX, gv); else MHC_CF(8, true, 1, g1); break;
+    default: MHC_CF(64, false, 1, g1); break;
+  }
+#undef MHC_CF
+  return check_launch("combine_fwd");
+}
+
+// dtype triples: y in {x, f32}; out in {f32, x}
+template <typename XT>
+static int combine_fwd_x(const void* x, const void* y, int ydt, const float* M, const float* hpre,
+                         const float* hpost, void* o, int odt, int64_t T, int n, int C,
+                         cudaStream_t st, int xdt) {
+  const bool y32 = ydt == MHC_F32, o32 = odt == MHC_F32;
+  if (!y32 && ydt != xdt) return set_error(MHC_ERR_UNSUPPORTED, "mix: y dtype must be fp32 or x's dtype");
+  if (!o32 && odt != xdt) return set_error(MHC_ERR_UNSUPPORTED, "mix: out dtype must be fp32 or x's dtype");
+  if (y32 && o32) return combine_fwd_t<XT, float, float>(x, y, M, hpre, hpost, o, T, n, C, st);
+  if (y32) return combine_fwd_t<XT, float, XT>(x, y, M, hpre, hpost, o, T, n, C, st);
+  if (o32) return combine_fwd_t<XT, XT, float>(x, y, M, hpre, hpost, o, T, n, C, st);
+  return combine_fwd_t<XT, XT, XT>(x, y, M, hpre, hpost, o, T, n, C, st);
+}
+
+static int combine_fwd(const void* x, int xdt, const void* y, int ydt, const float* M,
+                       const float* hpre, const float* hpost, void* o, int odt, int64_t T, int n,
+                       int C, cudaStream_t st) {
+  if (T == 0) return MHC_OK;
+  switch (xdt) {
+    case MHC_F32: return combine_fwd_x<float>(x, y, ydt, M, hpre, hpost, o, odt, T, n, C, st, xdt);
+    case MHC_BF16: return combine_fwd_x<bf16>(x, y, ydt, M, hpre, hpost, o, odt, T, n, C, st, xdt);
+    default: return combine_fwd_x<f16>(x, y, ydt, M, hpre, hpost, o, odt, T, n, C, st, xdt);
+  }
+}
+
+int launch_mix_add_fwd(const void* x, int xdt, const float* M, const void* y, int ydt, void* out,
+                       int odt, int64_t T, int n, int C, cudaStream_t st) {
+  return combine_fwd(x, xdt, y, ydt, M, nullptr, nullptr, out, odt, T, n, C, st);
+}
+
+int launch_rewire_fwd(const void* x, int xdt, const void* y, int ydt, const float* M,
+                      const float* hpre, const float* hpost, void* out, int odt, int64_t T,
+                      int n, int C, cudaStream_t st) {
+  return combine_fwd(x, xdt, y, ydt, M, hpre, hpost, out, odt, T, n, C, st);
+}
+
+// ---- combine backward --------------------------------------------------------
+size_t mix_ws_bytes(int64_t T, int n, int C) {
+  (void)T; (void)C;
+  return WsLayout::bytes(mix_rows_cap(), n, 0);
+}
+
+template <typename XT, typename YT, typename DT>
+static int combine_bwd_t(const void* xv, const void* yv, const void* dv, const float* M,
+                         const float* hpre, const float* hpost, void* dxv, void* dyv, int64_t T,
+                         int n, int C, void* ws, cudaStream_t st) {
+  using DXT = XT;
+  using DYT = YT;
+  constexpr int VX = VecOf<XT>::value;
+  const XT* x = static_cast<const XT*>(xv);
+  const YT* y = static_cast<const YT*>(yv);
+  const DT* d = static_cast<const DT*>(dv);
+  DXT* dx = static_cast<DXT*>(dxv);
+  DYT* dy = static_cast<DYT*>(dyv);
+  char* b = static_cast<char*>(ws);
+  float* wp = reinterpret_cast<float*>(b + WsLayout::params_off());
+  int* hdr = reinterpret_cast<int*>(b);
+  const int cap = mix_rows_cap();
+  const bool vec = (C % VX == 0) && all_aligned({xv, yv, dv, dxv, dyv});
+  const int gv = elem_grid(T * (C / VX), cap), g1 = elem_grid(T * C, cap);
+  const bool has_y = y != nullptr;
+#define MHC_CB(NN, V, HY, G)                                                                    \
+  k_combine_bwd_fast<NN, XT, YT, DT, DXT, DYT, V, HY><<<G, kMixBD, 0, st>>>(x, y, d, M, hpre,  \
+                                                                            hpost, dx, dy, T, \
+                                                                            C, wp, hdr)
+#define MHC_CB2(NN, V, G) \
+  do { if (has_y) MHC_CB(NN, V, true, G); else MHC_CB(NN, V, false, G); } while (0)
+  switch (n) {
+    case 1: if (vec) MHC_CB2(1, VX, gv); else MHC_CB2(1, 1, g1); return check_launch("combine_bwd");
+    case 2: if (vec) MHC_CB2(2, VX, gv); else MHC_CB2(2, 1, g1); return check_launch("combine_bwd");
+    case 4: if (vec) MHC_CB2(4, VX, gv); else MHC_CB2(4, 1, g1); return check_launch("combine_bwd");
+    case 8: MHC_CB2(8, 1, g1); return check_launch("combine_bwd");
+    default: break;
+  }
+#undef MHC_CB2
+#undef MHC_CB
+  const size_t smem = mix_gen_smem(n);
+  auto kern = k_combine_bwd_generic<XT, YT, DT, DXT, DYT>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "combine_bwd: %s", cudaGetErrorString(e));
+  }
+  const int64_t ntile = T * ((C + kMixGenBD - 1) / kMixGenBD);
+  const int G = (int)(ntile < cap ? (ntile < 1 ? 1 : ntile) : cap);
+  kern<<<G, kMixGenBD, smem, st>>>(x, y, d, M, hpre, hpost, dx, dy, T, n, C, wp, hdr);
+  return check_launch("combine_bwd(generic)");
+}
+
+template <typename XT>
+static int combine_bwd_x(const void* x, int xdt, const void* y, int ydt, const void* d, int ddt,
+                         const float* M, const float* hpre, const float* hpost, void* dx,
+                         void* dy, int64_t T, int n, int C, void* ws, cudaStream_t st) {
+  const bool y32 = (y == nullptr) || ydt == MHC_F32;
+  const bool d32 = ddt == MHC_F32;
+  if (y && !y32 && ydt != xdt) return set_error(MHC_ERR_UNSUPPORTED, "mix bwd: y dtype must be fp32 or x's dtype");
+  if (!d32 && ddt != xdt) return set_error(MHC_ERR_UNSUPPORTED, "mix bwd: d_out dtype must be fp32 or x's dtype");
+  if (y32 && d32) return combine_bwd_t<XT, float, float>(x, y, d, M, hpre, hpost, dx, dy, T, n, C, ws, st);
+  if (y32) return combine_bwd_t<XT, float, XT>(x, y, d, M, hpre, hpost, dx, dy, T, n, C, ws, st);
+  if (d32) return combine_bwd_t<XT, XT, float>(x, y, d, M, hpre, hpost, dx, dy, T, n, C, ws, st);
+  return combine_bwd_t<XT, XT, XT>(x, y, d, M, hpre, hpost, dx, dy, T, n, C, ws, st);
+}
+
+static int combine_bwd(const void* x, int xdt, const void* y, int ydt, const void* d, int ddt,
+                       const float* M, const float* hpre, const float* hpost, void* dx, int dxdt,
+                       void* dy, int dydt, int mode, float* dM, float* dhpre, float* dhpost,
+                       int64_t T, int n, int C, void* ws, size_t ws_bytes, cudaStream_t st) {
+  const size_t need = mix_ws_bytes(T, n, C);
+  if (!ws || ws_bytes < need)
+    return set_error(MHC_ERR_WORKSPACE, "mix bwd: workspace %zu < %zu bytes", ws_bytes, need);
+  if (dxdt != xdt) return set_error(MHC_ERR_UNSUPPORTED, "mix bwd: dx dtype must equal x dtype");
+  if (dy && dydt != (y ? ydt : dydt))
+    return set_error(MHC_ERR_UNSUPPORTED, "mix bwd: dy dtype must equal y dtype");
+  int r;
+  switch (xdt) {
+    case MHC_F32: r = combine_bwd_x<float>(x, xdt, y, ydt, d, ddt, M, hpre, hpost, dx, dy, T, n, C, ws, st); break;
+    case MHC_BF16: r = combine_bwd_x<bf16>(x, xdt, y, ydt, d, ddt, M, hpre, hpost, dx, dy, T, n, C, ws, st); break;
+    default: r = combine_bwd_x<f16>(x, xdt, y, ydt, d, ddt, M, hpre, hpost, dx, dy, T, n, C, ws, st); break;
+  }
+  if (r != MHC_OK) return r;
+  k_combine_finalize<<<1, 256, 0, st>>>(static_cast<const char*>(ws), n, M, hpre, hpost, mode,
+                                        dM, dhpre, dhpost);
+  return check_launch("combine_finalize");
+}
+
+int launch_mix_add_bwd(const void* x, int xdt, const float* M, const void* dout, int ddt,
+                       void* dx, int dxdt, float* dM, int64_t T, int n, int C, void* ws,
+                       size_t ws_bytes, cudaStream_t st) {
+  return combine_bwd(x, xdt, nullptr, MHC_F32, dout, ddt, M, nullptr, nullptr, dx, dxdt, nullptr,
+                     MHC_F32, 0, dM, nullptr, nullptr, T, n, C, ws, ws_bytes, st);
+}
+
+int launch_rewire_bwd(const void* x, int xdt, const void* y, int ydt, const void* dout, int ddt,
+                      const float* M, const float* hpre, const float* hpost, void* dx, int dxdt,
+                      void* dy, int dydt, float* dM, float* dhpre, float* dhpost, int64_t T,
+                      int n, int C, void* ws, size_t ws_bytes, cudaStream_t st) {
+  return combine_bwd(x, xdt, y, ydt, dout, ddt, M, hpre, hpost, dx, dxdt, dy, dydt, 1, dM,
+                     dhpre, dhpost, T, n, C, ws, ws_bytes, st);
+}
+
+// ---- pre-scale -----------------------------------------------------------------
+template <typename XT, typename OT>
+static int prescale_fwd_t(const void* xv, const float* hpre, void* ov, int64_t T, int n, int C,
+                          cudaStream_t st) {
+  constexpr int VX = VecOf<XT>::value;
+  const XT* x = static_cast<const XT*>(xv);
+  OT* o = static_cast<OT*>(ov);
+  const bool vec = (C % VX == 0) && all_aligned({xv, ov});
+  const int cap = sm_count() * 8;
+  const int gv = elem_grid(T * (C / VX), cap), g1 = elem_grid(T * C, cap);
+#define MHC_PF(NN, EX, V, G) \
+  k_prescale_fwd<NN, EX, XT, OT, V><<<G, kMixBD, 0, st>>>(x, hpre, o, T, n, C)
+  switch (n) {
+    case 1: if (vec) MHC_PF(1, true, VX, gv); else MHC_PF(1, true, 1, g1); break;
+    case 2: if (vec) MHC_PF(2, true, VX, gv); else MHC_PF(2, true, 1, g1); break;
+    case 4: if (vec) MHC_PF(4, true, VX, gv); else MHC_PF(4, true, 1, g1); break;
+    case 8: if (vec) MHC_PF(8, true, VX, gv); else MHC_PF(8, true, 1, g1); break;
+    default: if (vec) MHC_PF(64, false, VX, gv); else MHC_PF(64, false, 1, g1); break;
+  }
+#undef MHC_PF
+  return check_launch("prescale_fwd");
+}
+
+int launch_prescale_fwd(const void* x, int xdt, const float* hpre, void* xo, int odt, int64_t T,
+                        int n, int C, cudaStream_t st) {
+  if (T == 0) return MHC_OK;
+  if (odt != xdt && odt != MHC_F32)
+    return set_error(MHC_ERR_UNSUPPORTED, "prescale: out dtype must be fp32 or x's dtype");
+  switch (xdt) {
+    case MHC_F32: return prescale_fwd_t<float, float>(x, hpre, xo, T, n, C, st);
+    case MHC_BF16:
+      return odt == MHC_F32 ? prescale_fwd_t<bf16, float>(x, hpre, xo, T, n, C, st)
+                            : prescale_fwd_t<bf16, bf16>(x, hpre, xo, T, n, C, st);
+    default:
+      return odt == MHC_F32 ? prescale_fwd_t<f16, float>(x, hpre, xo, T, n, C, st)
+                            : prescale_fwd_t<f16, f16>(x, hpre, xo, T, n, C, st);
+  }
+}
+
+template <typename XT, typename DT>
+static int prescale_bwd_t(const void* xv, const void* dv, const float* hpre, void* dxv, int64_t T,
+                          int n, int C, void* ws, cudaStream_t st) {
+  constexpr int VX = VecOf<XT>::value;
+  const XT* x = static_cast<const XT*>(xv);
+  const DT* d = static_cast<const DT*>(dv);
+  XT* dx = static_cast<XT*>(dxv);
+  char* b = static_cast<char*>(ws);
+  float* wp = reinterpret_cast<float*>(b + WsLayout::params_off());
+  int* hdr = reinterpret_cast<int*>(b);
+  const bool vec = (C % VX == 0) && all_aligned({xv, dv, dxv});
+  const int cap = mix_rows_cap();
+  const int gv = elem_grid(T * (C / VX), cap), g1 = elem_grid(T * C, cap);
+#define MHC_PB(NN, EX, V, G) \
+  k_prescale_bwd<NN, EX, XT, DT, XT, V><<<G, kMixBD, 0, st>>>(x, d, hpre, dx, T, n, C, wp, hdr)
+  switch (n) {
+    case 1: if (vec) MHC_PB(1, true, VX, gv); else MHC_PB(1, true, 1, g1); break;
+    case 2: if (vec) MHC_PB(2, true, VX, gv); else MHC_PB(2, true, 1, g1); break;
+    case 4: if (vec) MHC_PB(4, true, VX, gv); else MHC_PB(4, true, 1, g1); break;
+    case 8: if (vec) MHC_PB(8, true, VX, gv); else MHC_PB(8, true, 1, g1); break;
+    default: MHC_PB(64, false, 1, g1); break;
+  }
+#undef MHC_PB
+  return check_launch("prescale_bwd");
+}
+
+int launch_prescale_bwd(const void* x, int xdt, const void* d, int ddt, const float* hpre,
+                        void* dx, int dxdt, float* dhpre, int64_t T, int n, int C, void* ws,
+                        size_t ws_bytes, cudaStream_t st) {
+  const size_t need = mix_ws_bytes(T, n, C);
+  if (!ws || ws_bytes < need)
+    return set_error(MHC_ERR_WORKSPACE, "prescale bwd: workspace %zu < %zu bytes", ws_bytes, need);
+  if (dxdt != xdt) return set_error(MHC_ERR_UNSUPPORTED, "prescale bwd: dx dtype must equal x dtype");
+  if (ddt != xdt && ddt != MHC_F32)
+    return set_error(MHC_ERR_UNSUPPORTED, "prescale bwd: d dtype must be fp32 or x's dtype");
+  int r;
+  switch (xdt) {
+    case MHC_F32: r = prescale_bwd_t<float, float>(x, d, hpre, dx, T, n, C, ws, st); break;
+    case MHC_BF16:
+      r = ddt == MHC_F32 ? prescale_bwd_t<bf16, float>(x, d, hpre, dx, T, n, C, ws, st)
+                         : prescale_bwd_t<bf16, bf16>(x, d, hpre, dx, T, n, C, ws, st);
+      break;
+    default:
+      r = ddt == MHC_F32 ? prescale_bwd_t<f16, float>(x, d, hpre, dx, T, n, C, ws, st)
+                         : prescale_bwd_t<f16, f16>(x, d, hpre, dx, T, n, C, ws, st);
+      break;
+  }
+  if (r != MHC_OK) return r;
+  k_combine_finalize<<<1, 256, 0, st>>>(static_cast<const char*>(ws), n, nullptr, nullptr, nullptr,
+                                        2, nullptr, dhpre, nullptr);
+  return check_launch("prescale_finalize");
+}
+
+// ---- residual add + aggregate ----------------------------------------------------
+template <typename XT, typename RT, typename OT>
+static int residual_t(const void* xv, const void* rv, const float* hpre, void* ov, float* yagg,
+                      int64_t T, int n, int C, cudaStream_t st) {
+  constexpr int VX = VecOf<XT>::value;
+  const XT* x = static_cast<const XT*>(xv);
+  const RT* r = static_cast<const RT*>(rv);
+  OT* o = static_cast<OT*>(ov);
+  const bool vec = (C % VX == 0) && all_aligned({xv, rv, ov, yagg});
+  const int cap = sm_count() * 8;
+  const int gv = elem_grid(T * (C / VX), cap), g1 = elem_grid(T * C, cap);
+#define MHC_RA(NN, EX, V, G) \
+  k_residual_add_agg<NN, EX, XT, RT, OT, V><<<G, kMixBD, 0, st>>>(x, r, hpre, o, yagg, T, n, C)
+  switch (n) {
+    case 1: if (vec) MHC_RA(1, true, VX, gv); else MHC_RA(1, true, 1, g1); break;
+    case 2: if (vec) MHC_RA(2, true, VX, gv); else MHC_RA(2, true, 1, g1); break;
+    case 4: if (vec) MHC_RA(4, true, VX, gv); else MHC_RA(4, true, 1, g1); break;
+    case 8: if (vec) MHC_RA(8, true, VX, gv); else MHC_RA(8, true, 1, g1); break;
+    default: MHC_RA(64, false, 1, g1); break;
+  }
+#undef MHC_RA
+  return check_launch("residual_add_agg");
+}
+
+template <typename XT>
+static int residual_x(const void* x, int xdt, const void* r, int rdt, const float* hpre, void* o,
+                      int odt, float* yagg, int64_t T, int n, int C, cudaStream_t st) {
+  if (rdt != xdt) return set_error(MHC_ERR_UNSUPPORTED, "residual_add_agg: res dtype must equal x dtype");
+  if (odt == MHC_F32) return residual_t<XT, XT, float>(x, r, hpre, o, yagg, T, n, C, st);
+  if (odt == MHC_BF16) return residual_t<XT, XT, bf16>(x, r, hpre, o, yagg, T, n, C, st);
+  return residual_t<XT, XT, f16>(x, r, hpre, o, yagg, T, n, C, st);
+}
+
+int launch_residual_add_agg(const void* x, int xdt, const void* res, int rdt, const float* hpre,
+                            void* out, int odt, float* yagg, int64_t T, int n, int C,
+                            cudaStream_t st) {
+  if (T == 0) return MHC_OK;
+  switch (xdt) {
+    case MHC_F32: return residual_x<float>(x, xdt, res, rdt, hpre, out, odt, yagg, T, n, C, st);
+    case MHC_BF16: return residual_x<bf16>(x, xdt, res, rdt, hpre, out, odt, yagg, T, n, C, st);
+    default: return residual_x<f16>(x, xdt, res, rdt, hpre, out, odt, yagg, T, n, C, st);
+  }
+}
+
+}  // namespace mhc

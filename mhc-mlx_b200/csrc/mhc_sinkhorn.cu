@@ -1,0 +1,329 @@
+// Parameter kernels: sigmoid activations + single-matrix Sinkhorn-Knopp
+// forward/backward, and the batched [batch, n, n] Sinkhorn kernels.
+//
+// Reference: reference.py:20-69 (math), metal.py:1525-1577 and
+// kernels/sinkhorn_knopp.metal (single-matrix forward launcher),
+// metal.py:1978-2016 and kernels/sinkhorn_knopp_backward.metal (backward).
+#include "mhc_sinkhorn.cuh"
+#include "mhc_internal.h"
+
+namespace mhc {
+
+size_t sk_tape_floats(int n, int iters) { return (size_t)iters * sk_tape_stride(n); }
+
+// ---------------------------------------------------------------------------
+// Single matrix: one CTA computes H_pre_act, H_post_act and M (+ tape).
+__global__ void __launch_bounds__(256)
+k_params_fwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost_raw,
+             const float* __restrict__ hres_raw, int n, int iters, float eps,
+             float* __restrict__ hpre, float* __restrict__ hpost, float* __restrict__ M,
+             float* __restrict__ tape) {
+  __shared__ float P[kMaxN * (kMaxN + 1)];
+  const int tid = threadIdx.x;
+  if (tid < n) {
+    if (hpre_raw) hpre[tid] = sigmoidf_(hpre_raw[tid]);
+    if (hpost_raw) hpost[tid] = 2.0f * sigmoidf_(hpost_raw[tid]);
+  }
+  if (hres_raw) sk_forward_block(hres_raw, n, iters, eps, P, tape, M);
+}
+
+__global__ void __launch_bounds__(256)
+k_params_bwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost_raw,
+             const float* __restrict__ hres_raw, const float* __restrict__ tape, int n,
+             int iters, float eps, const float* __restrict__ dhpre,
+             const float* __restrict__ dhpost, const float* __restrict__ dM,
+             float* __restrict__ dhpre_raw, float* __restrict__ dhpost_raw,
+             float* __restrict__ dhres_raw) {
+  __shared__ float D[kMaxN * (kMaxN + 1)];
+  const int tid = threadIdx.x, ld = sk_ld(n);
+  if (tid < n) {
+    // d/da sigmoid(a) = s (1 - s); H_post_act = 2 sigmoid(b)
+    if (hpre_raw && dhpre) {
+      const float s = sigmoidf_(hpre_raw[tid]);
+      dhpre_raw[tid] = dhpre[tid] * (1.0f - s) * s;
+    }
+    if (hpost_raw && dhpost) {
+      const float s = sigmoidf_(hpost_raw[tid]);
+      dhpost_raw[tid] = (2.0f * dhpost[tid]) * (1.0f - s) * s;
+    }
+  }
+  if (hres_raw && dM) {
+    for (int e = tid; e < n * n; e += blockDim.x) D[(e / n) * ld + e % n] = dM[e];
+    __syncthreads();
+    sk_backward_block(hres_raw, tape, n, iters, eps, D, dhres_raw);
+  }
+}
+
+int launch_params_fwd(const float* hpre_raw, const float* hpost_raw, const float* hres_raw,
+                      int n, int iters, float eps, float* hpre, float* hpost, float* M,
+                      float* tape, cudaStream_t st) {
+  const int threads = n <= 32 ? 32 : 64;
+  k_params_fwd<<<1, threads, 0, st>>>(hpre_raw, hpost_raw, hres_raw, n, iters, eps, hpre,
+                                      hpost, M, tape);
+  return check_launch("params_fwd");
+}
+
+int launch_params_bwd(const float* hpre_raw, const float* hpost_raw, const float* hres_raw,
+                      const float* tape, int n, int iters, float eps, const float* dhpre,
+                      const float* dhpost, const float* dM, float* dhpre_raw,
+                      float* dhpost_raw, float* dhres_raw, cudaStream_t st) {
+  const int threads = n <= 32 ? 32 : 64;
+  k_params_bwd<<<1, threads, 0, st>>>(hpre_raw, hpost_raw, hres_raw, tape, n, iters, eps,
+                                      dhpre, dhpost, dM, dhpre_raw, dhpost_raw, dhres_raw);
+  return check_launch("params_bwd");
+}
+
+// ---------------------------------------------------------------------------
+// Batched, n divides 32: one thread per matrix row, a matrix occupies n
+// consecutive lanes; row sums are per-thread, column sums are butterfly
+// shuffles across the n lanes (identical bits on every lane of the group).
+template <int N>
+__device__ __forceinline__ void sk_row_load(const float* __restrict__ src, float (&p)[N]) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < N; j += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(src) + j / 4);
+      p[j] = v.x; p[j + 1] = v.y; p[j + 2] = v.z; p[j + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; ++j) p[j] = __ldg(src + j);
+  }
+}
+template <int N>
+__device__ __forceinline__ void sk_row_store(float* __restrict__ dst, const float (&p)[N]) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < N; j += 4)
+      reinterpret_cast<float4*>(dst)[j / 4] = make_float4(p[j], p[j + 1], p[j + 2], p[j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; ++j) dst[j] = p[j];
+  }
+}
+
+template <int N>
+__global__ void __launch_bounds__(256)
+k_sk_batched_fwd(const float* __restrict__ H, int64_t batch, int iters, float eps,
+                 float* __restrict__ M) {
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t m = gid / N;
+  const int row = (int)(gid % N);
+  const bool valid = m < batch;
+  float p[N];
+  if (valid) sk_row_load<N>(H + (m * N + row) * N, p);
+  else
+#pragma unroll
+    for (int j = 0; j < N; ++j) p[j] = 0.f;
+  float mx = p[0];
+#pragma unroll
+  for (int j = 1; j < N; ++j) mx = fmaxf(mx, p[j]);
+#pragma unroll
+  for (int j = 0; j < N; ++j) p[j] = expf(p[j] - mx);
+  for (int k = 0; k < iters; ++k) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) s += p[j];
+    const float rs = row_scale(s, eps);
+#pragma unroll
+    for (int j = 0; j < N; ++j) p[j] *= rs;
+#pragma unroll
+    for (int j = 0; j < N; ++j) p[j] *= col_scale(group_sum<N>(p[j]), eps);
+  }
+  if (valid) sk_row_store<N>(M + (m * N + row) * N, p);
+}
+
+// Backward: replays the forward into a shared-memory tape laid out
+// [iters][N + 2][blockDim] (thread index fastest: conflict-free), then runs
+// reverse mode through the iterations.
+template <int N>
+__global__ void __launch_bounds__(256)
+k_sk_batched_bwd(const float* __restrict__ H, const float* __restrict__ dM, int64_t batch,
+                 int iters, float eps, float* __restrict__ dH) {
+  extern __shared__ float s_tape[];
+  const int bd = blockDim.x, tid = threadIdx.x;
+  const int64_t gid = (int64_t)blockIdx.x * bd + tid;
+  const int64_t m = gid / N;
+  const int row = (int)(gid % N);
+  const int gbase = (tid & 31) & ~(N - 1);
+  const bool valid = m < batch;
+  auto TP = [&](int k, int f) -> float& { return s_tape[((size_t)k * (N + 2) + f) * bd + tid]; };
+
+  float h[N], p[N];
+  if (valid) sk_row_load<N>(H + (m * N + row) * N, h);
+  else
+#pragma unroll
+    for (int j = 0; j < N; ++j) h[j] = 0.f;
+  float mx = h[0];
+#pragma unroll
+  for (int j = 1; j < N; ++j) mx = fmaxf(mx, h[j]);
+#pragma unroll
+  for (int j = 0; j < N; ++j) p[j] = expf(h[j] - mx);
+  for (int k = 0; k < iters; ++k) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) { TP(k, j) = p[j]; s += p[j]; }
+    TP(k, N) = s;
+    const float rs = row_scale(s, eps);
+#pragma unroll
+    for (int j = 0; j < N; ++j) p[j] *= rs;
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float c = group_sum<N>(p[j]);
+      if (j == row) TP(k, N + 1) = c;
+      p[j] *= col_scale(c, eps);
+    }
+  }
+
+  float d[N];
+  if (valid) sk_row_load<N>(dM + (m * N + row) * N, d);
+  else
+#pragma unroll
+    for (int j = 0; j < N; ++j) d[j] = 0.f;
+  for (int k = iters - 1; k >= 0; --k) {
+    float pa[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) pa[j] = TP(k, j);
+    const float r = TP(k, N);
+    const float rs = row_scale(r, eps);
+    const float cown = TP(k, N + 1);
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float c = __shfl_sync(0xffffffffu, cown, gbase + j);
+      const float dcs = group_sum<N>(d[j] * (pa[j] * rs));
+      const float dc = c > eps ? -dcs / (c * c) : 0.f;
+      d[j] = d[j] * col_scale(c, eps) + dc;
+    }
+    float drs = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) drs += d[j] * pa[j];
+    const float dr = r > eps ? -drs / (r * r) : 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) d[j] = d[j] * rs + dr;
+  }
+  float S = 0.f, cnt = 0.f;
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    d[j] *= expf(h[j] - mx);
+    S += d[j];
+    cnt += (h[j] == mx) ? 1.f : 0.f;
+  }
+  const float share = S / cnt;
+#pragma unroll
+  for (int j = 0; j < N; ++j) d[j] -= (h[j] == mx) ? share : 0.f;
+  if (valid) sk_row_store<N>(dH + (m * N + row) * N, d);
+}
+
+// Batched fallback for n that does not divide 32 (or a tape too large for
+// shared memory): persistent CTAs, one matrix at a time, tape in the
+// workspace (one tape region per CTA).
+__global__ void __launch_bounds__(64)
+k_sk_batched_generic(const float* __restrict__ H, const float* __restrict__ dM, int64_t batch,
+                     int n, int iters, float eps, float* __restrict__ out,
+                     float* __restrict__ tapes, int backward) {
+  __shared__ float P[kMaxN * (kMaxN + 1)];
+  const int ld = sk_ld(n), nn = n * n;
+  float* tape = backward ? tapes + (size_t)blockIdx.x * (size_t)iters * sk_tape_stride(n) : nullptr;
+  for (int64_t m = blockIdx.x; m < batch; m += gridDim.x) {
+    const float* Hm = H + m * nn;
+    if (!backward) {
+      sk_forward_block(Hm, n, iters, eps, P, nullptr, out + m * nn);
+    } else {
+      sk_forward_block(Hm, n, iters, eps, P, tape, nullptr);
+      __syncthreads();
+      for (int e = threadIdx.x; e < nn; e += blockDim.x) P[(e / n) * ld + e % n] = dM[m * nn + e];
+      __syncthreads();
+      sk_backward_block(Hm, tape, n, iters, eps, P, out + m * nn);
+    }
+    __syncthreads();
+  }
+}
+
+static bool sk_small_path(int n) { return n == 1 || n == 2 || n == 4 || n == 8 || n == 16 || n == 32; }
+
+// Threads per CTA for the shared-memory-tape backward; 0 if even one warp's
+// tape does not fit.
+static int sk_bwd_threads(int n, int iters) {
+  const size_t per_thread = (size_t)iters * (n + 2) * sizeof(float);
+  const size_t budget = 160 * 1024;
+  for (int t = 256; t >= 32; t -= 32)
+    if (per_thread * t <= budget) return t;
+  return 0;
+}
+
+static int sk_generic_grid(int64_t batch) {
+  int64_t g = (int64_t)sm_count() * 8;
+  if (g > batch) g = batch;
+  return (int)(g < 1 ? 1 : g);
+}
+
+size_t sk_batched_ws_bytes(int64_t batch, int n, int iters) {
+  if (sk_small_path(n) && sk_bwd_threads(n, iters) > 0) return 0;
+  return (size_t)sk_generic_grid(batch) * sk_tape_floats(n, iters) * sizeof(float);
+}
+
+template <int N>
+static int sk_fwd_small(const float* H, int64_t batch, int iters, float eps, float* M,
+                        cudaStream_t st) {
+  const int threads = 256;
+  const int64_t blocks = (batch * N + threads - 1) / threads;
+  k_sk_batched_fwd<N><<<(unsigned)blocks, threads, 0, st>>>(H, batch, iters, eps, M);
+  return check_launch("sinkhorn_batched_fwd");
+}
+
+template <int N>
+static int sk_bwd_small(const float* H, const float* dM, int64_t batch, int iters, float eps,
+                        float* dH, cudaStream_t st) {
+  const int threads = sk_bwd_threads(N, iters);
+  const size_t smem = (size_t)iters * (N + 2) * threads * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_sk_batched_bwd<N>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "sinkhorn_batched_bwd: %s", cudaGetErrorString(e));
+  }
+  const int64_t blocks = (batch * N + threads - 1) / threads;
+  k_sk_batched_bwd<N><<<(unsigned)blocks, threads, smem, st>>>(H, dM, batch, iters, eps, dH);
+  return check_launch("sinkhorn_batched_bwd");
+}
+
+int launch_sk_batched_fwd(const float* H, int64_t batch, int n, int iters, float eps, float* M,
+                          void* ws, size_t ws_bytes, cudaStream_t st) {
+  (void)ws; (void)ws_bytes;
+  if (batch == 0) return MHC_OK;
+  switch (n) {
+    case 1: return sk_fwd_small<1>(H, batch, iters, eps, M, st);
+    case 2: return sk_fwd_small<2>(H, batch, iters, eps, M, st);
+    case 4: return sk_fwd_small<4>(H, batch, iters, eps, M, st);
+    case 8: return sk_fwd_small<8>(H, batch, iters, eps, M, st);
+    case 16: return sk_fwd_small<16>(H, batch, iters, eps, M, st);
+    case 32: return sk_fwd_small<32>(H, batch, iters, eps, M, st);
+    default: break;
+  }
+  k_sk_batched_generic<<<sk_generic_grid(batch), 64, 0, st>>>(H, nullptr, batch, n, iters, eps, M,
+                                                              nullptr, 0);
+  return check_launch("sinkhorn_batched_fwd(generic)");
+}
+
+int launch_sk_batched_bwd(const float* H, const float* dM, int64_t batch, int n, int iters,
+                          float eps, float* dH, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (batch == 0) return MHC_OK;
+  if (sk_small_path(n) && sk_bwd_threads(n, iters) > 0) {
+    switch (n) {
+      case 1: return sk_bwd_small<1>(H, dM, batch, iters, eps, dH, st);
+      case 2: return sk_bwd_small<2>(H, dM, batch, iters, eps, dH, st);
+      case 4: return sk_bwd_small<4>(H, dM, batch, iters, eps, dH, st);
+      case 8: return sk_bwd_small<8>(H, dM, batch, iters, eps, dH, st);
+      case 16: return sk_bwd_small<16>(H, dM, batch, iters, eps, dH, st);
+      case 32: return sk_bwd_small<32>(H, dM, batch, iters, eps, dH, st);
+      default: break;
+    }
+  }
+  const size_t need = sk_batched_ws_bytes(batch, n, iters);
+  if (ws_bytes < need || (need && !ws))
+    return set_error(MHC_ERR_WORKSPACE, "sinkhorn_batched_bwd: workspace %zu < %zu bytes", ws_bytes, need);
+  k_sk_batched_generic<<<sk_generic_grid(batch), 64, 0, st>>>(H, dM, batch, n, iters, eps, dH,
+                                                              static_cast<float*>(ws), 1);
+  return check_launch("sinkhorn_batched_bwd(generic)");
+}
+
+}  // namespace mhc

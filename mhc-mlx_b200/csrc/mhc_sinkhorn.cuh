@@ -1,0 +1,113 @@
+// Block-level Sinkhorn-Knopp forward/backward for one n x n matrix (n <= 64),
+// shared by the parameter kernels, the batched fallback and the backward
+// finalize kernel.
+//
+// Forward (reference.py:20-48, :58-69):
+//   P0 = exp(H - rowmax(H));  repeat iters: rows scaled by 1/sum (if > eps,
+//   else 1), then columns scaled by 1/sum (if > eps, else 0).
+// Backward: reverse-mode through the recorded iterations; the tape holds,
+// per iteration k, the matrix before the row step (n*n), the row sums (n)
+// and the column sums (n).  The row-scaled matrix is recomputed bit-exactly
+// from them (same fp32 multiply as the forward).  The max shift contributes
+// -(rowsum of dS) split evenly over the row's maxima, as autodiff of max does.
+#pragma once
+
+#include "mhc_common.cuh"
+
+namespace mhc {
+
+// Shared-memory matrices use a padded leading dimension so that both the
+// thread-per-row and thread-per-column sweeps are bank-conflict free.
+__host__ __device__ constexpr int sk_ld(int n) { return n + 1; }
+
+__host__ __device__ inline size_t sk_tape_stride(int n) { return (size_t)n * n + 2 * (size_t)n; }
+
+// P: shared [n][ld]; tape: global, nullable.  Writes M (global, nullable).
+__device__ inline void sk_forward_block(const float* __restrict__ H, int n, int iters, float eps,
+                                        float* P, float* __restrict__ tape,
+                                        float* __restrict__ M) {
+  const int tid = threadIdx.x, bd = blockDim.x, ld = sk_ld(n), nn = n * n;
+  for (int i = tid; i < n; i += bd) {
+    float m = H[i * n];
+    for (int j = 1; j < n; ++j) m = fmaxf(m, H[i * n + j]);
+    for (int j = 0; j < n; ++j) P[i * ld + j] = expf(H[i * n + j] - m);
+  }
+  __syncthreads();
+  for (int k = 0; k < iters; ++k) {
+    float* tk = tape ? tape + (size_t)k * sk_tape_stride(n) : nullptr;
+    if (tk)
+      for (int e = tid; e < nn; e += bd) tk[e] = P[(e / n) * ld + e % n];
+    for (int i = tid; i < n; i += bd) {
+      float s = 0.f;
+      for (int j = 0; j < n; ++j) s += P[i * ld + j];
+      const float sc = row_scale(s, eps);
+      for (int j = 0; j < n; ++j) P[i * ld + j] *= sc;
+      if (tk) tk[nn + i] = s;
+    }
+    __syncthreads();
+    for (int j = tid; j < n; j += bd) {
+      float s = 0.f;
+      for (int i = 0; i < n; ++i) s += P[i * ld + j];
+      const float sc = col_scale(s, eps);
+      for (int i = 0; i < n; ++i) P[i * ld + j] *= sc;
+      if (tk) tk[nn + n + j] = s;
+    }
+    __syncthreads();
+  }
+  if (M)
+    for (int e = tid; e < nn; e += bd) M[e] = P[(e / n) * ld + e % n];
+}
+
+// D: shared [n][ld] holding dM on entry (caller fills it and syncs).
+// Writes dH (global).
+__device__ inline void sk_backward_block(const float* __restrict__ H,
+                                         const float* __restrict__ tape, int n, int iters,
+                                         float eps, float* D, float* __restrict__ dH) {
+  const int tid = threadIdx.x, bd = blockDim.x, ld = sk_ld(n), nn = n * n;
+  for (int k = iters - 1; k >= 0; --k) {
+    const float* tk = tape + (size_t)k * sk_tape_stride(n);
+    // column step: out = Pb * cs_j, c_j = sum_i Pb_ij
+    for (int j = tid; j < n; j += bd) {
+      const float c = tk[nn + n + j];
+      const float cs = col_scale(c, eps);
+      float dcs = 0.f;
+      for (int i = 0; i < n; ++i) {
+        const float pb = tk[i * n + j] * row_scale(tk[nn + i], eps);
+        dcs += D[i * ld + j] * pb;
+      }
+      const float dc = c > eps ? -dcs / (c * c) : 0.f;
+      for (int i = 0; i < n; ++i) D[i * ld + j] = D[i * ld + j] * cs + dc;
+    }
+    __syncthreads();
+    // row step: Pb = Pa * rs_i, r_i = sum_j Pa_ij
+    for (int i = tid; i < n; i += bd) {
+      const float r = tk[nn + i];
+      const float rs = row_scale(r, eps);
+      float drs = 0.f;
+      for (int j = 0; j < n; ++j) drs += D[i * ld + j] * tk[i * n + j];
+      const float dr = r > eps ? -drs / (r * r) : 0.f;
+      for (int j = 0; j < n; ++j) D[i * ld + j] = D[i * ld + j] * rs + dr;
+    }
+    __syncthreads();
+  }
+  // exp and the row-max shift
+  for (int i = tid; i < n; i += bd) {
+    float m = H[i * n];
+    for (int j = 1; j < n; ++j) m = fmaxf(m, H[i * n + j]);
+    float S = 0.f, cnt = 0.f;
+    for (int j = 0; j < n; ++j) {
+      const float h = H[i * n + j];
+      const float ds = D[i * ld + j] * expf(h - m);
+      D[i * ld + j] = ds;
+      S += ds;
+      cnt += (h == m) ? 1.f : 0.f;
+    }
+    const float share = S / cnt;
+    for (int j = 0; j < n; ++j) {
+      const float h = H[i * n + j];
+      dH[i * n + j] = D[i * ld + j] - ((h == m) ? share : 0.f);
+    }
+  }
+}
+
+}  // namespace mhc

@@ -1,0 +1,285 @@
+"""Tensor-level wrappers over the C ABI.
+
+Each function takes CUDA tensors, allocates outputs and workspaces through
+torch's caching allocator, and enqueues one or two kernels on the current
+stream.  Shapes are assumed validated by the caller (metal.py / layer.py);
+only contiguity, dtype and device are normalised here.
+"""
+
+from __future__ import annotations
+
+import contextlib
+
+import torch
+
+from . import _capi as C
+
+F32 = torch.float32
+
+# Optional per-launch timing: when set to a dict, each timed C-ABI launch
+# appends a (start, end) pair of CUDA events recorded on the launching
+# stream under the entry point's name.  Off (None) in normal use.
+TIMING: dict | None = None
+
+
+@contextlib.contextmanager
+def _timed(name: str, ref: torch.Tensor):
+    if TIMING is None:
+        yield
+        return
+    st = torch.cuda.current_stream(ref.device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    yield
+    b.record(st)
+    TIMING.setdefault(name, []).append((a, b))
+
+
+def _c(t: torch.Tensor) -> torch.Tensor:
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def _f32(t: torch.Tensor) -> torch.Tensor:
+    return _c(t if t.dtype == F32 else t.float())
+
+
+def _io(t: torch.Tensor) -> torch.Tensor:
+    """Activation tensors stay in fp32/fp16/bf16; anything else becomes fp32."""
+    if t.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        t = t.float()
+    return _c(t)
+
+
+def _ws(nbytes: int, dev: torch.device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=dev)
+
+
+# ------------------------------------------------------------ parameters --
+def tape_floats(n: int, iters: int) -> int:
+    return int(C.query("mhc_sinkhorn_tape_floats", n, iters))
+
+
+def params_fwd(H_pre_raw, H_post_raw, H_res_raw, iters: int, eps: float, want_tape: bool):
+    """(H_pre_act, H_post_act, M, tape); any raw input may be None."""
+    ref = next(t for t in (H_res_raw, H_pre_raw, H_post_raw) if t is not None)
+    dev = C.require_cuda(H_pre_raw, H_post_raw, H_res_raw)
+    n = ref.shape[0]
+    with torch.cuda.device(dev):
+        pre = _f32(H_pre_raw) if H_pre_raw is not None else None
+        post = _f32(H_post_raw) if H_post_raw is not None else None
+        res = _f32(H_res_raw) if H_res_raw is not None else None
+        hpre = torch.empty(n, dtype=F32, device=dev) if pre is not None else None
+        hpost = torch.empty(n, dtype=F32, device=dev) if post is not None else None
+        M = torch.empty(n, n, dtype=F32, device=dev) if res is not None else None
+        tape = None
+        if want_tape and res is not None and iters > 0:
+            tape = torch.empty(tape_floats(n, iters), dtype=F32, device=dev)
+        with _timed("mhc_params_fwd", ref):
+            C.call("mhc_params_fwd", C.ptr(pre), C.ptr(post), C.ptr(res), n, int(iters),
+                   float(eps), C.ptr(hpre), C.ptr(hpost), C.ptr(M), C.ptr(tape), C.stream_of(ref))
+    return hpre, hpost, M, tape
+
+
+def params_bwd(H_pre_raw, H_post_raw, H_res_raw, tape, iters: int, eps: float, dhpre, dhpost, dM):
+    """Gradients w.r.t. the raw parameters (None where the input was None)."""
+    ref = next(t for t in (H_res_raw, H_pre_raw, H_post_raw) if t is not None)
+    dev = C.require_cuda(H_pre_raw, H_post_raw, H_res_raw)
+    n = ref.shape[0]
+    with torch.cuda.device(dev):
+        pre = _f32(H_pre_raw) if (H_pre_raw is not None and dhpre is not None) else None
+        post = _f32(H_post_raw) if (H_post_raw is not None and dhpost is not None) else None
+        res = _f32(H_res_raw) if (H_res_raw is not None and dM is not None) else None
+        gpre = torch.empty(n, dtype=F32, device=dev) if pre is not None else None
+        gpost = torch.empty(n, dtype=F32, device=dev) if post is not None else None
+        gres = torch.empty(n, n, dtype=F32, device=dev) if res is not None else None
+        C.call("mhc_params_bwd", C.ptr(pre), C.ptr(post), C.ptr(res), C.ptr(tape), n, int(iters),
+               float(eps), C.ptr(_f32(dhpre) if pre is not None else None),
+               C.ptr(_f32(dhpost) if post is not None else None),
+               C.ptr(_f32(dM) if res is not None else None), C.ptr(gpre), C.ptr(gpost),
+               C.ptr(gres), C.stream_of(ref))
+    return gpre, gpost, gres
+
+
+def sinkhorn_batched_fwd(H: torch.Tensor, iters: int, eps: float) -> torch.Tensor:
+    dev = C.require_cuda(H)
+    B, n, _ = H.shape
+    with torch.cuda.device(dev):
+        Hc = _f32(H)
+        M = torch.empty(B, n, n, dtype=F32, device=dev)
+        C.call("mhc_sinkhorn_batched_fwd", C.ptr(Hc), B, n, int(iters), float(eps), C.ptr(M),
+               C.stream_of(Hc))
+    return M
+
+
+def sinkhorn_batched_bwd(H: torch.Tensor, dM: torch.Tensor, iters: int, eps: float) -> torch.Tensor:
+    dev = C.require_cuda(H, dM)
+    B, n, _ = H.shape
+    with torch.cuda.device(dev):
+        Hc, dMc = _f32(H), _f32(dM)
+        dH = torch.empty(B, n, n, dtype=F32, device=dev)
+        nb = int(C.query("mhc_sinkhorn_batched_workspace_bytes", B, n, int(iters)))
+        ws = _ws(nb, dev) if nb else None
+        C.call("mhc_sinkhorn_batched_bwd", C.ptr(Hc), C.ptr(dMc), B, n, int(iters), float(eps),
+               C.ptr(dH), C.ptr(ws), nb, C.stream_of(Hc))
+    return dH
+
+
+# ------------------------------------------------------------------ layer --
+def layer_fwd(x, M, hpre, hpost, w, eps: float, out_dtype: torch.dtype) -> torch.Tensor:
+    dev = C.require_cuda(x, M, hpre, hpost, w)
+    T, n, Cc = x.shape
+    with torch.cuda.device(dev):
+        xc = _io(x)
+        out = torch.empty(T, n, Cc, dtype=out_dtype, device=dev)
+        args = (C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(_f32(M)), C.ptr(_f32(hpre)),
+                C.ptr(_f32(hpost)), C.ptr(_f32(w)), C.ptr(out), C.dtype_code(out_dtype), T, n, Cc,
+                float(eps), C.stream_of(xc))
+        with _timed("mhc_fwd", xc):
+            C.call("mhc_fwd", *args)
+    return out
+
+
+def layer_bwd(x, dout, M, hpre, hpost, w, eps: float, raw=None):
+    """dx plus either (dM, dH_pre_act, dH_post_act, d_w) or, with
+    raw = (H_pre_raw, H_post_raw, H_res_raw, tape, iters), the raw-parameter
+    gradients (dH_pre_raw, dH_post_raw, dH_res_raw, d_w) from the same
+    finalize launch."""
+    dev = C.require_cuda(x, dout, M, hpre, hpost, w)
+    T, n, Cc = x.shape
+    with torch.cuda.device(dev):
+        xc = _io(x)
+        dc = _c(dout) if dout.dtype in (F32, xc.dtype) else dout.float().contiguous()
+        dx = torch.empty(T, n, Cc, dtype=xc.dtype, device=dev)
+        nb = int(C.query("mhc_bwd_workspace_bytes", T, n, Cc))
+        ws = _ws(nb, dev)
+        st = C.stream_of(xc)
+        args = (C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(dc), C.dtype_code(dc.dtype),
+                C.ptr(_f32(M)), C.ptr(_f32(hpre)), C.ptr(_f32(hpost)), C.ptr(_f32(w)), C.ptr(dx),
+                C.dtype_code(dx.dtype), T, n, Cc, float(eps), C.ptr(ws), nb, st)
+        with _timed("mhc_bwd", xc):
+            C.call("mhc_bwd", *args)
+        dw = torch.empty(Cc, dtype=F32, device=dev)
+        if raw is None:
+            dM = torch.empty(n, n, dtype=F32, device=dev)
+            dpre = torch.empty(n, dtype=F32, device=dev)
+            dpost = torch.empty(n, dtype=F32, device=dev)
+            C.call("mhc_bwd_finalize", C.ptr(ws), n, Cc, C.ptr(dM), C.ptr(dpre), C.ptr(dpost),
+                   C.ptr(dw), None, None, None, None, 0, float(eps), None, None, None, st)
+            return dx, dM, dpre, dpost, dw
+        pre_raw, post_raw, res_raw, tape, iters = raw
+        gpre = torch.empty(n, dtype=F32, device=dev)
+        gpost = torch.empty(n, dtype=F32, device=dev)
+        gres = torch.empty(n, n, dtype=F32, device=dev)
+        args = (C.ptr(ws), n, Cc, None, None, None, C.ptr(dw), C.ptr(_f32(pre_raw)),
+                C.ptr(_f32(post_raw)), C.ptr(_f32(res_raw)), C.ptr(tape), int(iters), float(eps),
+                C.ptr(gpre), C.ptr(gpost), C.ptr(gres), st)
+        with _timed("mhc_bwd_finalize", xc):
+            C.call("mhc_bwd_finalize", *args)
+        return dx, gpre, gpost, gres, dw
+
+
+# -------------------------------------------------------------------- mix --
+def mix_add_fwd(x, M, y, out_dtype=F32) -> torch.Tensor:
+    dev = C.require_cuda(x, M, y)
+    T, n, Cc = x.shape
+    with torch.cuda.device(dev):
+        xc = _io(x)
+        yc = _c(y) if y.dtype in (F32, xc.dtype) else y.float().contiguous()
+        out = torch.empty(T, n, Cc, dtype=out_dtype, device=dev)
+        C.call("mhc_mix_add_fwd", C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(_f32(M)), C.ptr(yc),
+               C.dtype_code(yc.dtype), C.ptr(out), C.dtype_code(out_dtype), T, n, Cc,
+               C.stream_of(xc))
+    return out
+
+
+def mix_add_bwd(x, M, dout):
+    dev = C.require_cuda(x, M, dout)
+    T, n, Cc = x.shape
+    with torch.cuda.device(dev):
+        xc = _io(x)
+        dc = _c(dout) if dout.dtype in (F32, xc.dtype) else dout.float().contiguous()
+        dx = torch.empty(T, n, Cc, dtype=xc.dtype, device=dev)
+        dM = torch.empty(n, n, dtype=F32, device=dev)
+        nb = int(C.query("mhc_mix_bwd_workspace_bytes", T, n, Cc))
+        ws = _ws(nb, dev)
+        C.call("mhc_mix_add_bwd", C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(_f32(M)), C.ptr(dc),
+               C.dtype_code(dc.dtype), C.ptr(dx), C.dtype_code(dx.dtype), C.ptr(dM), T, n, Cc,
+               C.ptr(ws), nb, C.stream_of(xc))
+    return dx, dM
+
+
+def rewire_fwd(x, y, M, hpre, hpost, out_dtype=F32) -> torch.Tensor:
+    dev = C.require_cuda(x, y, M, hpre, hpost)
+    T, n, Cc = x.shape
+    with torch.cuda.device(dev):
+        xc = _io(x)
+        yc = _c(y) if y.dtype in (F32, xc.dtype) else y.float().contiguous()
+        out = torch.empty(T, n, Cc, dtype=out_dtype, device=dev)
+        C.call("mhc_rewire_combine_fwd", C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(yc),
+               C.dtype_code(yc.dtype), C.ptr(_f32(M)), C.ptr(_f32(hpre)), C.ptr(_f32(hpost)),
+               C.ptr(out), C.dtype_code(out_dtype), T, n, Cc, C.stream_of(xc))
+    return out
+
+
+def rewire_bwd(x, y, dout, M, hpre, hpost):
+    dev = C.require_cuda(x, y, dout, M, hpre, hpost)
+    T, n, Cc = x.shape
+    with torch.cuda.device(dev):
+        xc = _io(x)
+        yc = _c(y) if y.dtype in (F32, xc.dtype) else y.float().contiguous()
+        dc = _c(dout) if dout.dtype in (F32, xc.dtype) else dout.float().contiguous()
+        dx = torch.empty(T, n, Cc, dtype=xc.dtype, device=dev)
+        dy = torch.empty(T, n, Cc, dtype=yc.dtype, device=dev)
+        dM = torch.empty(n, n, dtype=F32, device=dev)
+        dpre = torch.empty(n, dtype=F32, device=dev)
+        dpost = torch.empty(n, dtype=F32, device=dev)
+        nb = int(C.query("mhc_rewire_bwd_workspace_bytes", T, n, Cc))
+        ws = _ws(nb, dev)
+        C.call("mhc_rewire_combine_bwd", C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(yc),
+               C.dtype_code(yc.dtype), C.ptr(dc), C.dtype_code(dc.dtype), C.ptr(_f32(M)),
+               C.ptr(_f32(hpre)), C.ptr(_f32(hpost)), C.ptr(dx), C.dtype_code(dx.dtype), C.ptr(dy),
+               C.dtype_code(dy.dtype), C.ptr(dM), C.ptr(dpre), C.ptr(dpost), T, n, Cc, C.ptr(ws),
+               nb, C.stream_of(xc))
+    return dx, dy, dM, dpre, dpost
+
+
+def prescale_fwd(x, hpre, out_dtype=None) -> torch.Tensor:
+    dev = C.require_cuda(x, hpre)
+    T, n, Cc = x.shape
+    with torch.cuda.device(dev):
+        xc = _io(x)
+        odt = out_dtype or xc.dtype
+        out = torch.empty(T, n, Cc, dtype=odt, device=dev)
+        C.call("mhc_prescale_fwd", C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(_f32(hpre)), C.ptr(out),
+               C.dtype_code(odt), T, n, Cc, C.stream_of(xc))
+    return out
+
+
+def prescale_bwd(x, d, hpre):
+    dev = C.require_cuda(x, d, hpre)
+    T, n, Cc = x.shape
+    with torch.cuda.device(dev):
+        xc = _io(x)
+        dc = _c(d) if d.dtype in (F32, xc.dtype) else d.float().contiguous()
+        dx = torch.empty(T, n, Cc, dtype=xc.dtype, device=dev)
+        dpre = torch.empty(n, dtype=F32, device=dev)
+        nb = int(C.query("mhc_mix_bwd_workspace_bytes", T, n, Cc))
+        ws = _ws(nb, dev)
+        C.call("mhc_prescale_bwd", C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(dc),
+               C.dtype_code(dc.dtype), C.ptr(_f32(hpre)), C.ptr(dx), C.dtype_code(dx.dtype),
+               C.ptr(dpre), T, n, Cc, C.ptr(ws), nb, C.stream_of(xc))
+    return dx, dpre
+
+
+def residual_add_agg(x, res, hpre, out_dtype=F32):
+    dev = C.require_cuda(x, res, hpre)
+    T, n, Cc = x.shape
+    with torch.cuda.device(dev):
+        xc = _io(x)
+        rc = _c(res.to(xc.dtype))
+        out = torch.empty(T, n, Cc, dtype=out_dtype, device=dev)
+        yagg = torch.empty(T, Cc, dtype=F32, device=dev)
+        C.call("mhc_residual_add_agg", C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(rc),
+               C.dtype_code(rc.dtype), C.ptr(_f32(hpre)), C.ptr(out), C.dtype_code(out_dtype),
+               C.ptr(yagg), T, n, Cc, C.stream_of(xc))
+    return out, yagg

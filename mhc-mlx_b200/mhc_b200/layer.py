@@ -1,0 +1,305 @@
+"""MHCLayer and MHCRewire as torch modules over the sm_100a kernels.
+
+Same constructor arguments, parameters, initialisation and call semantics as
+the reference (mhc_mlx/layer.py:58-492):
+
+- H_pre_act = sigmoid(H_pre_raw), H_post_act = 2 sigmoid(H_post_raw)
+- M = sinkhorn_knopp(exp(H_res_raw - rowmax))
+- out = stream_mix(x, M) + H_post_act (x) RMSNorm(sum_i H_pre_act[i] x_i)
+
+Forward + backward of MHCLayer is four kernel launches: the parameter
+kernel (sigmoids + Sinkhorn, recording the Sinkhorn tape), the fused
+forward, the fused backward, and one finalize launch that reduces the
+parameter partials and runs the Sinkhorn / sigmoid chain rule.
+
+Differences from the reference, by design: there is no non-CUDA path, so
+``use_metal=False`` or ``MHC_MLX_DISABLE_METAL=1`` raise instead of
+silently switching to a slower implementation, and a kernel failure raises
+instead of warning and falling back (reference layer.py:408-422).
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+from torch import nn
+
+from . import _kernels as K
+from .metal import _HALF, _validate_n
+
+_DISABLE_ENV = "MHC_MLX_DISABLE_METAL"
+
+
+# ------------------------------------------------------- autograd functions --
+class _LayerFn(torch.autograd.Function):
+    """x, raw parameters, rms_weight -> out (fused parameter chain)."""
+
+    @staticmethod
+    def forward(ctx, x, H_pre_raw, H_post_raw, H_res_raw, rms_weight, iters, eps, out_dtype):
+        hpre, hpost, M, tape = K.params_fwd(H_pre_raw, H_post_raw, H_res_raw, iters, eps,
+                                            want_tape=True)
+        out = K.layer_fwd(x, M, hpre, hpost, rms_weight, eps, out_dtype)
+        empty = M.new_empty(0)
+        ctx.save_for_backward(x, H_pre_raw, H_post_raw, H_res_raw, rms_weight, hpre, hpost, M,
+                              tape if tape is not None else empty)
+        ctx.iters, ctx.eps = iters, eps
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        x, pre, post, res, w, hpre, hpost, M, tape = ctx.saved_tensors
+        dx, gpre, gpost, gres, dw = K.layer_bwd(
+            x, dout, M, hpre, hpost, w, ctx.eps,
+            raw=(pre, post, res, tape if tape.numel() else None, ctx.iters))
+        return dx, gpre, gpost, gres, dw, None, None, None
+
+
+class _ParamsFn(torch.autograd.Function):
+    """Raw parameters -> (H_pre_act, H_post_act, M) in one launch."""
+
+    @staticmethod
+    def forward(ctx, H_pre_raw, H_post_raw, H_res_raw, iters, eps):
+        hpre, hpost, M, tape = K.params_fwd(H_pre_raw, H_post_raw, H_res_raw, iters, eps,
+                                            want_tape=True)
+        ctx.save_for_backward(H_pre_raw, H_post_raw, H_res_raw,
+                              tape if tape is not None else M.new_empty(0))
+        ctx.iters, ctx.eps = iters, eps
+        return hpre, hpost, M
+
+    @staticmethod
+    def backward(ctx, dhpre, dhpost, dM):
+        pre, post, res, tape = ctx.saved_tensors
+        z = pre.new_zeros
+        dhpre = dhpre if dhpre is not None else z(pre.shape)
+        dhpost = dhpost if dhpost is not None else z(post.shape)
+        dM = dM if dM is not None else z(res.shape)
+        gpre, gpost, gres = K.params_bwd(pre, post, res, tape if tape.numel() else None,
+                                         ctx.iters, ctx.eps, dhpre, dhpost, dM)
+        return gpre, gpost, gres, None, None
+
+
+class _PrescaleFn(torch.autograd.Function):
+    """x_pre[t, i, c] = x[t, i, c] * H_pre_act[i]  (reference layer.py:478-480)."""
+
+    @staticmethod
+    def forward(ctx, x, hpre):
+        ctx.save_for_backward(x, hpre)
+        return K.prescale_fwd(x, hpre)
+
+    @staticmethod
+    def backward(ctx, d):
+        x, hpre = ctx.saved_tensors
+        dx, dpre = K.prescale_bwd(x, d, hpre)
+        return dx, dpre
+
+
+class _RewireCombineFn(torch.autograd.Function):
+    """out = H_post (y_inner + M (H_pre x))  (reference layer.py:302-337)."""
+
+    @staticmethod
+    def forward(ctx, x, y, M, hpre, hpost):
+        ctx.save_for_backward(x, y, M, hpre, hpost)
+        return K.rewire_fwd(x, y, M, hpre, hpost, torch.float32)
+
+    @staticmethod
+    def backward(ctx, dout):
+        x, y, M, hpre, hpost = ctx.saved_tensors
+        dx, dy, dM, dpre, dpost = K.rewire_bwd(x, y, dout, M, hpre, hpost)
+        return dx, dy, dM, dpre, dpost
+
+
+# --------------------------------------------------------------- modules --
+class MHCLayer(nn.Module):
+    """Manifold-constrained hyper-connection layer over x of shape [B, n, C]."""
+
+    def __init__(
+        self,
+        n: int,
+        C: int,
+        sinkhorn_iters: int = 20,
+        eps: float = 1e-5,
+        use_metal: bool = True,
+        threads_per_group: int | None = 256,
+        identity_init: bool = True,
+        auto_dispatch: bool = True,
+        compile_reference: bool | None = None,
+        dispatch_policy: str = "auto",
+        hybrid_latency: bool = False,
+        hybrid_min_C: int = 8192,
+        latency_avoid_fused_n32_max_C: int = 2048,
+        latency_avoid_fused_B1_min_n: int = 16,
+        throughput_allow_fused_n32_min_B: int = 8,
+        throughput_allow_fused_n32_min_C: int = 4096,
+        throughput_allow_fused_n32_small_C: int = 512,
+        fused_backward: bool = False,
+        mix_kernel: str = "auto",
+        device=None,
+    ):
+        super().__init__()
+        # argument checks of reference layer.py:83-102
+        if n <= 0:
+            raise ValueError("n must be positive")
+        if C <= 0:
+            raise ValueError("C must be positive")
+        if dispatch_policy not in {"auto", "throughput", "latency"}:
+            raise ValueError("dispatch_policy must be one of: auto, throughput, latency")
+        if hybrid_min_C <= 0:
+            raise ValueError("hybrid_min_C must be positive")
+        if latency_avoid_fused_n32_max_C <= 0:
+            raise ValueError("latency_avoid_fused_n32_max_C must be positive")
+        if latency_avoid_fused_B1_min_n <= 0:
+            raise ValueError("latency_avoid_fused_B1_min_n must be positive")
+        if throughput_allow_fused_n32_min_B <= 0:
+            raise ValueError("throughput_allow_fused_n32_min_B must be positive")
+        if throughput_allow_fused_n32_min_C <= 0:
+            raise ValueError("throughput_allow_fused_n32_min_C must be positive")
+        if throughput_allow_fused_n32_small_C < 0:
+            raise ValueError("throughput_allow_fused_n32_small_C must be >= 0")
+        if mix_kernel not in {"auto", "1d", "2d"}:
+            raise ValueError("mix_kernel must be one of: auto, 1d, 2d")
+
+        self.n = int(n)
+        self.C = int(C)
+        self.sinkhorn_iters = int(sinkhorn_iters)
+        self.eps = float(eps)
+        self.use_metal = bool(use_metal) and os.getenv(_DISABLE_ENV, "0") != "1"
+        self.threads_per_group = None if threads_per_group is None else int(threads_per_group)
+        self.identity_init = bool(identity_init)
+        self.auto_dispatch = bool(auto_dispatch)
+        self.compile_reference = bool(compile_reference) if compile_reference is not None else False
+        self.dispatch_policy = str(dispatch_policy)
+        self.hybrid_latency = bool(hybrid_latency)
+        self.hybrid_min_C = int(hybrid_min_C)
+        self.latency_avoid_fused_n32_max_C = int(latency_avoid_fused_n32_max_C)
+        self.latency_avoid_fused_B1_min_n = int(latency_avoid_fused_B1_min_n)
+        self.throughput_allow_fused_n32_min_B = int(throughput_allow_fused_n32_min_B)
+        self.throughput_allow_fused_n32_min_C = int(throughput_allow_fused_n32_min_C)
+        self.throughput_allow_fused_n32_small_C = int(throughput_allow_fused_n32_small_C)
+        self.fused_backward = bool(fused_backward)
+        self.mix_kernel = str(mix_kernel)
+
+        # identity-friendly init (reference layer.py:139-153)
+        f32 = dict(dtype=torch.float32, device=device)
+        if self.identity_init:
+            off = 12.0
+            pre = torch.full((self.n,), -off, **f32)
+            post = torch.full((self.n,), -off, **f32)
+            res = torch.full((self.n, self.n), -off, **f32) + torch.eye(self.n, **f32) * off
+        else:
+            pre = torch.zeros(self.n, **f32)
+            post = torch.zeros(self.n, **f32)
+            res = torch.zeros(self.n, self.n, **f32)
+        self.H_pre_raw = nn.Parameter(pre)
+        self.H_post_raw = nn.Parameter(post)
+        self.H_res_raw = nn.Parameter(res)
+        self.rms_weight = nn.Parameter(torch.ones(self.C, **f32))
+
+    # -- dispatch predicates kept for API compatibility (reference layer.py:175-244).
+    # On B200 every shape runs the fused CUDA kernels; these report that.
+    def _should_use_metal(self, B: int, n: int, C: int) -> bool:
+        if os.getenv(_DISABLE_ENV, "0") == "1" or not self.use_metal:
+            return False
+        return n <= 64
+
+    def _should_use_reference_fallback(self, B: int, n: int, C: int) -> bool:
+        return False
+
+    def _should_use_hybrid(self, B: int, n: int, C: int) -> bool:
+        return False
+
+    def _should_use_fused_backward(self, B: int, n: int, C: int) -> bool:
+        return True
+
+    def _require_cuda_path(self, B: int, n: int, C: int) -> None:
+        if not self._should_use_metal(B, n, C):
+            raise RuntimeError(
+                "mhc_b200 has only the sm_100a CUDA path: use_metal=False or "
+                f"{_DISABLE_ENV}=1 requests a non-CUDA path, which this package does not "
+                "provide (no silent fallback)."
+            )
+
+    def extra_repr(self) -> str:
+        return f"n={self.n}, C={self.C}, sinkhorn_iters={self.sinkhorn_iters}, eps={self.eps}"
+
+    def activations(self):
+        """(H_pre_act, H_post_act, M) with autograd to the raw parameters."""
+        _validate_n(self.n)
+        return _ParamsFn.apply(self.H_pre_raw, self.H_post_raw, self.H_res_raw,
+                               self.sinkhorn_iters, self.eps)
+
+    def mixing_matrix(self) -> torch.Tensor:
+        """Current mixing matrix M (after Sinkhorn), differentiable."""
+        return self.activations()[2]
+
+    def post_combine(self, x_reshaped: torch.Tensor, y_inner_reshaped: torch.Tensor) -> torch.Tensor:
+        """H_post * (y_inner + (M * H_pre) @ x), H_pre/H_post folded in-kernel
+        (reference layer.py:302-337).  Returns float32 like the reference."""
+        if x_reshaped.ndim != 3 or x_reshaped.shape[1] != self.n:
+            raise ValueError(f"x must be [B, n={self.n}, C], got shape {tuple(x_reshaped.shape)}")
+        if tuple(y_inner_reshaped.shape) != tuple(x_reshaped.shape):
+            raise ValueError(
+                f"inner output shape {tuple(y_inner_reshaped.shape)} does not match the residual "
+                f"shape {tuple(x_reshaped.shape)}")
+        B, n, C = x_reshaped.shape
+        self._require_cuda_path(B, n, C)
+        hpre, hpost, M = self.activations()
+        return _RewireCombineFn.apply(x_reshaped, y_inner_reshaped, M, hpre, hpost)
+
+    def forward(self, x_expanded: torch.Tensor, *, return_dtype: torch.dtype | None = None):
+        """out: [B, n, C]; float32 unless return_dtype is a half dtype equal to
+        x's dtype, in which case the kernel writes that dtype directly
+        (reference layer.py:339-435)."""
+        if x_expanded.ndim != 3:
+            raise ValueError(f"x_expanded must be [B, n, C], got shape {tuple(x_expanded.shape)}")
+        B, n, C = x_expanded.shape
+        if n != self.n:
+            raise ValueError(f"x_expanded n={n} does not match layer n={self.n}")
+        if C != self.C:
+            raise ValueError(f"x_expanded C={C} does not match layer C={self.C}")
+        _validate_n(n)
+        self._require_cuda_path(B, n, C)
+        out_dtype = torch.float32
+        if return_dtype is not None and return_dtype == x_expanded.dtype and return_dtype in _HALF:
+            out_dtype = return_dtype
+        out = _LayerFn.apply(x_expanded, self.H_pre_raw, self.H_post_raw, self.H_res_raw,
+                             self.rms_weight, self.sinkhorn_iters, self.eps, out_dtype)
+        if return_dtype is not None and out.dtype != return_dtype:
+            out = out.to(return_dtype)
+        return out
+
+
+class MHCRewire(nn.Module):
+    """Wrap any module F whose output has its input's shape:
+
+        y = H_post * (F(H_pre * x) + M * H_pre * x)
+
+    over the last axis split into n streams of C = dims // n channels
+    (reference layer.py:438-492)."""
+
+    def __init__(self, inner: nn.Module, dims: int, n: int = 32, **mhc_kwargs):
+        super().__init__()
+        self.inner = inner
+        self.n = n
+        self.dims = dims
+        if dims % n != 0:
+            raise ValueError(f"dims {dims} must be divisible by n={n}")
+        self.mhc = MHCLayer(n=n, C=dims // n, **mhc_kwargs)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        dims = x.shape[-1]
+        if dims % self.n != 0:
+            raise ValueError(f"input last dim {dims} must be divisible by n={self.n}")
+        C = dims // self.n
+        B = x.numel() // dims if dims else 0
+        self.mhc._require_cuda_path(B, self.n, C)
+        hpre, hpost, M = self.mhc.activations()
+        x3 = x.reshape(-1, self.n, C)
+        x_pre = _PrescaleFn.apply(x3, hpre).reshape(x.shape)
+        y_inner = self.inner(x_pre)
+        if tuple(y_inner.shape) != tuple(x.shape):
+            raise ValueError(
+                f"inner module output shape {tuple(y_inner.shape)} must equal its input shape "
+                f"{tuple(x.shape)} (mHC needs a residual-compatible module)")
+        out = _RewireCombineFn.apply(x3, y_inner.reshape(-1, self.n, C), M, hpre, hpost)
+        return out.reshape(x.shape)

@@ -1,0 +1,82 @@
+"""Test configuration: import paths, the `gpu` marker and golden fixtures."""
+
+from __future__ import annotations
+
+import json
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+for p in (ROOT, ROOT / "mhc-mlx_b200"):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+GOLDEN_DIR = ROOT / "tests" / "golden"
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA (sm_100a) device")
+    config.addinivalue_line("markers", "slow: long-running")
+
+
+def pytest_collection_modifyitems(config, items):
+    import torch
+
+    if torch.cuda.is_available():
+        return
+    skip = pytest.mark.skip(reason="no CUDA device")
+    for it in items:
+        if "gpu" in it.keywords:
+            it.add_marker(skip)
+
+
+class Golden:
+    """Cases from tests/golden/reference_golden.npz (see make_golden.py)."""
+
+    def __init__(self):
+        self.z = np.load(GOLDEN_DIR / "reference_golden.npz")
+        meta = json.loads((GOLDEN_DIR / "reference_golden.json").read_text())
+        self.cases = {c["case"]: c for c in meta["cases"]}
+
+    def names(self, kind: str) -> list[str]:
+        return [k for k, c in self.cases.items() if c["kind"] == kind]
+
+    def get(self, case: str) -> dict:
+        prefix = case + "/"
+        d = {k[len(prefix):]: self.z[k] for k in self.z.files if k.startswith(prefix)}
+        d.update(self.cases[case])
+        return d
+
+
+_GOLDEN = None
+
+
+def golden() -> Golden:
+    global _GOLDEN
+    if _GOLDEN is None:
+        _GOLDEN = Golden()
+    return _GOLDEN
+
+
+@pytest.fixture(scope="session")
+def gold() -> Golden:
+    return golden()
+
+
+def rel_err(a, b) -> float:
+    """max |a - b| / max |b|  (the reference's relative metric,
+    tests/test_correctness.py:249-251)."""
+    import torch
+
+    a = torch.as_tensor(a).double().cpu()
+    b = torch.as_tensor(b).double().cpu()
+    return float((a - b).abs().max() / max(float(b.abs().max()), 1e-30))
+
+
+def max_abs(a, b) -> float:
+    import torch
+
+    return float((torch.as_tensor(a).double().cpu() - torch.as_tensor(b).double().cpu()).abs().max())

@@ -1,0 +1,251 @@
+"""GPU parity of the fused layer path against the reference's golden vectors and
+the CPU oracle.  All calls go through the C ABI (libmhc_b200.so) via the
+reference-named Python entry points.
+
+Tolerances (max |diff| / max |ref| unless noted):
+  fp32 outputs and gradients: 1e-5 (the reference north star's fp32 bar)
+  half outputs: 5e-3 (fp16) / 2e-2 (bf16) absolute, the reference's test
+  tolerances (tests/test_correctness.py:178-186)
+"""
+
+from __future__ import annotations
+
+import os
+
+import pytest
+import torch
+
+import mhc_b200
+from conftest import golden, max_abs, rel_err
+from mhc_b200 import metal
+from oracle import mhc_oracle as O
+
+pytestmark = pytest.mark.gpu
+G = golden()
+DEV = "cuda"
+F64 = torch.float64
+
+
+def cu(a, dtype=torch.float32):
+    return torch.as_tensor(a).to(DEV, dtype)
+
+
+def x_of(d):
+    return cu(d["x"], getattr(torch, d.get("dtype", "float32")))
+
+
+# ------------------------------------------------------------- Sinkhorn --
+@pytest.mark.parametrize("case", G.names("sinkhorn"))
+def test_sinkhorn_matches_reference(case):
+    d = G.get(case)
+    M = metal.sinkhorn_knopp_metal(cu(d["H"]), iters=d["iters"], eps=d["eps"])
+    assert torch.isfinite(M).all()
+    assert max_abs(M, d["M"]) < 2e-6, case
+
+
+def test_sinkhorn_stability_bomb():
+    layer = mhc_b200.MHCLayer(n=32, C=64).to(DEV)
+    with torch.no_grad():
+        layer.H_res_raw.fill_(100.0)
+    M = layer.mixing_matrix().detach()
+    assert not torch.isnan(M).any()
+    assert (M.sum(1) - 1).abs().max() < 1e-3 and (M.sum(0) - 1).abs().max() < 1e-3
+
+
+@pytest.mark.parametrize("n,iters", [(4, 20), (16, 10), (32, 20), (64, 20), (3, 7), (4, 0), (1, 5)])
+def test_sinkhorn_backward_matches_oracle(n, iters):
+    g = torch.Generator().manual_seed(n * 100 + iters)
+    H = torch.randn(n, n, generator=g)
+    dM = torch.randn(n, n, generator=g)
+    _, dH_ref = O.sinkhorn_grads(H, dM, iters, 1e-5, dtype=F64)
+    dH = metal.sinkhorn_knopp_backward_metal(cu(H), cu(dM), iters=iters, eps=1e-5)
+    assert rel_err(dH, dH_ref) < 1e-5
+    H_ = cu(H).requires_grad_(True)
+    M = metal.sinkhorn_knopp_metal_autograd(H_, iters=iters, eps=1e-5)
+    (dH2,) = torch.autograd.grad(M, [H_], cu(dM))
+    assert torch.equal(dH2, dH)
+
+
+# ------------------------------------------------------------ fused fwd --
+@pytest.mark.parametrize("case", G.names("forward"))
+def test_fused_forward_matches_reference(case):
+    """mhc_forward_fused_metal with the reference's activations."""
+    d = G.get(case)
+    x = x_of(d)
+    pre, post, M = cu(d["H_pre_raw"]), cu(d["H_post_raw"]), cu(d["H_res_raw"])
+    hpre, hpost = torch.sigmoid(pre), 2 * torch.sigmoid(post)
+    M = metal.sinkhorn_knopp_metal(M, iters=d["iters"], eps=d["eps"])
+    out = metal.mhc_forward_fused_metal(x, M, hpre, hpost, cu(d["rms_weight"]), eps=d["eps"])
+    assert out.dtype == torch.float32 and out.shape == x.shape
+    assert rel_err(out, d["out"]) < 1e-5, case
+
+
+@pytest.mark.parametrize("case", [c for c in G.names("forward")
+                                  if G.cases[c]["dtype"] in ("float16", "bfloat16")])
+def test_fused_forward_half_output(case):
+    d = G.get(case)
+    x = x_of(d)
+    hpre, hpost = torch.sigmoid(cu(d["H_pre_raw"])), 2 * torch.sigmoid(cu(d["H_post_raw"]))
+    M = metal.sinkhorn_knopp_metal(cu(d["H_res_raw"]), iters=d["iters"], eps=d["eps"])
+    out = metal.mhc_forward_fused_metal(x, M, hpre, hpost, cu(d["rms_weight"]), eps=d["eps"],
+                                        output_dtype=x.dtype)
+    assert out.dtype == x.dtype
+    tol = 5e-3 if x.dtype == torch.float16 else 2e-2
+    # the output rounding is relative; the reference tolerance is absolute on O(1) data
+    assert max_abs(out, d["out"]) < tol * max(1.0, float(abs(d["out"]).max())), case
+
+
+def test_identity_mapping_n4():
+    d = G.get("identity_bf16")
+    x = x_of(d)
+    layer = mhc_b200.MHCLayer(n=4, C=64).to(DEV)
+    out = layer(x)
+    assert max_abs(out, x.float()) < 1e-4
+
+
+# ---------------------------------------------------------------- layer --
+@pytest.mark.parametrize("case", G.names("layer"))
+def test_layer_forward_matches_reference(case):
+    d = G.get(case)
+    layer = mhc_b200.MHCLayer(n=d["n"], C=d["C"]).to(DEV)
+    with torch.no_grad():
+        for k in ("H_pre_raw", "H_post_raw", "H_res_raw", "rms_weight"):
+            getattr(layer, k).copy_(cu(d[k]))
+    out = layer(x_of(d))
+    assert rel_err(out, d["out"]) < 1e-5, case
+
+
+def test_layer_init_matches_reference():
+    d = G.get("layer_init_identity")
+    layer = mhc_b200.MHCLayer(n=4, C=8)
+    for k in ("H_pre_raw", "H_post_raw", "H_res_raw", "rms_weight"):
+        assert torch.equal(getattr(layer, k).detach(), torch.as_tensor(d[k]))
+
+
+def _layer_grads(x, params, d_out, iters, eps, return_dtype=None):
+    n, C = x.shape[1], x.shape[2]
+    layer = mhc_b200.MHCLayer(n=n, C=C, sinkhorn_iters=iters, eps=eps).to(DEV)
+    with torch.no_grad():
+        for k, v in zip(("H_pre_raw", "H_post_raw", "H_res_raw", "rms_weight"), params):
+            getattr(layer, k).copy_(v)
+    xg = x.detach().clone().requires_grad_(True)
+    out = layer(xg, return_dtype=return_dtype)
+    out.backward(d_out.to(out.dtype))
+    return (out.detach(), xg.grad, layer.H_pre_raw.grad, layer.H_post_raw.grad,
+            layer.H_res_raw.grad, layer.rms_weight.grad)
+
+
+GRAD_SHAPES = [(1, 4, 16, 5), (2, 4, 128, 20), (3, 4, 129, 20), (2, 1, 64, 3), (2, 2, 100, 20),
+               (2, 8, 128, 20), (2, 3, 40, 20), (2, 16, 256, 20), (1, 32, 256, 20),
+               (1, 64, 96, 20), (5, 4, 4096, 20), (4, 4, 2048, 20), (2, 8, 4096, 10)]
+
+
+@pytest.mark.parametrize("B,n,C,iters", GRAD_SHAPES)
+def test_layer_gradients_match_oracle_fp32(B, n, C, iters):
+    g = torch.Generator().manual_seed(B * 1000 + n * 10 + C)
+    x = torch.randn(B, n, C, generator=g)
+    params = [0.5 * torch.randn(n, generator=g), 0.5 * torch.randn(n, generator=g),
+              torch.randn(n, n, generator=g), 1 + 0.1 * torch.randn(C, generator=g)]
+    d_out = torch.randn(B, n, C, generator=g)
+    ref = O.layer_grads(x, *params, d_out, iters, 1e-5, dtype=F64)
+    got = _layer_grads(cu(x), [cu(p) for p in params], cu(d_out), iters, 1e-5)
+    names = ("out", "dx", "dH_pre", "dH_post", "dH_res", "d_w")
+    for name, a, b in zip(names, got, ref):
+        assert rel_err(a, b) < 1e-5, (name, rel_err(a, b))
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,n,C", [(2, 4, 128), (3, 4, 4096), (2, 16, 64), (2, 4, 129)])
+def test_layer_gradients_half_inputs(dt, B, n, C):
+    """Half x, fp32 out: the math is fp32 on exactly-representable inputs, so
+    out and the parameter grads hold the fp32 bar; dx is rounded to x's dtype."""
+    g = torch.Generator().manual_seed(7 + C)
+    x = torch.randn(B, n, C, generator=g).to(dt)
+    params = [0.5 * torch.randn(n, generator=g), 0.5 * torch.randn(n, generator=g),
+              torch.randn(n, n, generator=g), 1 + 0.1 * torch.randn(C, generator=g)]
+    d_out = torch.randn(B, n, C, generator=g)
+    ref = O.layer_grads(x, *params, d_out, 20, 1e-5, dtype=F64)
+    got = _layer_grads(cu(x, dt), [cu(p) for p in params], cu(d_out), 20, 1e-5)
+    assert got[1].dtype == dt
+    half_tol = 2e-2 if dt == torch.bfloat16 else 5e-3
+    for name, a, b in zip(("out", "dx", "dH_pre", "dH_post", "dH_res", "d_w"), got, ref):
+        tol = half_tol if name == "dx" else 1e-5
+        assert rel_err(a, b) < tol, (name, rel_err(a, b))
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_layer_half_output_gradients(dt):
+    """return_dtype = x's half dtype: the kernel writes half out; d_out arrives in half."""
+    g = torch.Generator().manual_seed(11)
+    B, n, C = 4, 4, 512
+    x = torch.randn(B, n, C, generator=g).to(dt)
+    params = [0.5 * torch.randn(n, generator=g), 0.5 * torch.randn(n, generator=g),
+              torch.randn(n, n, generator=g), 1 + 0.1 * torch.randn(C, generator=g)]
+    d_out = torch.randn(B, n, C, generator=g).to(dt)
+    ref = O.layer_grads(x, *params, d_out.float(), 20, 1e-5, dtype=F64)
+    got = _layer_grads(cu(x, dt), [cu(p) for p in params], cu(d_out, dt), 20, 1e-5,
+                       return_dtype=dt)
+    assert got[0].dtype == dt
+    tol = 2e-2 if dt == torch.bfloat16 else 5e-3
+    for name, a, b in zip(("out", "dx"), got[:2], ref[:2]):
+        assert rel_err(a, b) < tol, (name, rel_err(a, b))
+    for name, a, b in zip(("dH_pre", "dH_post", "dH_res", "d_w"), got[2:], ref[2:]):
+        assert rel_err(a, b) < 1e-5, (name, rel_err(a, b))
+
+
+def test_fused_autograd_matches_oracle():
+    """mhc_forward_fused_metal_autograd: grads w.r.t. (x, M, H_pre, H_post, w)."""
+    g = torch.Generator().manual_seed(5)
+    B, n, C = 3, 4, 256
+    x = torch.randn(B, n, C, generator=g)
+    M = O.mixing_matrix_from_logits(torch.randn(n, n, generator=g), 20, 1e-5)
+    hpre, hpost = torch.rand(n, generator=g), 2 * torch.rand(n, generator=g)
+    w = 1 + 0.1 * torch.randn(C, generator=g)
+    d_out = torch.randn(B, n, C, generator=g)
+    ref = O.fused_grads(x, M, hpre, hpost, w, d_out, 1e-5, dtype=F64)
+    leaves = [cu(t).requires_grad_(True) for t in (x, M, hpre, hpost, w)]
+    out = metal.mhc_forward_fused_metal_autograd(*leaves, eps=1e-5)
+    grads = torch.autograd.grad(out, leaves, cu(d_out))
+    assert rel_err(out, ref[0]) < 1e-5
+    for k, (a, b) in enumerate(zip(grads, ref[1:])):
+        assert rel_err(a, b) < 1e-5, (k, rel_err(a, b))
+    dx, dM, dpre, dpost, dw = metal.mhc_backward_fused_metal(*[t.detach() for t in leaves],
+                                                             cu(d_out))
+    for a, b in zip((dx, dM, dpre, dpost, dw), grads):
+        assert torch.equal(a, b)
+
+
+def test_backward_loss_matches_reference():
+    """reference tests/test_correctness.py:295-344: loss = sum(out)."""
+    d = G.get("bwd_case_f32")
+    x = x_of(d)
+    layer = mhc_b200.MHCLayer(n=4, C=16, sinkhorn_iters=5).to(DEV)
+    with torch.no_grad():
+        for k in ("H_pre_raw", "H_post_raw", "H_res_raw", "rms_weight"):
+            getattr(layer, k).copy_(cu(d[k]))
+    loss = layer(x).sum()
+    assert abs(float(loss) - float(d["out"].sum())) < 1e-4
+
+
+def test_use_metal_false_raises():
+    layer = mhc_b200.MHCLayer(n=4, C=16, use_metal=False).to(DEV)
+    with pytest.raises(RuntimeError):
+        layer(torch.randn(1, 4, 16, device=DEV))
+
+
+def test_generic_path_matches_fast_path():
+    """MHC_B200_GENERIC=1 forces the any-n kernels; results agree with the
+    specialised ones to fp32 rounding."""
+    g = torch.Generator().manual_seed(9)
+    B, n, C = 6, 4, 1024
+    x, d_out = cu(torch.randn(B, n, C, generator=g)), cu(torch.randn(B, n, C, generator=g))
+    params = [cu(0.5 * torch.randn(n, generator=g)), cu(0.5 * torch.randn(n, generator=g)),
+              cu(torch.randn(n, n, generator=g)), cu(1 + 0.1 * torch.randn(C, generator=g))]
+    fast = _layer_grads(x, params, d_out, 20, 1e-5)
+    os.environ["MHC_B200_GENERIC"] = "1"
+    try:
+        gen = _layer_grads(x, params, d_out, 20, 1e-5)
+    finally:
+        del os.environ["MHC_B200_GENERIC"]
+    for a, b in zip(fast, gen):
+        assert rel_err(a, b) < 1e-5
