@@ -100,6 +100,26 @@ __device__ __forceinline__ void store_vec(T* __restrict__ p, const float (&v)[V]
   }
 }
 
+// ------------------------------------------------ async global->shared copy --
+// 16-byte cp.async (L2 only).  Used to prefetch the next token row into
+// thread-private shared-memory slots while the current row is processed;
+// completion is awaited with cp.async.wait_all (a hardware wait, no spin).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+// Unpack one 16-byte chunk holding V elements of T into fp32.
+template <typename T, int V>
+__device__ __forceinline__ void unpack16(const uint4& u, float (&o)[V]) {
+  static_assert(V * sizeof(T) == 16, "one 16-byte chunk");
+  const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int k = 0; k < V; ++k) o[k] = to_f(h[k]);
+}
+
 // Plain fp32 vector load for parameter vectors (w) of width V.
 template <int V>
 __device__ __forceinline__ void load_f32(const float* __restrict__ p, float (&o)[V]) {

@@ -24,11 +24,15 @@
 namespace mhc {
 
 // ===================================================================== fwd ==
-template <int N, typename InT, typename OutT, int VEC, int ITEMS, int MAXT>
+// PIPE: the next token's x is prefetched with cp.async into thread-private
+// shared-memory slots once the current token's values are in registers.
+template <int N, typename InT, typename OutT, int VEC, int ITEMS, int MAXT, bool PIPE>
 __global__ void __launch_bounds__(MAXT)
 k_fwd_fast(const InT* __restrict__ x, const float* __restrict__ Mg,
            const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
            const float* __restrict__ w, OutT* __restrict__ out, int64_t T, int C, float eps) {
+  static_assert(!PIPE || VEC * sizeof(InT) == 16, "16-byte chunks");
+  extern __shared__ uint4 s_stage[];
   constexpr bool kMReg = N <= 8;
   __shared__ float sM[N * N];
   __shared__ float red[2][32];
@@ -59,18 +63,37 @@ k_fwd_fast(const InT* __restrict__ x, const float* __restrict__ Mg,
   }
 
   const int64_t rs = (int64_t)N * C;
+  auto slot = [&](int it, int i) -> uint4* {
+    return s_stage + (it * N + i) * blockDim.x + threadIdx.x;
+  };
+  auto prefetch = [&](int64_t tp) {
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it) {
+      if (!ok[it]) continue;
+#pragma unroll
+      for (int i = 0; i < N; ++i) cp_async16(slot(it, i), x + tp * rs + (int64_t)i * C + col[it]);
+    }
+    cp_async_commit();
+  };
+  if constexpr (PIPE) {
+    if ((int64_t)blockIdx.x < T) prefetch(blockIdx.x);
+  }
   int par = 0;
   for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
     const InT* xt = x + t * rs;
     float xr[ITEMS][N][VEC];
+    if constexpr (PIPE) cp_async_wait_all();
 #pragma unroll
     for (int it = 0; it < ITEMS; ++it)
 #pragma unroll
       for (int i = 0; i < N; ++i) {
-        if (ok[it]) load_vec<InT, VEC>(xt + (int64_t)i * C + col[it], xr[it][i]);
-        else
+        if (ok[it]) {
+          if constexpr (PIPE) unpack16<InT, VEC>(*slot(it, i), xr[it][i]);
+          else load_vec<InT, VEC>(xt + (int64_t)i * C + col[it], xr[it][i]);
+        } else {
 #pragma unroll
           for (int v = 0; v < VEC; ++v) xr[it][i][v] = 0.f;
+        }
       }
     float y[ITEMS][VEC];
     float ss = 0.f;
@@ -84,6 +107,10 @@ k_fwd_fast(const InT* __restrict__ x, const float* __restrict__ Mg,
         y[it][v] = a;
         ss = fmaf(a, a, ss);
       }
+    // the staged chunks are all in registers now: refill with the next token
+    if constexpr (PIPE) {
+      if (t + gridDim.x < T) prefetch(t + gridDim.x);
+    }
     ss = block_sum(ss, red[par]);
     par ^= 1;
     const float inv = inv_rms(ss, C, eps);
@@ -169,12 +196,19 @@ k_fwd_generic(const InT* __restrict__ x, const float* __restrict__ Mg,
 // Accumulated over tokens and columns (per CTA, then finalize):
 //   dM_ij += d_i x_j, dHpre_j += dya x_j, dHpost_i += d_i (y inv w),
 //   dw_c += dyn (y inv)
-template <int N, typename XT, typename DT, typename DXT, int VEC, int ITEMS, int MAXT>
+//
+// PIPE: the next token's x and d_out chunks are prefetched with cp.async into
+// thread-private shared-memory slots (one 16-byte chunk per (item, stream))
+// as soon as the current token's values have been consumed by the first
+// pass, so HBM keeps streaming while the CTA reduces, computes and stores.
+template <int N, typename XT, typename DT, typename DXT, int VEC, int ITEMS, int MAXT, bool PIPE>
 __global__ void __launch_bounds__(MAXT)
 k_bwd_fast(const XT* __restrict__ x, const DT* __restrict__ dout, const float* __restrict__ Mg,
            const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
            const float* __restrict__ w, DXT* __restrict__ dx, int64_t T, int C, float eps,
            float* __restrict__ ws_p, float* __restrict__ ws_c, int* __restrict__ ws_hdr) {
+  static_assert(!PIPE || (VEC * sizeof(XT) == 16 && VEC * sizeof(DT) == 16), "16-byte chunks");
+  extern __shared__ uint4 s_stage[];
   constexpr int P = N * N + 2 * N;
   __shared__ float sM[N * N];
   __shared__ float red[2][64];
@@ -206,18 +240,43 @@ k_bwd_fast(const XT* __restrict__ x, const DT* __restrict__ dout, const float* _
 
   const int64_t rs = (int64_t)N * C;
   const float invC = 1.0f / (float)C;
+  // slot(kind, it, i): kind 0 = x, 1 = d_out; thread index fastest
+  auto slot = [&](int kind, int it, int i) -> uint4* {
+    return s_stage + ((kind * ITEMS + it) * N + i) * blockDim.x + threadIdx.x;
+  };
+  auto prefetch = [&](int64_t tp) {
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it) {
+      if (!ok[it]) continue;
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        cp_async16(slot(0, it, i), x + tp * rs + (int64_t)i * C + col[it]);
+        cp_async16(slot(1, it, i), dout + tp * rs + (int64_t)i * C + col[it]);
+      }
+    }
+    cp_async_commit();
+  };
+  if constexpr (PIPE) {
+    if ((int64_t)blockIdx.x < T) prefetch(blockIdx.x);
+  }
   int par = 0;
   for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
     const XT* xt = x + t * rs;
     const DT* dt = dout + t * rs;
     float xr[ITEMS][N][VEC], dr[ITEMS][N][VEC];
+    if constexpr (PIPE) cp_async_wait_all();
 #pragma unroll
     for (int it = 0; it < ITEMS; ++it)
 #pragma unroll
       for (int i = 0; i < N; ++i) {
         if (ok[it]) {
-          load_vec<XT, VEC>(xt + (int64_t)i * C + col[it], xr[it][i]);
-          load_vec<DT, VEC>(dt + (int64_t)i * C + col[it], dr[it][i]);
+          if constexpr (PIPE) {
+            unpack16<XT, VEC>(*slot(0, it, i), xr[it][i]);
+            unpack16<DT, VEC>(*slot(1, it, i), dr[it][i]);
+          } else {
+            load_vec<XT, VEC>(xt + (int64_t)i * C + col[it], xr[it][i]);
+            load_vec<DT, VEC>(dt + (int64_t)i * C + col[it], dr[it][i]);
+          }
         } else {
 #pragma unroll
           for (int v = 0; v < VEC; ++v) { xr[it][i][v] = 0.f; dr[it][i][v] = 0.f; }
@@ -242,6 +301,11 @@ k_bwd_fast(const XT* __restrict__ x, const DT* __restrict__ dout, const float* _
         ss = fmaf(y, y, ss);
         pd = fmaf(dyn * wv[v], y, pd);
       }
+    }
+    // every staged value has been consumed above: refill the slots with the
+    // next token while this one is reduced, computed and stored
+    if constexpr (PIPE) {
+      if (t + gridDim.x < T) prefetch(t + gridDim.x);
     }
     const float2 red2 = block_sum2(ss, pd, red[par]);
     par ^= 1;
@@ -560,7 +624,22 @@ static int try_fwd_items(const InT* x, const float* M, const float* hpre, const 
     const int groups = (C + VEC - 1) / VEC;
     const int threads = round32((groups + ITEMS - 1) / ITEMS);
     if (threads > MAXT) return -1;
-    auto kern = k_fwd_fast<N, InT, OutT, VEC, ITEMS, MAXT>;
+    const size_t smem = (size_t)ITEMS * N * 16 * threads;
+    // Measured on B200 (n=4, C=4096, 64K tokens): staging the next row helps
+    // 16-bit inputs (715 -> 685 us) and costs fp32 inputs (1380 -> 1438 us),
+    // whose two resident CTAs per SM already overlap load and store phases.
+    if constexpr (VEC * sizeof(InT) == 16 && sizeof(InT) == 2) {
+      if (env_int("MHC_B200_PIPE", 1) && smem <= (size_t)max_smem_optin()) {
+        auto kern = k_fwd_fast<N, InT, OutT, VEC, ITEMS, MAXT, true>;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_fwd: %s", cudaGetErrorString(e));
+        const int grid = persistent_grid(kern, threads, smem, T, 1 << 30);
+        kern<<<grid, threads, smem, st>>>(x, M, hpre, hpost, w, out, T, C, eps);
+        return check_launch("mhc_fwd");
+      }
+    }
+    auto kern = k_fwd_fast<N, InT, OutT, VEC, ITEMS, MAXT, false>;
     const int grid = persistent_grid(kern, threads, 0, T, 1 << 30);
     kern<<<grid, threads, 0, st>>>(x, M, hpre, hpost, w, out, T, C, eps);
     return check_launch("mhc_fwd");
@@ -686,7 +765,21 @@ static int try_bwd_items(const XT* x, const DT* d, const float* M, const float* 
     const int groups = (C + VEC - 1) / VEC;
     const int threads = round32((groups + ITEMS - 1) / ITEMS);
     if (threads > MAXT) return -1;
-    auto kern = k_bwd_fast<N, XT, DT, DXT, VEC, ITEMS, MAXT>;
+    constexpr bool kCanPipe = VEC * sizeof(XT) == 16 && VEC * sizeof(DT) == 16;
+    const size_t smem = (size_t)2 * ITEMS * N * 16 * threads;
+    if constexpr (kCanPipe) {
+      if (env_int("MHC_B200_PIPE", 1) && smem <= (size_t)max_smem_optin()) {
+        auto kern = k_bwd_fast<N, XT, DT, DXT, VEC, ITEMS, MAXT, true>;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_bwd: %s", cudaGetErrorString(e));
+        const int G = persistent_grid(kern, threads, smem, T, max_partial_rows(T));
+        BwdPtrs p = ws_ptrs(ws, G, N);
+        kern<<<G, threads, smem, st>>>(x, d, M, hpre, hpost, w, dx, T, C, eps, p.p, p.c, p.hdr);
+        return check_launch("mhc_bwd");
+      }
+    }
+    auto kern = k_bwd_fast<N, XT, DT, DXT, VEC, ITEMS, MAXT, false>;
     const int G = persistent_grid(kern, threads, 0, T, max_partial_rows(T));
     BwdPtrs p = ws_ptrs(ws, G, N);
     kern<<<G, threads, 0, st>>>(x, d, M, hpre, hpost, w, dx, T, C, eps, p.p, p.c, p.hdr);

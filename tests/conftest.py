@@ -80,3 +80,22 @@ def max_abs(a, b) -> float:
     import torch
 
     return float((torch.as_tensor(a).double().cpu() - torch.as_tensor(b).double().cpu()).abs().max())
+
+
+def assert_close_to_reference(name, got, ref64, ref32, rel=1e-5, noise_factor=4.0):
+    """got must match the float64 oracle within `rel` of max|ref|, or be no
+    further from it than `noise_factor` times the reference algorithm's own
+    float32 rounding error (|ref32 - ref64|).  The second branch covers
+    quantities that are small differences of large terms (e.g. dH_pre at
+    n = 1, where RMSNorm cancels the H_pre scale analytically)."""
+    e = max_abs(got, ref64)
+    scale = max(float(torch_abs_max(ref64)), 1e-30)
+    e32 = max_abs(ref32, ref64)
+    assert e <= rel * scale or e <= noise_factor * e32 + 1e-12, (
+        f"{name}: err {e:.3e}, rel {e / scale:.3e}, fp32-oracle err {e32:.3e}")
+
+
+def torch_abs_max(t):
+    import torch
+
+    return torch.as_tensor(t).double().abs().max()

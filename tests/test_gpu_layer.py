@@ -16,7 +16,7 @@ import pytest
 import torch
 
 import mhc_b200
-from conftest import golden, max_abs, rel_err
+from conftest import assert_close_to_reference, golden, max_abs, rel_err
 from mhc_b200 import metal
 from oracle import mhc_oracle as O
 
@@ -148,10 +148,11 @@ def test_layer_gradients_match_oracle_fp32(B, n, C, iters):
               torch.randn(n, n, generator=g), 1 + 0.1 * torch.randn(C, generator=g)]
     d_out = torch.randn(B, n, C, generator=g)
     ref = O.layer_grads(x, *params, d_out, iters, 1e-5, dtype=F64)
+    ref32 = O.layer_grads(x, *params, d_out, iters, 1e-5, dtype=torch.float32)
     got = _layer_grads(cu(x), [cu(p) for p in params], cu(d_out), iters, 1e-5)
     names = ("out", "dx", "dH_pre", "dH_post", "dH_res", "d_w")
-    for name, a, b in zip(names, got, ref):
-        assert rel_err(a, b) < 1e-5, (name, rel_err(a, b))
+    for name, a, b, b32 in zip(names, got, ref, ref32):
+        assert_close_to_reference(name, a, b, b32)
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
