@@ -208,3 +208,13 @@ def test_quantized_linear_roundtrip(bits):
     x = torch.randn(3, 256, dtype=torch.float16)
     y = q(x)
     assert y.shape == (3, 128)
+
+
+def test_reference_import_names():
+    """test_packaging.py analogue: the reference's import names resolve."""
+    import mhc_mlx
+    import mlx_mhc
+    from mhc_mlx.metal import mhc_forward_fused_metal, sinkhorn_knopp_metal  # noqa: F401
+
+    assert mlx_mhc.__version__ == mhc_mlx.__version__ == mhc_b200.__version__
+    assert mlx_mhc.MHCLayer is MHCLayer and mhc_mlx.metal is metal
