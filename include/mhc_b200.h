@@ -12,7 +12,8 @@
  *   - Every function returns 0 on success, a nonzero MHC_ERR_* code otherwise;
  *     mhc_last_error() returns a thread-local message for the last failure.
  *   - The caller owns every buffer, including workspaces; the library keeps no
- *     device allocation between calls.  All work is enqueued on `stream`
+ *     device allocation between calls, except the fixed scratch array that
+ *     mhc_bwd_noalloc uses.  All work is enqueued on `stream`
  *     (a cudaStream_t passed as void*; NULL = legacy default stream) and no
  *     call synchronises the host.
  *   - Tensors are row-contiguous.  x / out / dx are [T, n, C] (T = tokens,
@@ -133,6 +134,27 @@ MHC_API int mhc_bwd_finalize(const void* workspace, int n, int C, float* dM,
                      const float* H_res_raw, const float* tape, int iters,
                      float eps, float* dH_pre_raw, float* dH_post_raw,
                      float* dH_res_raw, void* stream);
+
+/* ---- fused layer backward without caller-provided memory ------------------
+ * No counterpart in the reference.  Same result as mhc_bwd followed by
+ * mhc_bwd_finalize (activated-parameter gradients), for callers that cannot
+ * allocate device memory: a plugin boundary that hands a kernel only its
+ * inputs and outputs (as the reference's mx.fast.metal_kernel boundary
+ * does), or a runtime whose allocator may not be called on this path.
+ * The per-block partial sums live in one file-scope device array of
+ * MHC_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps until
+ * process exit; the call allocates nothing.  It fails with MHC_ERR_WORKSPACE
+ * when mhc_bwd_workspace_bytes(T, n, C) exceeds that size (on a 148-SM B200:
+ * n = 4 fits any T up to C = 7,060).  The first call on a device looks up
+ * the array's device address (once per device): make it before any stream
+ * capture.  All calls share the array, so calls that overlap on the GPU
+ * (different streams, or several host threads) race: serialise them. */
+#define MHC_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+MHC_API int mhc_bwd_noalloc(const void* x, int x_dtype, const void* d_out, int dout_dtype,
+                            const float* M, const float* H_pre_act, const float* H_post_act,
+                            const float* rms_weight, void* dx, int dx_dtype, float* dM,
+                            float* dH_pre_act, float* dH_post_act, float* d_rms_weight,
+                            int64_t T, int n, int C, float eps, void* stream);
 
 /* ---- stream mix + add (MHCRewire post-combine) ---------------------------
  * Replaces metal.py:954 stream_mix_add_metal (kernel stream_mix_add.metal):

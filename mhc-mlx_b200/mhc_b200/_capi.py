@@ -39,6 +39,8 @@ SIGNATURES: dict[str, tuple] = {
                         c_float, _P, c_size_t, _P]),
     "mhc_bwd_finalize": (c_int, [_P, c_int, c_int, _P, _P, _P, _P, _P, _P, _P, _P, c_int, c_float,
                                  _P, _P, _P, _P]),
+    "mhc_bwd_noalloc": (c_int, [_P, c_int, _P, c_int, _P, _P, _P, _P, _P, c_int, _P, _P, _P, _P,
+                                c_int64, c_int, c_int, c_float, _P]),
     "mhc_mix_add_fwd": (c_int, [_P, c_int, _P, _P, c_int, _P, c_int, c_int64, c_int, c_int, _P]),
     "mhc_mix_bwd_workspace_bytes": (c_size_t, [c_int64, c_int, c_int]),
     "mhc_mix_add_bwd": (c_int, [_P, c_int, _P, _P, c_int, _P, c_int, _P, c_int64, c_int, c_int, _P,
