@@ -342,7 +342,24 @@ def latency_b1(layer, n, C, dev, iters=1000):
             p.grad = None
         layer(x).backward(d)
 
-    return {"fwd": measure(fwd), "fwd_bwd": measure(fwd_bwd)}
+    res = {"fwd": measure(fwd), "fwd_bwd": measure(fwd_bwd)}
+    # the same fwd+bwd captured once in a CUDA graph and replayed: the
+    # device-side latency of the four kernels without per-call host work
+    try:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(st)
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fwd_bwd()
+        st.wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fwd_bwd()
+        res["fwd_bwd_graph"] = measure(graph.replay)
+        res["fwd_bwd_graph"]["kernels_per_replay"] = 4
+    except Exception as e:  # report, never hide: the eager numbers stand
+        res["fwd_bwd_graph"] = {"error": f"{type(e).__name__}: {e}"[:200]}
+    return res
 
 
 def traffic_from_profile(name):

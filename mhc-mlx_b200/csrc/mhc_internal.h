@@ -22,6 +22,15 @@ int max_smem_optin();
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Allow `dyn` bytes of dynamic shared memory for `kernel`.  Needed whenever
+// static + dynamic shared memory exceeds the 48 KB default, so it is set for
+// every launch that uses dynamic shared memory.
+template <typename K>
+inline cudaError_t allow_dyn_smem(K kernel, size_t dyn) {
+  if (dyn == 0) return cudaSuccess;
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+}
+
 inline int dtype_size(int dt) { return dt == MHC_F32 ? 4 : 2; }
 inline bool dtype_ok(int dt) { return dt == MHC_F32 || dt == MHC_F16 || dt == MHC_BF16; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

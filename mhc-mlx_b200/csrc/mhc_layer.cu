@@ -522,11 +522,23 @@ k_bwd_generic(const XT* __restrict__ x, const DT* __restrict__ dout, const float
 }
 
 // ================================================================ finalize ==
-// Blocks [0, nbc) reduce d_rms_weight columns; the last block reduces the
-// n*n + 2n parameter partials and optionally runs the parameter chain
-// (Sinkhorn backward + sigmoid derivatives).  Summation is sequential over
-// partial rows: deterministic for a given partial count.
+// Blocks [0, nbc) reduce d_rms_weight, 32 columns per block: thread
+// (slice r, column c) sums partial rows r, r + 8, r + 16, ... and the 8
+// slice sums are added in slice order -- a fixed order for a given row count,
+// with 8x fewer dependent loads per thread than a plain column walk.  The
+// last block reduces the n*n + 2n parameter partials the same way and
+// optionally runs the parameter chain (Sinkhorn backward from a staged tape
+// + sigmoid derivatives).
 constexpr int kFinBD = 256;
+constexpr int kFinSlices = kFinBD / 32;
+
+__device__ __forceinline__ float sliced_row_sum(const float* __restrict__ base, size_t stride,
+                                                int G, int r0) {
+  float s = 0.f;
+#pragma unroll 4
+  for (int g = r0; g < G; g += kFinSlices) s += base[(size_t)g * stride];
+  return s;
+}
 
 __global__ void __launch_bounds__(kFinBD)
 k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
@@ -534,33 +546,44 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
            const float* __restrict__ hpre_raw, const float* __restrict__ hpost_raw,
            const float* __restrict__ hres_raw, const float* __restrict__ tape, int iters,
            float eps, float* __restrict__ dhpre_raw, float* __restrict__ dhpost_raw,
-           float* __restrict__ dhres_raw) {
+           float* __restrict__ dhres_raw, int stage_sk) {
   const int G = *reinterpret_cast<const int*>(ws);
   const int P = n * n + 2 * n;
   const float* wp = reinterpret_cast<const float*>(ws + WsLayout::params_off());
   const float* wc = reinterpret_cast<const float*>(ws + WsLayout::cols_off(G, n));
-  const int nbc = (C + kFinBD - 1) / kFinBD;
+  const int nbc = (C + 31) / 32;
+  const int tid = threadIdx.x, lane = tid & 31, r0 = tid >> 5;
+  __shared__ float part[kFinSlices][32];
   if ((int)blockIdx.x < nbc) {
-    const int c = blockIdx.x * kFinBD + threadIdx.x;
-    if (c < C && dw) {
+    const int c = blockIdx.x * 32 + lane;
+    part[r0][lane] = (c < C) ? sliced_row_sum(wc + c, C, G, r0) : 0.f;
+    __syncthreads();
+    if (r0 == 0 && c < C && dw) {
       float s = 0.f;
-      for (int g = 0; g < G; ++g) s += wc[(size_t)g * C + c];
+#pragma unroll
+      for (int q = 0; q < kFinSlices; ++q) s += part[q][lane];
       dw[c] = s;
     }
     return;
   }
   __shared__ float sP[kMaxN * kMaxN + 2 * kMaxN];
   __shared__ float D[kMaxN * (kMaxN + 1)];
-  for (int e = threadIdx.x; e < P; e += kFinBD) {
-    float s = 0.f;
-    for (int g = 0; g < G; ++g) s += wp[(size_t)g * P + e];
-    sP[e] = s;
-    if (e < n * n) { if (dM) dM[e] = s; }
-    else if (e < n * n + n) { if (dhpre) dhpre[e - n * n] = s; }
-    else if (dhpost) dhpost[e - n * n - n] = s;
+  extern __shared__ float s_fin[];  // optional staged copy of tape + logits
+  for (int e0 = 0; e0 < P; e0 += 32) {
+    const int e = e0 + lane;
+    part[r0][lane] = (e < P) ? sliced_row_sum(wp + e, P, G, r0) : 0.f;
+    __syncthreads();
+    if (r0 == 0 && e < P) {
+      float s = 0.f;
+#pragma unroll
+      for (int q = 0; q < kFinSlices; ++q) s += part[q][lane];
+      sP[e] = s;
+      if (e < n * n) { if (dM) dM[e] = s; }
+      else if (e < n * n + n) { if (dhpre) dhpre[e - n * n] = s; }
+      else if (dhpost) dhpost[e - n * n - n] = s;
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  const int tid = threadIdx.x;
   if (tid < n) {
     if (hpre_raw && dhpre_raw) {
       const float s = sigmoidf_(hpre_raw[tid]);
@@ -572,10 +595,33 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
     }
   }
   if (hres_raw && dhres_raw && (tape || iters == 0)) {
+    const float* Hs = hres_raw;
+    const float* Ts = tape;
+    if (stage_sk) {  // dynamic shared memory holds [tape | logits]
+      const size_t tf = (size_t)iters * sk_tape_stride(n);
+      for (size_t e = tid; e < tf; e += kFinBD) s_fin[e] = tape[e];
+      for (int e = tid; e < n * n; e += kFinBD) s_fin[tf + e] = hres_raw[e];
+      Ts = s_fin;
+      Hs = s_fin + tf;
+    }
+    __syncthreads();
+    if (sk_warp_ok(n)) {
+      if (tid < 32) {
+        const int row = tid % n;
+        MHC_SK_WARP_SWITCH(n, ({
+          float d[SK_N];
+          for (int j = 0; j < SK_N; ++j) d[j] = sP[row * SK_N + j];
+          sk_backward_warp<SK_N>(Hs, Ts, iters, eps, d);
+          if (tid < SK_N)
+            for (int j = 0; j < SK_N; ++j) dhres_raw[row * SK_N + j] = d[j];
+        }))
+      }
+      return;
+    }
     const int ld = sk_ld(n);
     for (int e = tid; e < n * n; e += kFinBD) D[(e / n) * ld + e % n] = sP[e];
     __syncthreads();
-    sk_backward_block(hres_raw, tape, n, iters, eps, D, dhres_raw);
+    sk_backward_block(Hs, Ts, n, iters, eps, D, dhres_raw);
   }
 }
 
@@ -631,8 +677,7 @@ static int try_fwd_items(const InT* x, const float* M, const float* hpre, const 
     if constexpr (VEC * sizeof(InT) == 16 && sizeof(InT) == 2) {
       if (env_int("MHC_B200_PIPE", 1) && smem <= (size_t)max_smem_optin()) {
         auto kern = k_fwd_fast<N, InT, OutT, VEC, ITEMS, MAXT, true>;
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
+        cudaError_t e = allow_dyn_smem(kern, smem);
         if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_fwd: %s", cudaGetErrorString(e));
         const int grid = persistent_grid(kern, threads, smem, T, 1 << 30);
         kern<<<grid, threads, smem, st>>>(x, M, hpre, hpost, w, out, T, C, eps);
@@ -767,23 +812,19 @@ static int try_bwd_items(const XT* x, const DT* d, const float* M, const float* 
     if (threads > MAXT) return -1;
     constexpr bool kCanPipe = VEC * sizeof(XT) == 16 && VEC * sizeof(DT) == 16;
     const size_t smem = (size_t)2 * ITEMS * N * 16 * threads;
+    const bool pipe = kCanPipe && env_int("MHC_B200_PIPE", 1) && smem <= (size_t)max_smem_optin();
+    auto launch = [&](auto kern, size_t dyn) -> int {
+      cudaError_t e = allow_dyn_smem(kern, dyn);
+      if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_bwd: %s", cudaGetErrorString(e));
+      const int G = persistent_grid(kern, threads, dyn, T, max_partial_rows(T));
+      BwdPtrs p = ws_ptrs(ws, G, N);
+      kern<<<G, threads, dyn, st>>>(x, d, M, hpre, hpost, w, dx, T, C, eps, p.p, p.c, p.hdr);
+      return check_launch("mhc_bwd");
+    };
     if constexpr (kCanPipe) {
-      if (env_int("MHC_B200_PIPE", 1) && smem <= (size_t)max_smem_optin()) {
-        auto kern = k_bwd_fast<N, XT, DT, DXT, VEC, ITEMS, MAXT, true>;
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_bwd: %s", cudaGetErrorString(e));
-        const int G = persistent_grid(kern, threads, smem, T, max_partial_rows(T));
-        BwdPtrs p = ws_ptrs(ws, G, N);
-        kern<<<G, threads, smem, st>>>(x, d, M, hpre, hpost, w, dx, T, C, eps, p.p, p.c, p.hdr);
-        return check_launch("mhc_bwd");
-      }
+      if (pipe) return launch(k_bwd_fast<N, XT, DT, DXT, VEC, ITEMS, MAXT, true>, smem);
     }
-    auto kern = k_bwd_fast<N, XT, DT, DXT, VEC, ITEMS, MAXT, false>;
-    const int G = persistent_grid(kern, threads, 0, T, max_partial_rows(T));
-    BwdPtrs p = ws_ptrs(ws, G, N);
-    kern<<<G, threads, 0, st>>>(x, d, M, hpre, hpost, w, dx, T, C, eps, p.p, p.c, p.hdr);
-    return check_launch("mhc_bwd");
+    return launch(k_bwd_fast<N, XT, DT, DXT, VEC, ITEMS, MAXT, false>, 0);
   }
 }
 
@@ -849,8 +890,8 @@ static int bwd_typed(const void* xv, const void* dv, const float* M, const float
   const int na = n + 1;
   const size_t smem = ((size_t)n * n + 2 * n + 2 * (size_t)na * kGenLD) * sizeof(float);
   auto kern = k_bwd_generic<XT, DT, DXT>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    cudaError_t e = allow_dyn_smem(kern, smem);
     if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_bwd(generic): %s", cudaGetErrorString(e));
   }
   const int G = persistent_grid(kern, kGenBD, smem, T, max_partial_rows(T));
@@ -886,10 +927,17 @@ int launch_finalize(const void* ws, int n, int C, float* dM, float* dhpre, float
                     float* dw, const float* hpre_raw, const float* hpost_raw,
                     const float* hres_raw, const float* tape, int iters, float eps,
                     float* dhpre_raw, float* dhpost_raw, float* dhres_raw, cudaStream_t st) {
-  const int nbc = (C + kFinBD - 1) / kFinBD;
-  k_finalize<<<nbc + 1, kFinBD, 0, st>>>(static_cast<const char*>(ws), n, C, dM, dhpre, dhpost,
-                                          dw, hpre_raw, hpost_raw, hres_raw, tape, iters, eps,
-                                          dhpre_raw, dhpost_raw, dhres_raw);
+  const int nbc = (C + 31) / 32;
+  // Stage the Sinkhorn tape and logits in shared memory when they fit.
+  size_t smem = 0;
+  if (hres_raw && dhres_raw && tape) {
+    const size_t b = ((size_t)iters * sk_tape_stride(n) + (size_t)n * n) * sizeof(float);
+    if (b <= 160 * 1024) smem = b;
+  }
+  if (allow_dyn_smem(k_finalize, smem) != cudaSuccess) smem = 0;
+  k_finalize<<<nbc + 1, kFinBD, smem, st>>>(static_cast<const char*>(ws), n, C, dM, dhpre, dhpost,
+                                            dw, hpre_raw, hpost_raw, hres_raw, tape, iters, eps,
+                                            dhpre_raw, dhpost_raw, dhres_raw, smem > 0);
   return check_launch("mhc_bwd_finalize");
 }
 

@@ -573,8 +573,8 @@ static int combine_bwd_t(const void* xv, const void* yv, const void* dv, const f
 #undef MHC_CB
   const size_t smem = mix_gen_smem(n);
   auto kern = k_combine_bwd_generic<XT, YT, DT, DXT, DYT>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    cudaError_t e = allow_dyn_smem(kern, smem);
     if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "combine_bwd: %s", cudaGetErrorString(e));
   }
   const int64_t ntile = T * ((C + kMixGenBD - 1) / kMixGenBD);

@@ -24,7 +24,12 @@ k_params_fwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost
     if (hpre_raw) hpre[tid] = sigmoidf_(hpre_raw[tid]);
     if (hpost_raw) hpost[tid] = 2.0f * sigmoidf_(hpost_raw[tid]);
   }
-  if (hres_raw) sk_forward_block(hres_raw, n, iters, eps, P, tape, M);
+  if (!hres_raw) return;
+  if (sk_warp_ok(n)) {
+    if (threadIdx.x < 32) MHC_SK_WARP_SWITCH(n, (sk_forward_warp<SK_N>(hres_raw, iters, eps, tape, M)))
+    return;
+  }
+  sk_forward_block(hres_raw, n, iters, eps, P, tape, M);
 }
 
 __global__ void __launch_bounds__(256)
@@ -33,8 +38,9 @@ k_params_bwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost
              int iters, float eps, const float* __restrict__ dhpre,
              const float* __restrict__ dhpost, const float* __restrict__ dM,
              float* __restrict__ dhpre_raw, float* __restrict__ dhpost_raw,
-             float* __restrict__ dhres_raw) {
+             float* __restrict__ dhres_raw, int stage) {
   __shared__ float D[kMaxN * (kMaxN + 1)];
+  extern __shared__ float s_stage_sk[];  // optional [tape | logits]
   const int tid = threadIdx.x, ld = sk_ld(n);
   if (tid < n) {
     // d/da sigmoid(a) = s (1 - s); H_post_act = 2 sigmoid(b)
@@ -48,9 +54,32 @@ k_params_bwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost
     }
   }
   if (hres_raw && dM) {
+    const float* Hs = hres_raw;
+    const float* Ts = tape;
+    if (stage) {
+      const size_t tf = (size_t)iters * sk_tape_stride(n);
+      for (size_t e = tid; e < tf; e += blockDim.x) s_stage_sk[e] = tape[e];
+      for (int e = tid; e < n * n; e += blockDim.x) s_stage_sk[tf + e] = hres_raw[e];
+      Ts = s_stage_sk;
+      Hs = s_stage_sk + tf;
+    }
+    if (sk_warp_ok(n)) {
+      __syncthreads();
+      if (threadIdx.x < 32) {
+        const int row = threadIdx.x % n;
+        MHC_SK_WARP_SWITCH(n, ({
+          float d[SK_N];
+          for (int j = 0; j < SK_N; ++j) d[j] = dM[row * SK_N + j];
+          sk_backward_warp<SK_N>(Hs, Ts, iters, eps, d);
+          if (threadIdx.x < SK_N)
+            for (int j = 0; j < SK_N; ++j) dhres_raw[row * SK_N + j] = d[j];
+        }))
+      }
+      return;
+    }
     for (int e = tid; e < n * n; e += blockDim.x) D[(e / n) * ld + e % n] = dM[e];
     __syncthreads();
-    sk_backward_block(hres_raw, tape, n, iters, eps, D, dhres_raw);
+    sk_backward_block(Hs, Ts, n, iters, eps, D, dhres_raw);
   }
 }
 
@@ -68,8 +97,15 @@ int launch_params_bwd(const float* hpre_raw, const float* hpost_raw, const float
                       const float* dhpost, const float* dM, float* dhpre_raw,
                       float* dhpost_raw, float* dhres_raw, cudaStream_t st) {
   const int threads = n <= 32 ? 32 : 64;
-  k_params_bwd<<<1, threads, 0, st>>>(hpre_raw, hpost_raw, hres_raw, tape, n, iters, eps,
-                                      dhpre, dhpost, dM, dhpre_raw, dhpost_raw, dhres_raw);
+  size_t smem = 0;
+  if (hres_raw && dM && tape) {
+    const size_t b = ((size_t)iters * sk_tape_stride(n) + (size_t)n * n) * sizeof(float);
+    if (b <= 160 * 1024) smem = b;
+  }
+  if (allow_dyn_smem(k_params_bwd, smem) != cudaSuccess) smem = 0;
+  k_params_bwd<<<1, threads, smem, st>>>(hpre_raw, hpost_raw, hres_raw, tape, n, iters, eps,
+                                         dhpre, dhpost, dM, dhpre_raw, dhpost_raw, dhres_raw,
+                                         smem > 0);
   return check_launch("params_bwd");
 }
 
@@ -276,9 +312,8 @@ static int sk_bwd_small(const float* H, const float* dM, int64_t batch, int iter
                         float* dH, cudaStream_t st) {
   const int threads = sk_bwd_threads(N, iters);
   const size_t smem = (size_t)iters * (N + 2) * threads * sizeof(float);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(k_sk_batched_bwd<N>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    cudaError_t e = allow_dyn_smem(k_sk_batched_bwd<N>, smem);
     if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "sinkhorn_batched_bwd: %s", cudaGetErrorString(e));
   }
   const int64_t blocks = (batch * N + threads - 1) / threads;

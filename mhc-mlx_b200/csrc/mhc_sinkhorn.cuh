@@ -27,10 +27,13 @@ __device__ inline void sk_forward_block(const float* __restrict__ H, int n, int 
                                         float* P, float* __restrict__ tape,
                                         float* __restrict__ M) {
   const int tid = threadIdx.x, bd = blockDim.x, ld = sk_ld(n), nn = n * n;
+  // stage the logits with one coalesced pass, then shift by the row max and exp
+  for (int e = tid; e < nn; e += bd) P[(e / n) * ld + e % n] = H[e];
+  __syncthreads();
   for (int i = tid; i < n; i += bd) {
-    float m = H[i * n];
-    for (int j = 1; j < n; ++j) m = fmaxf(m, H[i * n + j]);
-    for (int j = 0; j < n; ++j) P[i * ld + j] = expf(H[i * n + j] - m);
+    float m = P[i * ld];
+    for (int j = 1; j < n; ++j) m = fmaxf(m, P[i * ld + j]);
+    for (int j = 0; j < n; ++j) P[i * ld + j] = expf(P[i * ld + j] - m);
   }
   __syncthreads();
   for (int k = 0; k < iters; ++k) {
@@ -59,7 +62,8 @@ __device__ inline void sk_forward_block(const float* __restrict__ H, int n, int 
 }
 
 // D: shared [n][ld] holding dM on entry (caller fills it and syncs).
-// Writes dH (global).
+// H and tape may point to global or (faster: no dependent global loads in
+// the iteration loop) shared memory.  Writes dH (global).
 __device__ inline void sk_backward_block(const float* __restrict__ H,
                                          const float* __restrict__ tape, int n, int iters,
                                          float eps, float* D, float* __restrict__ dH) {
@@ -108,6 +112,116 @@ __device__ inline void sk_backward_block(const float* __restrict__ H,
       dH[i * n + j] = D[i * ld + j] - ((h == m) ? share : 0.f);
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// Warp-level single matrix, n divides 32: lane i (< n) holds row i in
+// registers; column sums are butterfly shuffles over the n lanes of the
+// group (identical bits on every lane).  Other lane groups compute on a copy
+// and write nothing.  Same arithmetic and tape layout as the block versions,
+// but a half-step is a few dependent instructions instead of shared-memory
+// round trips and barriers -- this matters because the kernels that run it
+// are one-CTA latency chains.
+template <int N>
+__device__ __forceinline__ void sk_forward_warp(const float* __restrict__ H, int iters, float eps,
+                                                float* __restrict__ tape, float* __restrict__ M) {
+  const int lane = threadIdx.x & 31, row = lane % N;
+  const bool w = lane < N;
+  constexpr int nn = N * N;
+  float p[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) p[j] = H[row * N + j];
+  float m = p[0];
+#pragma unroll
+  for (int j = 1; j < N; ++j) m = fmaxf(m, p[j]);
+#pragma unroll
+  for (int j = 0; j < N; ++j) p[j] = expf(p[j] - m);
+  for (int k = 0; k < iters; ++k) {
+    float* tk = tape ? tape + (size_t)k * (nn + 2 * N) : nullptr;
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      if (tk && w) tk[row * N + j] = p[j];
+      s += p[j];
+    }
+    if (tk && w) tk[nn + row] = s;
+    const float rs = row_scale(s, eps);
+#pragma unroll
+    for (int j = 0; j < N; ++j) p[j] *= rs;
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float c = group_sum<N>(p[j]);
+      if (tk && w && j == row) tk[nn + N + j] = c;
+      p[j] *= col_scale(c, eps);
+    }
+  }
+  if (M && w)
+#pragma unroll
+    for (int j = 0; j < N; ++j) M[row * N + j] = p[j];
+}
+
+// d: this lane's row of dM on entry, of dH_res on exit.  tape: the record
+// of sk_forward_* (global or shared memory).
+template <int N>
+__device__ __forceinline__ void sk_backward_warp(const float* __restrict__ H,
+                                                 const float* __restrict__ tape, int iters,
+                                                 float eps, float (&d)[N]) {
+  const int lane = threadIdx.x & 31, row = lane % N, gbase = lane & ~(N - 1);
+  constexpr int nn = N * N;
+  for (int k = iters - 1; k >= 0; --k) {
+    const float* tk = tape + (size_t)k * (nn + 2 * N);
+    float pa[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) pa[j] = tk[row * N + j];
+    const float r = tk[nn + row];
+    const float cown = tk[nn + N + row];
+    const float rs = row_scale(r, eps);
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float c = __shfl_sync(0xffffffffu, cown, gbase + j);
+      const float dcs = group_sum<N>(d[j] * (pa[j] * rs));
+      const float dc = c > eps ? -dcs / (c * c) : 0.f;
+      d[j] = d[j] * col_scale(c, eps) + dc;
+    }
+    float drs = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) drs += d[j] * pa[j];
+    const float dr = r > eps ? -drs / (r * r) : 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) d[j] = d[j] * rs + dr;
+  }
+  float h[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) h[j] = H[row * N + j];
+  float m = h[0];
+#pragma unroll
+  for (int j = 1; j < N; ++j) m = fmaxf(m, h[j]);
+  float S = 0.f, cnt = 0.f;
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    d[j] *= expf(h[j] - m);
+    S += d[j];
+    cnt += (h[j] == m) ? 1.f : 0.f;
+  }
+  const float share = S / cnt;
+#pragma unroll
+  for (int j = 0; j < N; ++j) d[j] -= (h[j] == m) ? share : 0.f;
+}
+
+// Expand BODY with the compile-time constant SK_N equal to n (n | 32).
+#define MHC_SK_WARP_SWITCH(n, BODY)                 \
+  switch (n) {                                      \
+    case 1: { constexpr int SK_N = 1; BODY; } break;   \
+    case 2: { constexpr int SK_N = 2; BODY; } break;   \
+    case 4: { constexpr int SK_N = 4; BODY; } break;   \
+    case 8: { constexpr int SK_N = 8; BODY; } break;   \
+    case 16: { constexpr int SK_N = 16; BODY; } break; \
+    case 32: { constexpr int SK_N = 32; BODY; } break; \
+    default: break;                                 \
+  }
+
+__host__ __device__ inline bool sk_warp_ok(int n) {
+  return n == 1 || n == 2 || n == 4 || n == 8 || n == 16 || n == 32;
 }
 
 }  // namespace mhc
