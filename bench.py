@@ -54,6 +54,10 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-latency", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--workload", choices=["layer", "sweep", "sinkhorn", "rewire", "all"],
+                    default="layer",
+                    help="layer = the headline (BASELINE target); the others measure BASELINE "
+                         "configs 1-4 and print one JSON line each (1 GPU)")
     return ap.parse_args()
 
 
@@ -492,10 +496,175 @@ def run_reference(args):
     }), flush=True)
 
 
+# ------------------------------------------------- other BASELINE configs --
+def _median_us(fn, dev, iters=200, warm=20):
+    st = torch.cuda.current_stream(dev)
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize(dev)
+    ts = []
+    for _ in range(iters):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        fn()
+        b.record(st)
+        ts.append((a, b))
+    torch.cuda.synchronize(dev)
+    v = sorted(1e3 * a.elapsed_time(b) for a, b in ts)
+    return v[len(v) // 2]
+
+
+def _graph_us(fn, dev, iters=200):
+    st = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(st)
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
+    st.wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return _median_us(g.replay, dev, iters)
+
+
+def _kernel_us_per_step(step, dev, steps=20):
+    """Sum of this library's kernel durations (CUDA events around each
+    C-ABI launch) per step: excludes any library GEMM in the step."""
+    from mhc_b200 import _kernels
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(dev)
+    _kernels.TIMING = {}
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize(dev)
+    timing, _kernels.TIMING = _kernels.TIMING, None
+    per = {k: 1e3 * sum(a.elapsed_time(b) for a, b in v) / steps for k, v in timing.items()}
+    return sum(per.values()), per
+
+
+def run_configs(args):
+    import mhc_b200
+    from mhc_b200 import metal
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak, peak_kind = load_peaks()
+    out = []
+    w = args.workload
+    if w in ("sweep", "all"):
+        # config 2: MHCLayer x[B, 4, C], B in {1, 32}, C in {512, 2048, 4096}, fp32 / bf16
+        rows = []
+        for io in ("f32", "bf16"):
+            dt = torch.float32 if io == "f32" else torch.bfloat16
+            for C in (512, 2048, 4096):
+                for B in (1, 32):
+                    layer = make_layer(4, C, dev)
+                    x = torch.randn(B, 4, C, device=dev).to(dt).requires_grad_(True)
+                    rdt = None if io == "f32" else dt
+                    d = torch.randn(B, 4, C, device=dev).to(rdt or torch.float32)
+
+                    def fb():
+                        x.grad = None
+                        for p_ in layer.parameters():
+                            p_.grad = None
+                        layer(x, return_dtype=rdt).backward(d)
+
+                    def fo():
+                        with torch.no_grad():
+                            layer(x, return_dtype=rdt)
+
+                    rows.append({"io": io, "B": B, "C": C, "fwd_us": _median_us(fo, dev),
+                                 "fwd_bwd_us": _median_us(fb, dev),
+                                 "fwd_bwd_graph_us": _graph_us(fb, dev)})
+        out.append({"metric": "MHCLayer per-call latency, BASELINE config 2 sweep (n=4)",
+                    "unit": "us", "higher_is_better": False, "rows": rows,
+                    "config": {"workload": "config 2 op sweep", "n": 4,
+                               "note": "median of 200 calls, CUDA events; graph = replay of one "
+                                       "captured fwd+bwd"}})
+    if w in ("sinkhorn", "all"):
+        # config 3: 65,536 independent 4x4 logits, 20 iterations, fwd + bwd
+        from mhc_b200 import _kernels as K
+
+        H = torch.randn(65536, 4, 4, device=dev)
+        dM = torch.randn(65536, 4, 4, device=dev)
+        def sk_step():
+            K.sinkhorn_batched_fwd(H, 20, 1e-5)
+            K.sinkhorn_batched_bwd(H, dM, 20, 1e-5)
+
+        tot, per = _kernel_us_per_step(sk_step, dev, steps=50)
+        fw, bw = per["mhc_sinkhorn_batched_fwd"], per["mhc_sinkhorn_batched_bwd"]
+        out.append({"metric": "batched Sinkhorn fwd+bwd matrices/s (65,536 x 4x4, 20 iters)",
+                    "value": 65536 / (tot * 1e-6), "unit": "matrices/s", "higher_is_better": True,
+                    "fwd_us": fw, "bwd_us": bw,
+                    "fwd_gbs": 65536 * 128 / (fw * 1e-6) / 1e9,
+                    "bwd_gbs": 65536 * 192 / (bw * 1e-6) / 1e9,
+                    "config": {"workload": "BASELINE config 3", "note": "8 MB working set: "
+                               "L2-resident, latency/compute-bound (backward replays 20 "
+                               "iterations and reverses them)"}})
+    if w in ("rewire", "all"):
+        from torch import nn
+
+        # config 1: README quick-start, MHCRewire(Linear(2048, 2048), n=32), one row, fp32
+        torch.manual_seed(0)
+        model = mhc_b200.MHCRewire(nn.Linear(2048, 2048), dims=2048, n=32).to(dev)
+        x = torch.randn(1, 2048, device=dev, requires_grad=True)
+
+        def fb1():
+            x.grad = None
+            for p_ in model.parameters():
+                p_.grad = None
+            model(x).sum().backward()
+
+        mk, per1 = _kernel_us_per_step(fb1, dev)
+        out.append({"metric": "MHCRewire quick-start fwd+bwd latency (BASELINE config 1)",
+                    "unit": "us", "higher_is_better": False,
+                    "eager_us": _median_us(fb1, dev), "graph_us": _graph_us(fb1, dev),
+                    "mhc_kernels_us": mk, "mhc_kernels": per1,
+                    "config": {"workload": "MHCRewire(nn.Linear(2048, 2048), dims=2048, n=32), "
+                                           "x (1, 2048) fp32, loss = sum(y), grads of all params"}})
+        # config 4: MHCRewire around a 4-bit QuantizedLinear 4096 -> 4096, n=4, 8192 bf16 tokens
+        g = torch.Generator().manual_seed(4)
+        ql = mhc_b200.QuantizedLinear.random(4096, 4096, group_size=64, bits=4,
+                                             dtype=torch.bfloat16, generator=g).to(dev)
+        model4 = mhc_b200.MHCRewire(ql, dims=4096, n=4).to(dev)
+        x4 = torch.randn(8192, 4096, device=dev).to(torch.bfloat16).requires_grad_(True)
+        d4 = torch.randn(8192, 4096, device=dev)
+
+        def fb4():
+            x4.grad = None
+            for p_ in model4.parameters():
+                p_.grad = None
+            model4(x4).backward(d4)
+
+        mk4, per4 = _kernel_us_per_step(fb4, dev)
+        step_us = _median_us(fb4, dev, iters=30, warm=3)
+        # algorithmic bytes of the mHC kernels per step (bf16 x / y_inner, fp32 out / d_out):
+        #   prescale fwd x->x_pre 2+2; combine fwd x,y->out 2+2+4; combine bwd x,y,d->dx,dy
+        #   2+2+4+2+2; prescale bwd x,d_xpre->dx 2+2+2  (bytes per element)
+        elems = 8192 * 4096
+        mbytes = elems * ((2 + 2) + (2 + 2 + 4) + (2 + 2 + 4 + 2 + 2) + (2 + 2 + 2))
+        out.append({"metric": "MHCRewire(QuantizedLinear 4096, n=4) mHC fwd+bwd tokens/s, GEMM "
+                              "excluded (BASELINE config 4)",
+                    "value": 8192 / (mk4 * 1e-6), "unit": "tokens/s", "higher_is_better": True,
+                    "mhc_kernels_us": mk4, "mhc_kernels": per4,
+                    "mhc_achieved_gbs": mbytes / (mk4 * 1e-6) / 1e9, "peak": peak,
+                    "whole_step_us_incl_gemm": step_us,
+                    "config": {"workload": "8192 bf16 tokens, 4-bit affine QuantizedLinear "
+                                           "(group 64), random codes, fp16-range scales",
+                               "peak_source": f"{peak_kind} hbm_gbs"}})
+    for r in out:
+        print(json.dumps(r), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "layer":
+        run_configs(args)
     else:
         run_b200(args)
 

@@ -595,17 +595,17 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
     }
   }
   if (hres_raw && dhres_raw && (tape || iters == 0)) {
-    const float* Hs = hres_raw;
-    const float* Ts = tape;
-    if (stage_sk) {  // dynamic shared memory holds [tape | logits]
-      const size_t tf = (size_t)iters * sk_tape_stride(n);
-      for (size_t e = tid; e < tf; e += kFinBD) s_fin[e] = tape[e];
-      for (int e = tid; e < n * n; e += kFinBD) s_fin[tf + e] = hres_raw[e];
-      Ts = s_fin;
-      Hs = s_fin + tf;
-    }
-    __syncthreads();
     if (sk_warp_ok(n)) {
+      const float* Hs = hres_raw;
+      const float* Ts = tape;
+      if (stage_sk) {  // dynamic shared memory holds [tape | logits]
+        const size_t tf = (size_t)iters * sk_tape_stride(n);
+        for (size_t e = tid; e < tf; e += kFinBD) s_fin[e] = tape[e];
+        for (int e = tid; e < n * n; e += kFinBD) s_fin[tf + e] = hres_raw[e];
+        Ts = s_fin;
+        Hs = s_fin + tf;
+      }
+      __syncthreads();
       if (tid < 32) {
         const int row = tid % n;
         MHC_SK_WARP_SWITCH(n, ({
@@ -618,10 +618,12 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
       }
       return;
     }
+    const SkTape tp = stage_sk ? sk_stage_tape(tape, n, iters, s_fin)
+                               : SkTape{tape, n, sk_tape_stride(n)};
     const int ld = sk_ld(n);
     for (int e = tid; e < n * n; e += kFinBD) D[(e / n) * ld + e % n] = sP[e];
     __syncthreads();
-    sk_backward_block(Hs, Ts, n, iters, eps, D, dhres_raw);
+    sk_backward_block(hres_raw, tp, n, iters, eps, D, dhres_raw);
   }
 }
 
@@ -931,7 +933,7 @@ int launch_finalize(const void* ws, int n, int C, float* dM, float* dhpre, float
   // Stage the Sinkhorn tape and logits in shared memory when they fit.
   size_t smem = 0;
   if (hres_raw && dhres_raw && tape) {
-    const size_t b = ((size_t)iters * sk_tape_stride(n) + (size_t)n * n) * sizeof(float);
+    const size_t b = sk_stage_floats(n, iters) * sizeof(float);
     if (b <= 160 * 1024) smem = b;
   }
   if (allow_dyn_smem(k_finalize, smem) != cudaSuccess) smem = 0;

@@ -13,7 +13,7 @@ size_t sk_tape_floats(int n, int iters) { return (size_t)iters * sk_tape_stride(
 
 // ---------------------------------------------------------------------------
 // Single matrix: one CTA computes H_pre_act, H_post_act and M (+ tape).
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(1024)
 k_params_fwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost_raw,
              const float* __restrict__ hres_raw, int n, int iters, float eps,
              float* __restrict__ hpre, float* __restrict__ hpost, float* __restrict__ M,
@@ -32,7 +32,7 @@ k_params_fwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost
   sk_forward_block(hres_raw, n, iters, eps, P, tape, M);
 }
 
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(1024)
 k_params_bwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost_raw,
              const float* __restrict__ hres_raw, const float* __restrict__ tape, int n,
              int iters, float eps, const float* __restrict__ dhpre,
@@ -54,16 +54,16 @@ k_params_bwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost
     }
   }
   if (hres_raw && dM) {
-    const float* Hs = hres_raw;
-    const float* Ts = tape;
-    if (stage) {
-      const size_t tf = (size_t)iters * sk_tape_stride(n);
-      for (size_t e = tid; e < tf; e += blockDim.x) s_stage_sk[e] = tape[e];
-      for (int e = tid; e < n * n; e += blockDim.x) s_stage_sk[tf + e] = hres_raw[e];
-      Ts = s_stage_sk;
-      Hs = s_stage_sk + tf;
-    }
     if (sk_warp_ok(n)) {
+      const float* Hs = hres_raw;
+      const float* Ts = tape;
+      if (stage) {
+        const size_t tf = (size_t)iters * sk_tape_stride(n);
+        for (size_t e = tid; e < tf; e += blockDim.x) s_stage_sk[e] = tape[e];
+        for (int e = tid; e < n * n; e += blockDim.x) s_stage_sk[tf + e] = hres_raw[e];
+        Ts = s_stage_sk;
+        Hs = s_stage_sk + tf;
+      }
       __syncthreads();
       if (threadIdx.x < 32) {
         const int row = threadIdx.x % n;
@@ -77,16 +77,18 @@ k_params_bwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost
       }
       return;
     }
+    const SkTape tp = stage ? sk_stage_tape(tape, n, iters, s_stage_sk)
+                            : SkTape{tape, n, sk_tape_stride(n)};
     for (int e = tid; e < n * n; e += blockDim.x) D[(e / n) * ld + e % n] = dM[e];
     __syncthreads();
-    sk_backward_block(Hs, Ts, n, iters, eps, D, dhres_raw);
+    sk_backward_block(hres_raw, tp, n, iters, eps, D, dhres_raw);
   }
 }
 
 int launch_params_fwd(const float* hpre_raw, const float* hpost_raw, const float* hres_raw,
                       int n, int iters, float eps, float* hpre, float* hpost, float* M,
                       float* tape, cudaStream_t st) {
-  const int threads = n <= 32 ? 32 : 64;
+  const int threads = sk_threads(n);
   k_params_fwd<<<1, threads, 0, st>>>(hpre_raw, hpost_raw, hres_raw, n, iters, eps, hpre,
                                       hpost, M, tape);
   return check_launch("params_fwd");
@@ -96,10 +98,10 @@ int launch_params_bwd(const float* hpre_raw, const float* hpost_raw, const float
                       const float* tape, int n, int iters, float eps, const float* dhpre,
                       const float* dhpost, const float* dM, float* dhpre_raw,
                       float* dhpost_raw, float* dhres_raw, cudaStream_t st) {
-  const int threads = n <= 32 ? 32 : 64;
+  const int threads = sk_threads(n);
   size_t smem = 0;
   if (hres_raw && dM && tape) {
-    const size_t b = ((size_t)iters * sk_tape_stride(n) + (size_t)n * n) * sizeof(float);
+    const size_t b = sk_stage_floats(n, iters) * sizeof(float);
     if (b <= 160 * 1024) smem = b;
   }
   if (allow_dyn_smem(k_params_bwd, smem) != cudaSuccess) smem = 0;
@@ -269,7 +271,7 @@ k_sk_batched_generic(const float* __restrict__ H, const float* __restrict__ dM, 
       __syncthreads();
       for (int e = threadIdx.x; e < nn; e += blockDim.x) P[(e / n) * ld + e % n] = dM[m * nn + e];
       __syncthreads();
-      sk_backward_block(Hm, tape, n, iters, eps, P, out + m * nn);
+      sk_backward_block(Hm, SkTape{tape, n, sk_tape_stride(n)}, n, iters, eps, P, out + m * nn);
     }
     __syncthreads();
   }

@@ -22,38 +22,52 @@ __host__ __device__ constexpr int sk_ld(int n) { return n + 1; }
 
 __host__ __device__ inline size_t sk_tape_stride(int n) { return (size_t)n * n + 2 * (size_t)n; }
 
-// P: shared [n][ld]; tape: global, nullable.  Writes M (global, nullable).
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block version, any n <= 64, blockDim a multiple of 32: one warp per row
+// (row step) or per column (column step); lanes cover the line's entries and
+// reduce with a warp butterfly.  P: shared [n][ld] with ld = n + 1, so row
+// and column sweeps are both conflict-free.  tape (global, nullable) uses
+// the pitch-n layout [k][n*n | n row sums | n column sums].  Writes M
+// (global, nullable).
 __device__ inline void sk_forward_block(const float* __restrict__ H, int n, int iters, float eps,
                                         float* P, float* __restrict__ tape,
                                         float* __restrict__ M) {
   const int tid = threadIdx.x, bd = blockDim.x, ld = sk_ld(n), nn = n * n;
-  // stage the logits with one coalesced pass, then shift by the row max and exp
+  const int lane = tid & 31, warp = tid >> 5, nw = bd >> 5;
   for (int e = tid; e < nn; e += bd) P[(e / n) * ld + e % n] = H[e];
   __syncthreads();
-  for (int i = tid; i < n; i += bd) {
-    float m = P[i * ld];
-    for (int j = 1; j < n; ++j) m = fmaxf(m, P[i * ld + j]);
-    for (int j = 0; j < n; ++j) P[i * ld + j] = expf(P[i * ld + j] - m);
+  for (int i = warp; i < n; i += nw) {
+    float m = -INFINITY;
+    for (int j = lane; j < n; j += 32) m = fmaxf(m, P[i * ld + j]);
+    m = warp_max(m);
+    for (int j = lane; j < n; j += 32) P[i * ld + j] = expf(P[i * ld + j] - m);
   }
   __syncthreads();
   for (int k = 0; k < iters; ++k) {
     float* tk = tape ? tape + (size_t)k * sk_tape_stride(n) : nullptr;
     if (tk)
       for (int e = tid; e < nn; e += bd) tk[e] = P[(e / n) * ld + e % n];
-    for (int i = tid; i < n; i += bd) {
+    for (int i = warp; i < n; i += nw) {
       float s = 0.f;
-      for (int j = 0; j < n; ++j) s += P[i * ld + j];
+      for (int j = lane; j < n; j += 32) s += P[i * ld + j];
+      s = warp_sum(s);
       const float sc = row_scale(s, eps);
-      for (int j = 0; j < n; ++j) P[i * ld + j] *= sc;
-      if (tk) tk[nn + i] = s;
+      for (int j = lane; j < n; j += 32) P[i * ld + j] *= sc;
+      if (tk && lane == 0) tk[nn + i] = s;
     }
     __syncthreads();
-    for (int j = tid; j < n; j += bd) {
+    for (int j = warp; j < n; j += nw) {
       float s = 0.f;
-      for (int i = 0; i < n; ++i) s += P[i * ld + j];
+      for (int i = lane; i < n; i += 32) s += P[i * ld + j];
+      s = warp_sum(s);
       const float sc = col_scale(s, eps);
-      for (int i = 0; i < n; ++i) P[i * ld + j] *= sc;
-      if (tk) tk[nn + n + j] = s;
+      for (int i = lane; i < n; i += 32) P[i * ld + j] *= sc;
+      if (tk && lane == 0) tk[nn + n + j] = s;
     }
     __syncthreads();
   }
@@ -61,53 +75,83 @@ __device__ inline void sk_forward_block(const float* __restrict__ H, int n, int 
     for (int e = tid; e < nn; e += bd) M[e] = P[(e / n) * ld + e % n];
 }
 
+// Tape view: matrix pitch `tp` (n for the global layout, n + 1 when staged in
+// shared memory to keep column reads conflict-free) and iteration stride.
+struct SkTape {
+  const float* base;
+  int tp;
+  size_t stride;
+  __device__ const float* it(int k) const { return base + (size_t)k * stride; }
+};
+
+// Copy the pitch-n global tape into shared memory with pitch n + 1.
+__device__ inline SkTape sk_stage_tape(const float* __restrict__ tape, int n, int iters,
+                                       float* smem) {
+  const int nn = n * n, ld = sk_ld(n);
+  const size_t gs = sk_tape_stride(n), ss = (size_t)n * ld + 2 * n;
+  for (size_t e = threadIdx.x; e < (size_t)iters * gs; e += blockDim.x) {
+    const size_t k = e / gs, r = e - k * gs;
+    const size_t dst = r < (size_t)nn ? (r / n) * ld + r % n : (size_t)n * ld + (r - nn);
+    smem[k * ss + dst] = tape[e];
+  }
+  return SkTape{smem, ld, ss};
+}
+
+__host__ __device__ inline size_t sk_staged_tape_floats(int n, int iters) {
+  return (size_t)iters * ((size_t)n * sk_ld(n) + 2 * (size_t)n);
+}
+
 // D: shared [n][ld] holding dM on entry (caller fills it and syncs).
-// H and tape may point to global or (faster: no dependent global loads in
-// the iteration loop) shared memory.  Writes dH (global).
-__device__ inline void sk_backward_block(const float* __restrict__ H,
-                                         const float* __restrict__ tape, int n, int iters,
-                                         float eps, float* D, float* __restrict__ dH) {
-  const int tid = threadIdx.x, bd = blockDim.x, ld = sk_ld(n), nn = n * n;
+// H: logits (global or shared).  Writes dH (global).  Same warp-per-line
+// mapping as the forward.
+__device__ inline void sk_backward_block(const float* __restrict__ H, SkTape tape, int n,
+                                         int iters, float eps, float* D, float* __restrict__ dH) {
+  const int tid = threadIdx.x, bd = blockDim.x, ld = sk_ld(n);
+  const int lane = tid & 31, warp = tid >> 5, nw = bd >> 5;
+  const int tp = tape.tp, rofs = n * tp, cofs = n * tp + n;
   for (int k = iters - 1; k >= 0; --k) {
-    const float* tk = tape + (size_t)k * sk_tape_stride(n);
+    const float* tk = tape.it(k);
     // column step: out = Pb * cs_j, c_j = sum_i Pb_ij
-    for (int j = tid; j < n; j += bd) {
-      const float c = tk[nn + n + j];
+    for (int j = warp; j < n; j += nw) {
+      const float c = tk[cofs + j];
       const float cs = col_scale(c, eps);
       float dcs = 0.f;
-      for (int i = 0; i < n; ++i) {
-        const float pb = tk[i * n + j] * row_scale(tk[nn + i], eps);
-        dcs += D[i * ld + j] * pb;
-      }
+      for (int i = lane; i < n; i += 32)
+        dcs += D[i * ld + j] * (tk[i * tp + j] * row_scale(tk[rofs + i], eps));
+      dcs = warp_sum(dcs);
       const float dc = c > eps ? -dcs / (c * c) : 0.f;
-      for (int i = 0; i < n; ++i) D[i * ld + j] = D[i * ld + j] * cs + dc;
+      for (int i = lane; i < n; i += 32) D[i * ld + j] = D[i * ld + j] * cs + dc;
     }
     __syncthreads();
     // row step: Pb = Pa * rs_i, r_i = sum_j Pa_ij
-    for (int i = tid; i < n; i += bd) {
-      const float r = tk[nn + i];
+    for (int i = warp; i < n; i += nw) {
+      const float r = tk[rofs + i];
       const float rs = row_scale(r, eps);
       float drs = 0.f;
-      for (int j = 0; j < n; ++j) drs += D[i * ld + j] * tk[i * n + j];
+      for (int j = lane; j < n; j += 32) drs += D[i * ld + j] * tk[i * tp + j];
+      drs = warp_sum(drs);
       const float dr = r > eps ? -drs / (r * r) : 0.f;
-      for (int j = 0; j < n; ++j) D[i * ld + j] = D[i * ld + j] * rs + dr;
+      for (int j = lane; j < n; j += 32) D[i * ld + j] = D[i * ld + j] * rs + dr;
     }
     __syncthreads();
   }
   // exp and the row-max shift
-  for (int i = tid; i < n; i += bd) {
-    float m = H[i * n];
-    for (int j = 1; j < n; ++j) m = fmaxf(m, H[i * n + j]);
+  for (int i = warp; i < n; i += nw) {
+    float m = -INFINITY;
+    for (int j = lane; j < n; j += 32) m = fmaxf(m, H[i * n + j]);
+    m = warp_max(m);
     float S = 0.f, cnt = 0.f;
-    for (int j = 0; j < n; ++j) {
+    for (int j = lane; j < n; j += 32) {
       const float h = H[i * n + j];
       const float ds = D[i * ld + j] * expf(h - m);
       D[i * ld + j] = ds;
       S += ds;
       cnt += (h == m) ? 1.f : 0.f;
     }
+    S = warp_sum(S);
+    cnt = warp_sum(cnt);
     const float share = S / cnt;
-    for (int j = 0; j < n; ++j) {
+    for (int j = lane; j < n; j += 32) {
       const float h = H[i * n + j];
       dH[i * n + j] = D[i * ld + j] - ((h == m) ? share : 0.f);
     }
@@ -215,13 +259,23 @@ __device__ __forceinline__ void sk_backward_warp(const float* __restrict__ H,
     case 2: { constexpr int SK_N = 2; BODY; } break;   \
     case 4: { constexpr int SK_N = 4; BODY; } break;   \
     case 8: { constexpr int SK_N = 8; BODY; } break;   \
-    case 16: { constexpr int SK_N = 16; BODY; } break; \
-    case 32: { constexpr int SK_N = 32; BODY; } break; \
     default: break;                                 \
   }
 
+// The one-lane-per-row register path pays off for small n; from n = 16 on a
+// lane would walk n^2 / 32 entries per step, so the warp-per-line block
+// version is used instead.
 __host__ __device__ inline bool sk_warp_ok(int n) {
-  return n == 1 || n == 2 || n == 4 || n == 8 || n == 16 || n == 32;
+  return n == 1 || n == 2 || n == 4 || n == 8;
 }
+
+// Shared-memory floats a one-CTA Sinkhorn backward stages: the pitch-n tape
+// plus the logits for the register path (n <= 8), the padded tape for the
+// warp-per-line path.  Threads per CTA for the single-matrix kernels.
+__host__ __device__ inline size_t sk_stage_floats(int n, int iters) {
+  return sk_warp_ok(n) ? (size_t)iters * sk_tape_stride(n) + (size_t)n * n
+                       : sk_staged_tape_floats(n, iters);
+}
+__host__ __device__ inline int sk_threads(int n) { return sk_warp_ok(n) ? 32 : 32 * (n < 32 ? n : 32); }
 
 }  // namespace mhc

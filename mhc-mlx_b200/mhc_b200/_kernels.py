@@ -35,6 +35,12 @@ def _timed(name: str, ref: torch.Tensor):
     TIMING.setdefault(name, []).append((a, b))
 
 
+def _call(name: str, ref: torch.Tensor, *args) -> None:
+    """C.call with optional per-launch event timing (see TIMING)."""
+    with _timed(name, ref):
+        C.call(name, *args)
+
+
 def _c(t: torch.Tensor) -> torch.Tensor:
     return t if t.is_contiguous() else t.contiguous()
 
@@ -74,9 +80,8 @@ def params_fwd(H_pre_raw, H_post_raw, H_res_raw, iters: int, eps: float, want_ta
         tape = None
         if want_tape and res is not None and iters > 0:
             tape = torch.empty(tape_floats(n, iters), dtype=F32, device=dev)
-        with _timed("mhc_params_fwd", ref):
-            C.call("mhc_params_fwd", C.ptr(pre), C.ptr(post), C.ptr(res), n, int(iters),
-                   float(eps), C.ptr(hpre), C.ptr(hpost), C.ptr(M), C.ptr(tape), C.stream_of(ref))
+        _call("mhc_params_fwd", ref, C.ptr(pre), C.ptr(post), C.ptr(res), n, int(iters),
+              float(eps), C.ptr(hpre), C.ptr(hpost), C.ptr(M), C.ptr(tape), C.stream_of(ref))
     return hpre, hpost, M, tape
 
 
@@ -92,7 +97,7 @@ def params_bwd(H_pre_raw, H_post_raw, H_res_raw, tape, iters: int, eps: float, d
         gpre = torch.empty(n, dtype=F32, device=dev) if pre is not None else None
         gpost = torch.empty(n, dtype=F32, device=dev) if post is not None else None
         gres = torch.empty(n, n, dtype=F32, device=dev) if res is not None else None
-        C.call("mhc_params_bwd", C.ptr(pre), C.ptr(post), C.ptr(res), C.ptr(tape), n, int(iters),
+        _call("mhc_params_bwd", ref, C.ptr(pre), C.ptr(post), C.ptr(res), C.ptr(tape), n, int(iters),
                float(eps), C.ptr(_f32(dhpre) if pre is not None else None),
                C.ptr(_f32(dhpost) if post is not None else None),
                C.ptr(_f32(dM) if res is not None else None), C.ptr(gpre), C.ptr(gpost),
@@ -106,7 +111,7 @@ def sinkhorn_batched_fwd(H: torch.Tensor, iters: int, eps: float) -> torch.Tenso
     with torch.cuda.device(dev):
         Hc = _f32(H)
         M = torch.empty(B, n, n, dtype=F32, device=dev)
-        C.call("mhc_sinkhorn_batched_fwd", C.ptr(Hc), B, n, int(iters), float(eps), C.ptr(M),
+        _call("mhc_sinkhorn_batched_fwd", Hc, C.ptr(Hc), B, n, int(iters), float(eps), C.ptr(M),
                C.stream_of(Hc))
     return M
 
@@ -119,7 +124,7 @@ def sinkhorn_batched_bwd(H: torch.Tensor, dM: torch.Tensor, iters: int, eps: flo
         dH = torch.empty(B, n, n, dtype=F32, device=dev)
         nb = int(C.query("mhc_sinkhorn_batched_workspace_bytes", B, n, int(iters)))
         ws = _ws(nb, dev) if nb else None
-        C.call("mhc_sinkhorn_batched_bwd", C.ptr(Hc), C.ptr(dMc), B, n, int(iters), float(eps),
+        _call("mhc_sinkhorn_batched_bwd", Hc, C.ptr(Hc), C.ptr(dMc), B, n, int(iters), float(eps),
                C.ptr(dH), C.ptr(ws), nb, C.stream_of(Hc))
     return dH
 
@@ -134,8 +139,7 @@ def layer_fwd(x, M, hpre, hpost, w, eps: float, out_dtype: torch.dtype) -> torch
         args = (C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(_f32(M)), C.ptr(_f32(hpre)),
                 C.ptr(_f32(hpost)), C.ptr(_f32(w)), C.ptr(out), C.dtype_code(out_dtype), T, n, Cc,
                 float(eps), C.stream_of(xc))
-        with _timed("mhc_fwd", xc):
-            C.call("mhc_fwd", *args)
+        _call("mhc_fwd", xc, *args)
     return out
 
 
@@ -156,14 +160,13 @@ def layer_bwd(x, dout, M, hpre, hpost, w, eps: float, raw=None):
         args = (C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(dc), C.dtype_code(dc.dtype),
                 C.ptr(_f32(M)), C.ptr(_f32(hpre)), C.ptr(_f32(hpost)), C.ptr(_f32(w)), C.ptr(dx),
                 C.dtype_code(dx.dtype), T, n, Cc, float(eps), C.ptr(ws), nb, st)
-        with _timed("mhc_bwd", xc):
-            C.call("mhc_bwd", *args)
+        _call("mhc_bwd", xc, *args)
         dw = torch.empty(Cc, dtype=F32, device=dev)
         if raw is None:
             dM = torch.empty(n, n, dtype=F32, device=dev)
             dpre = torch.empty(n, dtype=F32, device=dev)
             dpost = torch.empty(n, dtype=F32, device=dev)
-            C.call("mhc_bwd_finalize", C.ptr(ws), n, Cc, C.ptr(dM), C.ptr(dpre), C.ptr(dpost),
+            _call("mhc_bwd_finalize", xc, C.ptr(ws), n, Cc, C.ptr(dM), C.ptr(dpre), C.ptr(dpost),
                    C.ptr(dw), None, None, None, None, 0, float(eps), None, None, None, st)
             return dx, dM, dpre, dpost, dw
         pre_raw, post_raw, res_raw, tape, iters = raw
@@ -173,8 +176,7 @@ def layer_bwd(x, dout, M, hpre, hpost, w, eps: float, raw=None):
         args = (C.ptr(ws), n, Cc, None, None, None, C.ptr(dw), C.ptr(_f32(pre_raw)),
                 C.ptr(_f32(post_raw)), C.ptr(_f32(res_raw)), C.ptr(tape), int(iters), float(eps),
                 C.ptr(gpre), C.ptr(gpost), C.ptr(gres), st)
-        with _timed("mhc_bwd_finalize", xc):
-            C.call("mhc_bwd_finalize", *args)
+        _call("mhc_bwd_finalize", xc, *args)
         return dx, gpre, gpost, gres, dw
 
 
@@ -186,7 +188,7 @@ def mix_add_fwd(x, M, y, out_dtype=F32) -> torch.Tensor:
         xc = _io(x)
         yc = _c(y) if y.dtype in (F32, xc.dtype) else y.float().contiguous()
         out = torch.empty(T, n, Cc, dtype=out_dtype, device=dev)
-        C.call("mhc_mix_add_fwd", C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(_f32(M)), C.ptr(yc),
+        _call("mhc_mix_add_fwd", xc, C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(_f32(M)), C.ptr(yc),
                C.dtype_code(yc.dtype), C.ptr(out), C.dtype_code(out_dtype), T, n, Cc,
                C.stream_of(xc))
     return out
@@ -202,7 +204,7 @@ def mix_add_bwd(x, M, dout):
         dM = torch.empty(n, n, dtype=F32, device=dev)
         nb = int(C.query("mhc_mix_bwd_workspace_bytes", T, n, Cc))
         ws = _ws(nb, dev)
-        C.call("mhc_mix_add_bwd", C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(_f32(M)), C.ptr(dc),
+        _call("mhc_mix_add_bwd", xc, C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(_f32(M)), C.ptr(dc),
                C.dtype_code(dc.dtype), C.ptr(dx), C.dtype_code(dx.dtype), C.ptr(dM), T, n, Cc,
                C.ptr(ws), nb, C.stream_of(xc))
     return dx, dM
@@ -215,7 +217,7 @@ def rewire_fwd(x, y, M, hpre, hpost, out_dtype=F32) -> torch.Tensor:
         xc = _io(x)
         yc = _c(y) if y.dtype in (F32, xc.dtype) else y.float().contiguous()
         out = torch.empty(T, n, Cc, dtype=out_dtype, device=dev)
-        C.call("mhc_rewire_combine_fwd", C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(yc),
+        _call("mhc_rewire_combine_fwd", xc, C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(yc),
                C.dtype_code(yc.dtype), C.ptr(_f32(M)), C.ptr(_f32(hpre)), C.ptr(_f32(hpost)),
                C.ptr(out), C.dtype_code(out_dtype), T, n, Cc, C.stream_of(xc))
     return out
@@ -235,7 +237,7 @@ def rewire_bwd(x, y, dout, M, hpre, hpost):
         dpost = torch.empty(n, dtype=F32, device=dev)
         nb = int(C.query("mhc_rewire_bwd_workspace_bytes", T, n, Cc))
         ws = _ws(nb, dev)
-        C.call("mhc_rewire_combine_bwd", C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(yc),
+        _call("mhc_rewire_combine_bwd", xc, C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(yc),
                C.dtype_code(yc.dtype), C.ptr(dc), C.dtype_code(dc.dtype), C.ptr(_f32(M)),
                C.ptr(_f32(hpre)), C.ptr(_f32(hpost)), C.ptr(dx), C.dtype_code(dx.dtype), C.ptr(dy),
                C.dtype_code(dy.dtype), C.ptr(dM), C.ptr(dpre), C.ptr(dpost), T, n, Cc, C.ptr(ws),
@@ -250,7 +252,7 @@ def prescale_fwd(x, hpre, out_dtype=None) -> torch.Tensor:
         xc = _io(x)
         odt = out_dtype or xc.dtype
         out = torch.empty(T, n, Cc, dtype=odt, device=dev)
-        C.call("mhc_prescale_fwd", C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(_f32(hpre)), C.ptr(out),
+        _call("mhc_prescale_fwd", xc, C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(_f32(hpre)), C.ptr(out),
                C.dtype_code(odt), T, n, Cc, C.stream_of(xc))
     return out
 
@@ -265,7 +267,7 @@ def prescale_bwd(x, d, hpre):
         dpre = torch.empty(n, dtype=F32, device=dev)
         nb = int(C.query("mhc_mix_bwd_workspace_bytes", T, n, Cc))
         ws = _ws(nb, dev)
-        C.call("mhc_prescale_bwd", C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(dc),
+        _call("mhc_prescale_bwd", xc, C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(dc),
                C.dtype_code(dc.dtype), C.ptr(_f32(hpre)), C.ptr(dx), C.dtype_code(dx.dtype),
                C.ptr(dpre), T, n, Cc, C.ptr(ws), nb, C.stream_of(xc))
     return dx, dpre
@@ -279,7 +281,7 @@ def residual_add_agg(x, res, hpre, out_dtype=F32):
         rc = _c(res.to(xc.dtype))
         out = torch.empty(T, n, Cc, dtype=out_dtype, device=dev)
         yagg = torch.empty(T, Cc, dtype=F32, device=dev)
-        C.call("mhc_residual_add_agg", C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(rc),
+        _call("mhc_residual_add_agg", xc, C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(rc),
                C.dtype_code(rc.dtype), C.ptr(_f32(hpre)), C.ptr(out), C.dtype_code(out_dtype),
                C.ptr(yagg), T, n, Cc, C.stream_of(xc))
     return out, yagg
