@@ -489,6 +489,8 @@ static int combine_fwd_t(const void* xv, const void* yv, const float* M, const f
     case 2: if (vec) MHC_CF(2, true, VX, gv); else MHC_CF(2, true, 1, g1); break;
     case 4: if (vec) MHC_CF(4, true, VX, gv); else MHC_CF(4, true, 1, g1); break;
     case 8: if (vec) MHC_CF(8, true, VX, gv); else MHC_CF(8, true, 1, g1); break;
+    case 16: MHC_CF(16, true, 1, g1); break;
+    case 32: MHC_CF(32, true, 1, g1); break;
     default: MHC_CF(64, false, 1, g1); break;
   }
 #undef MHC_CF
@@ -651,6 +653,8 @@ static int prescale_fwd_t(const void* xv, const float* hpre, void* ov, int64_t T
     case 2: if (vec) MHC_PF(2, true, VX, gv); else MHC_PF(2, true, 1, g1); break;
     case 4: if (vec) MHC_PF(4, true, VX, gv); else MHC_PF(4, true, 1, g1); break;
     case 8: if (vec) MHC_PF(8, true, VX, gv); else MHC_PF(8, true, 1, g1); break;
+    case 16: if (vec) MHC_PF(16, true, VX, gv); else MHC_PF(16, true, 1, g1); break;
+    case 32: if (vec) MHC_PF(32, true, VX, gv); else MHC_PF(32, true, 1, g1); break;
     default: if (vec) MHC_PF(64, false, VX, gv); else MHC_PF(64, false, 1, g1); break;
   }
 #undef MHC_PF
@@ -693,6 +697,8 @@ static int prescale_bwd_t(const void* xv, const void* dv, const float* hpre, voi
     case 2: if (vec) MHC_PB(2, true, VX, gv); else MHC_PB(2, true, 1, g1); break;
     case 4: if (vec) MHC_PB(4, true, VX, gv); else MHC_PB(4, true, 1, g1); break;
     case 8: if (vec) MHC_PB(8, true, VX, gv); else MHC_PB(8, true, 1, g1); break;
+    case 16: MHC_PB(16, true, 1, g1); break;
+    case 32: MHC_PB(32, true, 1, g1); break;
     default: MHC_PB(64, false, 1, g1); break;
   }
 #undef MHC_PB
@@ -744,6 +750,8 @@ static int residual_t(const void* xv, const void* rv, const float* hpre, void* o
     case 2: if (vec) MHC_RA(2, true, VX, gv); else MHC_RA(2, true, 1, g1); break;
     case 4: if (vec) MHC_RA(4, true, VX, gv); else MHC_RA(4, true, 1, g1); break;
     case 8: if (vec) MHC_RA(8, true, VX, gv); else MHC_RA(8, true, 1, g1); break;
+    case 16: if (vec) MHC_RA(16, true, VX, gv); else MHC_RA(16, true, 1, g1); break;
+    case 32: if (vec) MHC_RA(32, true, VX, gv); else MHC_RA(32, true, 1, g1); break;
     default: MHC_RA(64, false, 1, g1); break;
   }
 #undef MHC_RA

@@ -171,9 +171,13 @@ k_sk_batched_fwd(const float* __restrict__ H, int64_t batch, int iters, float ep
   if (valid) sk_row_store<N>(M + (m * N + row) * N, p);
 }
 
-// Backward: replays the forward into a shared-memory tape laid out
-// [iters][N + 2][blockDim] (thread index fastest: conflict-free), then runs
-// reverse mode through the iterations.
+// Backward: replays the forward into a shared-memory tape that keeps only
+// each thread's row before every row step, [iters][N][blockDim] (thread index
+// fastest: conflict-free).  The row sum and the column sums of an iteration
+// are recomputed from it in the backward with the forward's own operations
+// in the same order (sequential row sum; product by the row scale, then the
+// same butterfly), so they are bit-identical to the forward's.  Storing N
+// floats per iteration instead of N + 2 lets more threads stay resident.
 template <int N>
 __global__ void __launch_bounds__(256)
 k_sk_batched_bwd(const float* __restrict__ H, const float* __restrict__ dM, int64_t batch,
@@ -183,9 +187,8 @@ k_sk_batched_bwd(const float* __restrict__ H, const float* __restrict__ dM, int6
   const int64_t gid = (int64_t)blockIdx.x * bd + tid;
   const int64_t m = gid / N;
   const int row = (int)(gid % N);
-  const int gbase = (tid & 31) & ~(N - 1);
   const bool valid = m < batch;
-  auto TP = [&](int k, int f) -> float& { return s_tape[((size_t)k * (N + 2) + f) * bd + tid]; };
+  auto TP = [&](int k, int j) -> float& { return s_tape[((size_t)k * N + j) * bd + tid]; };
 
   float h[N], p[N];
   if (valid) sk_row_load<N>(H + (m * N + row) * N, h);
@@ -201,16 +204,11 @@ k_sk_batched_bwd(const float* __restrict__ H, const float* __restrict__ dM, int6
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < N; ++j) { TP(k, j) = p[j]; s += p[j]; }
-    TP(k, N) = s;
     const float rs = row_scale(s, eps);
 #pragma unroll
     for (int j = 0; j < N; ++j) p[j] *= rs;
 #pragma unroll
-    for (int j = 0; j < N; ++j) {
-      const float c = group_sum<N>(p[j]);
-      if (j == row) TP(k, N + 1) = c;
-      p[j] *= col_scale(c, eps);
-    }
+    for (int j = 0; j < N; ++j) p[j] *= col_scale(group_sum<N>(p[j]), eps);
   }
 
   float d[N];
@@ -219,16 +217,16 @@ k_sk_batched_bwd(const float* __restrict__ H, const float* __restrict__ dM, int6
 #pragma unroll
     for (int j = 0; j < N; ++j) d[j] = 0.f;
   for (int k = iters - 1; k >= 0; --k) {
-    float pa[N];
+    float pa[N], pb[N];
+    float r = 0.f;
 #pragma unroll
-    for (int j = 0; j < N; ++j) pa[j] = TP(k, j);
-    const float r = TP(k, N);
+    for (int j = 0; j < N; ++j) { pa[j] = TP(k, j); r += pa[j]; }
     const float rs = row_scale(r, eps);
-    const float cown = TP(k, N + 1);
 #pragma unroll
     for (int j = 0; j < N; ++j) {
-      const float c = __shfl_sync(0xffffffffu, cown, gbase + j);
-      const float dcs = group_sum<N>(d[j] * (pa[j] * rs));
+      pb[j] = pa[j] * rs;
+      const float c = group_sum<N>(pb[j]);
+      const float dcs = group_sum<N>(d[j] * pb[j]);
       const float dc = c > eps ? -dcs / (c * c) : 0.f;
       d[j] = d[j] * col_scale(c, eps) + dc;
     }
@@ -279,14 +277,22 @@ k_sk_batched_generic(const float* __restrict__ H, const float* __restrict__ dM, 
 
 static bool sk_small_path(int n) { return n == 1 || n == 2 || n == 4 || n == 8 || n == 16 || n == 32; }
 
-// Threads per CTA for the shared-memory-tape backward; 0 if even one warp's
-// tape does not fit.
+// Threads per CTA for the shared-memory-tape backward: the size that keeps
+// the most threads resident per SM given the per-thread tape; 0 if even one
+// warp's tape does not fit in a CTA.
 static int sk_bwd_threads(int n, int iters) {
-  const size_t per_thread = (size_t)iters * (n + 2) * sizeof(float);
-  const size_t budget = 160 * 1024;
-  for (int t = 256; t >= 32; t -= 32)
-    if (per_thread * t <= budget) return t;
-  return 0;
+  const size_t per_thread = (size_t)iters * n * sizeof(float);
+  const size_t cta_cap = (size_t)max_smem_optin();
+  const size_t sm_cap = 227 * 1024;
+  int best = 0, best_resident = 0;
+  for (int t = 32; t <= 256; t += 32) {
+    const size_t b = per_thread * t;
+    if (b > cta_cap) break;
+    int ctas = b ? (int)(sm_cap / b) : 64;
+    if (ctas > 2048 / t) ctas = 2048 / t;
+    if (ctas * t >= best_resident) { best_resident = ctas * t; best = t; }
+  }
+  return best;
 }
 
 static int sk_generic_grid(int64_t batch) {
@@ -313,7 +319,7 @@ template <int N>
 static int sk_bwd_small(const float* H, const float* dM, int64_t batch, int iters, float eps,
                         float* dH, cudaStream_t st) {
   const int threads = sk_bwd_threads(N, iters);
-  const size_t smem = (size_t)iters * (N + 2) * threads * sizeof(float);
+  const size_t smem = (size_t)iters * N * threads * sizeof(float);
   {
     cudaError_t e = allow_dyn_smem(k_sk_batched_bwd<N>, smem);
     if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "sinkhorn_batched_bwd: %s", cudaGetErrorString(e));
