@@ -54,7 +54,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-latency", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--workload", choices=["layer", "sweep", "sinkhorn", "rewire", "all"],
+    ap.add_argument("--workload", choices=["layer", "sweep", "sinkhorn", "rewire", "llama", "all"],
                     default="layer",
                     help="layer = the headline (BASELINE target); the others measure BASELINE "
                          "configs 1-4 and print one JSON line each (1 GPU)")
@@ -659,10 +659,77 @@ def run_configs(args):
         print(json.dumps(r), flush=True)
 
 
+def run_llama(args):
+    """Llama-style mock (32 layers, hidden 4096, SwiGLU
+    11008, vocab 32000, bf16 random init), every square projection wrapped
+    with MHCRewire n=4; batch 8 x seq 4096 random token ids, sequences
+    sharded over ranks (strong scaling), mHC fine-tuning step."""
+    import datetime
+
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(ROOT / "mhc-mlx_b200" / "examples"))
+    import llama_mock
+    from mhc_b200 import _kernels
+    from mhc_b200.dist import shard_tokens
+
+    rank, local, world = env_rank()
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, S, V = 8, 4096, 32000
+    model = llama_mock.build(device=dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    tokens = torch.randint(0, V, (B, S), device=dev, generator=g)
+    targets = torch.randint(0, V, (B, S), device=dev, generator=g)
+    tok, tgt = shard_tokens(tokens, rank, world), shard_tokens(targets, rank, world)
+    steps = max(1, min(args.steps, 5))
+    for _ in range(max(1, min(args.warmup, 2))):
+        llama_mock.train_step(model, tok, tgt, B * S)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    st = torch.cuda.current_stream(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _kernels.TIMING = {}
+    a.record(st)
+    for _ in range(steps):
+        loss = llama_mock.train_step(model, tok, tgt, B * S)
+    b.record(st)
+    torch.cuda.synchronize(dev)
+    timing, _kernels.TIMING = _kernels.TIMING, None
+    ms = a.elapsed_time(b) / steps
+    mhc_ms = sum(e0.elapsed_time(e1) for v in timing.values() for e0, e1 in v) / steps
+    if world > 1:
+        t = torch.tensor([ms, mhc_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, mhc_ms = float(t[0]), float(t[1])
+        lt = loss.clone()
+        dist.all_reduce(lt)
+        loss = lt
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Llama-mock mHC fine-tuning step tokens/s (BASELINE config 5)",
+            "value": B * S / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
+            "data": "synthetic", "loss": float(loss),
+            "mhc_kernels_ms_per_step_max_rank": mhc_ms,
+            "config": {"workload": "32 x (RMSNorm, mock attention, RMSNorm, SwiGLU 11008), hidden "
+                                   "4096, vocab 32000, bf16; 128 MHCRewire(n=4, C=1024) around "
+                                   "wq/wk/wv/wo; batch 8 x seq 4096; wrapped weights frozen",
+                       "parallelism": f"sequences sharded over {world} rank(s), one NCCL "
+                                      "all-reduce of the mHC gradients per step"}}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "llama":
+        run_llama(args)
     elif args.workload != "layer":
         run_configs(args)
     else:

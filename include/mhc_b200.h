@@ -208,6 +208,18 @@ MHC_API int mhc_residual_add_agg(const void* x, int x_dtype, const void* res,
                          int out_dtype, float* y_agg, int64_t T, int n, int C,
                          void* stream);
 
+/* Backward of mhc_residual_add_agg (the reference registers no VJP for it):
+ *   dx = dres = d_out + H_pre[i] * d_y,   dH_pre[i] = sum d_y * out_i
+ * out is the forward's output (dtype out_dtype); d_out (same dtype as out)
+ * and d_y ([T, C] fp32) may each be NULL (treated as zero).  dx is written in
+ * dx_dtype; dH_pre is reduced in a fixed order.  Workspace:
+ * mhc_mix_bwd_workspace_bytes(T, n, C). */
+MHC_API int mhc_residual_add_agg_bwd(const void* out, int out_dtype, const void* d_out,
+                                     int dout_dtype, const float* d_y, const float* H_pre,
+                                     void* dx, int dx_dtype, float* dH_pre, int64_t T, int n,
+                                     int C, void* workspace, size_t workspace_bytes,
+                                     void* stream);
+
 #ifdef __cplusplus
 }
 #endif

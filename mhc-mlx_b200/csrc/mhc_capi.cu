@@ -335,4 +335,21 @@ int mhc_residual_add_agg(const void* x, int x_dtype, const void* res, int res_dt
   MHC_TRY_END
 }
 
+int mhc_residual_add_agg_bwd(const void* out, int out_dtype, const void* d_out, int dout_dtype,
+                             const float* d_y, const float* H_pre, void* dx, int dx_dtype,
+                             float* dH_pre, int64_t T, int n, int C, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  MHC_TRY_BEGIN
+  MHC_CHK(check_common(__func__, T, n, C));
+  MHC_CHK(check_dtype(__func__, "out", out_dtype));
+  MHC_CHK(check_dtype(__func__, "dx", dx_dtype));
+  if (d_out) MHC_CHK(check_dtype(__func__, "d_out", dout_dtype));
+  MHC_REQ(H_pre && dH_pre, "%s: NULL H_pre/dH_pre", __func__);
+  MHC_REQ(T == 0 || (out && dx), "%s: NULL out/dx", __func__);
+  return launch_residual_add_agg_bwd(out, out_dtype, d_out, d_out ? dout_dtype : out_dtype, d_y,
+                                     H_pre, dx, dx_dtype, dH_pre, T, n, C, workspace,
+                                     workspace_bytes, as_stream(stream));
+  MHC_TRY_END
+}
+
 }  // extern "C"

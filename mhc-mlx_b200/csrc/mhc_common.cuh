@@ -83,6 +83,12 @@ __device__ __forceinline__ void store_vec(T* __restrict__ p, const float (&v)[V]
       if constexpr (Stream) __stcs(reinterpret_cast<float4*>(p) + k / 4, f);
       else reinterpret_cast<float4*>(p)[k / 4] = f;
     }
+  } else if constexpr (V == 2) {
+    unsigned u;
+    T* h = reinterpret_cast<T*>(&u);
+    h[0] = from_f<T>(v[0]);
+    h[1] = from_f<T>(v[1]);
+    *reinterpret_cast<unsigned*>(p) = u;  // 4-byte aligned
   } else if constexpr (V == 4) {
     uint2 u;
     T* h = reinterpret_cast<T*>(&u);
@@ -90,7 +96,7 @@ __device__ __forceinline__ void store_vec(T* __restrict__ p, const float (&v)[V]
     for (int k = 0; k < 4; ++k) h[k] = from_f<T>(v[k]);
     *reinterpret_cast<uint2*>(p) = u;
   } else {
-    static_assert(V == 8, "16-bit store width is 4 or 8");
+    static_assert(V == 8, "16-bit store width is 2, 4 or 8");
     uint4 u;
     T* h = reinterpret_cast<T*>(&u);
 #pragma unroll

@@ -88,5 +88,9 @@ int launch_prescale_bwd(const void* x, int xdt, const void* d, int ddt, const fl
 int launch_residual_add_agg(const void* x, int xdt, const void* res, int rdt, const float* hpre,
                             void* out, int odt, float* yagg, int64_t T, int n, int C,
                             cudaStream_t st);
+int launch_residual_add_agg_bwd(const void* out, int odt, const void* dout, int ddt,
+                                const float* dy, const float* hpre, void* dx, int dxdt,
+                                float* dhpre, int64_t T, int n, int C, void* ws, size_t ws_bytes,
+                                cudaStream_t st);
 
 }  // namespace mhc

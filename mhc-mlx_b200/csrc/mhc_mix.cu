@@ -412,26 +412,106 @@ k_prescale_bwd(const XT* __restrict__ x, const DT* __restrict__ dout,
   if (blockIdx.x == 0 && threadIdx.x == 0) ws_hdr[0] = gridDim.x;
 }
 
+// ------------------------------------------------- residual add agg bwd --
+// Backward of out = x + res, y_agg = sum_i hpre_i out_i (the reference
+// registers no VJP for residual_add_agg; this adds it):
+//   dx = dres = d_out + hpre_i * d_y;  dH_pre_i = sum d_y * out_i.
+// out is read from the forward's saved output; d_out or d_y may be absent.
+template <int MAXN, bool EXACT, typename OT, typename DT, typename DXT, int VEC>
+__global__ void __launch_bounds__(kMixBD)
+k_residual_bwd(const OT* __restrict__ out, const DT* __restrict__ dout,
+               const float* __restrict__ dy, const float* __restrict__ hpre_g,
+               DXT* __restrict__ dx, int64_t T, int n, int C, float* __restrict__ ws_p,
+               int* __restrict__ ws_hdr) {
+  __shared__ float shpre[MAXN];
+  __shared__ float sacc[(kMixBD / 32) * MAXN];
+  const int nr = EXACT ? MAXN : n;
+  for (int e = threadIdx.x; e < nr; e += blockDim.x) shpre[e] = hpre_g[e];
+  __syncthreads();
+  float aR[MAXN];
+#pragma unroll
+  for (int i = 0; i < MAXN; ++i) aR[i] = 0.f;
+  const int groups = (C + VEC - 1) / VEC;
+  const int64_t items = T * groups;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < items;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = q / groups;
+    const int col = (int)(q - t * groups) * VEC;
+    const int64_t base = t * (int64_t)nr * C + col;
+    float g[VEC];
+    if (dy) load_vec<float, VEC>(dy + t * C + col, g);
+    else
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) g[v] = 0.f;
+    MHC_FOR_N(i) {
+      float o[VEC], d[VEC];
+      if (dout) load_vec<DT, VEC>(dout + base + (int64_t)i * C, d);
+      else
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) d[v] = 0.f;
+      if (dy) {
+        load_vec<OT, VEC>(out + base + (int64_t)i * C, o);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) aR[i] = fmaf(g[v], o[v], aR[i]);
+      }
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) d[v] = fmaf(shpre[i], g[v], d[v]);
+      store_vec<DXT, VEC>(dx + base + (int64_t)i * C, d);
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  MHC_FOR_N(i) {
+    const float v = warp_sum(aR[i]);
+    if (lane == 0) sacc[warp * MAXN + i] = v;
+  }
+  __syncthreads();
+  const int P = nr * nr + 2 * nr;
+  float* pr = ws_p + (size_t)blockIdx.x * P;
+  for (int e = threadIdx.x; e < P; e += blockDim.x) {
+    float s = 0.f;
+    if (e >= nr * nr && e < nr * nr + nr)
+      for (int w = 0; w < nw; ++w) s += sacc[w * MAXN + (e - nr * nr)];
+    pr[e] = s;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) ws_hdr[0] = gridDim.x;
+}
+
 // --------------------------------------------------------------- finalize --
 // One CTA: sums the partial rows (fixed order) into Q (n*n) and R (n), then
 //   mode 0 (mix):      dM = Q
 //   mode 1 (rewire):   dM_ij = hpost_i hpre_j Q_ij, dhpre_j = sum_i hpost_i M_ij Q_ij,
 //                      dhpost_i = R_i + sum_j M_ij hpre_j Q_ij
 //   mode 2 (prescale): dhpre = R
+// The partial rows are summed in 8 interleaved slices per entry (slice r
+// takes rows r, r + 8, ...), then the slices in order: a fixed order for a
+// given row count, with 8x fewer dependent loads per thread.
 __global__ void __launch_bounds__(256)
 k_combine_finalize(const char* __restrict__ ws, int n, const float* __restrict__ M,
                    const float* __restrict__ hpre, const float* __restrict__ hpost, int mode,
                    float* __restrict__ dM, float* __restrict__ dhpre, float* __restrict__ dhpost) {
   __shared__ float sQ[kMaxN * kMaxN + kMaxN];
+  __shared__ float part[8][32];
   const int G = *reinterpret_cast<const int*>(ws);
   const int P = n * n + 2 * n;
   const float* wp = reinterpret_cast<const float*>(ws + WsLayout::params_off());
-  for (int e = threadIdx.x; e < n * n + n; e += blockDim.x) {
+  const int lane = threadIdx.x & 31, r0 = threadIdx.x >> 5;  // blockDim = 256
+  for (int e0 = 0; e0 < n * n + n; e0 += 32) {
+    const int e = e0 + lane;
     float s = 0.f;
-    for (int g = 0; g < G; ++g) s += wp[(size_t)g * P + e];
-    sQ[e] = s;
+    if (e < n * n + n) {
+#pragma unroll 4
+      for (int g = r0; g < G; g += 8) s += wp[(size_t)g * P + e];
+    }
+    part[r0][lane] = s;
+    __syncthreads();
+    if (r0 == 0 && e < n * n + n) {
+      float t = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) t += part[q][lane];
+      sQ[e] = t;
+    }
+    __syncthreads();
   }
-  __syncthreads();
   const float* sR = sQ + n * n;
   if (mode == 0) {
     for (int e = threadIdx.x; e < n * n; e += blockDim.x) dM[e] = sQ[e];
@@ -776,6 +856,68 @@ int launch_residual_add_agg(const void* x, int xdt, const void* res, int rdt, co
     case MHC_BF16: return residual_x<bf16>(x, xdt, res, rdt, hpre, out, odt, yagg, T, n, C, st);
     default: return residual_x<f16>(x, xdt, res, rdt, hpre, out, odt, yagg, T, n, C, st);
   }
+}
+
+// ---- residual add + aggregate: backward -----------------------------------------
+template <typename OT, typename DT, typename DXT>
+static int residual_bwd_t(const void* ov, const void* dv, const float* dy, const float* hpre,
+                          void* dxv, int64_t T, int n, int C, void* ws, cudaStream_t st) {
+  constexpr int VO = VecOf<OT>::value, VD = VecOf<DT>::value, VX = VecOf<DXT>::value;
+  constexpr int V = VO < VD ? (VO < VX ? VO : VX) : (VD < VX ? VD : VX);  // fp32 anywhere -> 4
+  const OT* o = static_cast<const OT*>(ov);
+  const DT* d = static_cast<const DT*>(dv);
+  DXT* dx = static_cast<DXT*>(dxv);
+  char* b = static_cast<char*>(ws);
+  float* wp = reinterpret_cast<float*>(b + WsLayout::params_off());
+  int* hdr = reinterpret_cast<int*>(b);
+  const bool vec = (C % 4 == 0) && (C % V == 0) && all_aligned({ov, dv, dy, dxv});
+  const int cap = mix_rows_cap();
+  const int gv = elem_grid(T * (C / V), cap), g1 = elem_grid(T * C, cap);
+#define MHC_RB(NN, EX, VV, G) \
+  k_residual_bwd<NN, EX, OT, DT, DXT, VV><<<G, kMixBD, 0, st>>>(o, d, dy, hpre, dx, T, n, C, wp, hdr)
+  switch (n) {
+    case 1: if (vec) MHC_RB(1, true, V, gv); else MHC_RB(1, true, 1, g1); break;
+    case 2: if (vec) MHC_RB(2, true, V, gv); else MHC_RB(2, true, 1, g1); break;
+    case 4: if (vec) MHC_RB(4, true, V, gv); else MHC_RB(4, true, 1, g1); break;
+    case 8: if (vec) MHC_RB(8, true, V, gv); else MHC_RB(8, true, 1, g1); break;
+    case 16: MHC_RB(16, true, 1, g1); break;
+    case 32: MHC_RB(32, true, 1, g1); break;
+    default: MHC_RB(64, false, 1, g1); break;
+  }
+#undef MHC_RB
+  return check_launch("residual_add_agg_bwd");
+}
+
+template <typename OT>
+static int residual_bwd_o(const void* o, const void* d, int ddt, const float* dy,
+                          const float* hpre, void* dx, int dxdt, int64_t T, int n, int C,
+                          void* ws, cudaStream_t st, int odt) {
+  // d_out has out's dtype (or is absent); dx has the dtype chosen by the caller
+  if (d && ddt != odt) return set_error(MHC_ERR_UNSUPPORTED, "residual_add_agg_bwd: d_out dtype must equal out dtype");
+  switch (dxdt) {
+    case MHC_F32: return residual_bwd_t<OT, OT, float>(o, d, dy, hpre, dx, T, n, C, ws, st);
+    case MHC_BF16: return residual_bwd_t<OT, OT, bf16>(o, d, dy, hpre, dx, T, n, C, ws, st);
+    default: return residual_bwd_t<OT, OT, f16>(o, d, dy, hpre, dx, T, n, C, ws, st);
+  }
+}
+
+int launch_residual_add_agg_bwd(const void* out, int odt, const void* dout, int ddt,
+                                const float* dy, const float* hpre, void* dx, int dxdt,
+                                float* dhpre, int64_t T, int n, int C, void* ws, size_t ws_bytes,
+                                cudaStream_t st) {
+  const size_t need = mix_ws_bytes(T, n, C);
+  if (!ws || ws_bytes < need)
+    return set_error(MHC_ERR_WORKSPACE, "residual_add_agg_bwd: workspace %zu < %zu bytes", ws_bytes, need);
+  int r;
+  switch (odt) {
+    case MHC_F32: r = residual_bwd_o<float>(out, dout, ddt, dy, hpre, dx, dxdt, T, n, C, ws, st, odt); break;
+    case MHC_BF16: r = residual_bwd_o<bf16>(out, dout, ddt, dy, hpre, dx, dxdt, T, n, C, ws, st, odt); break;
+    default: r = residual_bwd_o<f16>(out, dout, ddt, dy, hpre, dx, dxdt, T, n, C, ws, st, odt); break;
+  }
+  if (r != MHC_OK) return r;
+  k_combine_finalize<<<1, 256, 0, st>>>(static_cast<const char*>(ws), n, nullptr, nullptr, nullptr,
+                                        2, nullptr, dhpre, nullptr);
+  return check_launch("residual_add_agg_bwd_finalize");
 }
 
 }  // namespace mhc

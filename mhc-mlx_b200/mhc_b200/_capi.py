@@ -55,6 +55,8 @@ SIGNATURES: dict[str, tuple] = {
                                  c_size_t, _P]),
     "mhc_residual_add_agg": (c_int, [_P, c_int, _P, c_int, _P, _P, c_int, _P, c_int64, c_int, c_int,
                                      _P]),
+    "mhc_residual_add_agg_bwd": (c_int, [_P, c_int, _P, c_int, _P, _P, _P, c_int, _P, c_int64,
+                                         c_int, c_int, _P, c_size_t, _P]),
 }
 
 _lib = None

@@ -285,3 +285,21 @@ def residual_add_agg(x, res, hpre, out_dtype=F32):
                C.dtype_code(rc.dtype), C.ptr(_f32(hpre)), C.ptr(out), C.dtype_code(out_dtype),
                C.ptr(yagg), T, n, Cc, C.stream_of(xc))
     return out, yagg
+
+
+def residual_add_agg_bwd(out, d_out, d_y, hpre, dx_dtype):
+    """(dx, dH_pre) for out = x + res, y_agg = sum_i hpre_i out_i; d_out or d_y may be None."""
+    dev = C.require_cuda(out, d_out, d_y, hpre)
+    T, n, Cc = out.shape
+    with torch.cuda.device(dev):
+        oc = _c(out)
+        dc = None if d_out is None else _c(d_out.to(oc.dtype))
+        yc = None if d_y is None else _f32(d_y)
+        dx = torch.empty(T, n, Cc, dtype=dx_dtype, device=dev)
+        dpre = torch.empty(n, dtype=F32, device=dev)
+        nb = int(C.query("mhc_mix_bwd_workspace_bytes", T, n, Cc))
+        ws = _ws(nb, dev)
+        _call("mhc_residual_add_agg_bwd", oc, C.ptr(oc), C.dtype_code(oc.dtype), C.ptr(dc),
+              C.dtype_code(oc.dtype), C.ptr(yc), C.ptr(_f32(hpre)), C.ptr(dx),
+              C.dtype_code(dx_dtype), C.ptr(dpre), T, n, Cc, C.ptr(ws), nb, C.stream_of(oc))
+    return dx, dpre

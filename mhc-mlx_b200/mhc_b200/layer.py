@@ -98,15 +98,15 @@ class _RewireCombineFn(torch.autograd.Function):
     """out = H_post (y_inner + M (H_pre x))  (reference layer.py:302-337)."""
 
     @staticmethod
-    def forward(ctx, x, y, M, hpre, hpost):
+    def forward(ctx, x, y, M, hpre, hpost, out_dtype=torch.float32):
         ctx.save_for_backward(x, y, M, hpre, hpost)
-        return K.rewire_fwd(x, y, M, hpre, hpost, torch.float32)
+        return K.rewire_fwd(x, y, M, hpre, hpost, out_dtype)
 
     @staticmethod
     def backward(ctx, dout):
         x, y, M, hpre, hpost = ctx.saved_tensors
         dx, dy, dM, dpre, dpost = K.rewire_bwd(x, y, dout, M, hpre, hpost)
-        return dx, dy, dM, dpre, dpost
+        return dx, dy, dM, dpre, dpost, None
 
 
 # --------------------------------------------------------------- modules --
@@ -277,13 +277,19 @@ class MHCRewire(nn.Module):
     over the last axis split into n streams of C = dims // n channels
     (reference layer.py:438-492)."""
 
-    def __init__(self, inner: nn.Module, dims: int, n: int = 32, **mhc_kwargs):
+    def __init__(self, inner: nn.Module, dims: int, n: int = 32, output_dtype=None,
+                 **mhc_kwargs):
+        """output_dtype: None returns float32 as the reference does; "input"
+        returns x's dtype (the kernel writes it directly, e.g. bf16 models)."""
         super().__init__()
         self.inner = inner
         self.n = n
         self.dims = dims
         if dims % n != 0:
             raise ValueError(f"dims {dims} must be divisible by n={n}")
+        if output_dtype not in (None, "input", torch.float32):
+            raise ValueError('output_dtype must be None, torch.float32 or "input"')
+        self.output_dtype = output_dtype
         self.mhc = MHCLayer(n=n, C=dims // n, **mhc_kwargs)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -301,5 +307,8 @@ class MHCRewire(nn.Module):
             raise ValueError(
                 f"inner module output shape {tuple(y_inner.shape)} must equal its input shape "
                 f"{tuple(x.shape)} (mHC needs a residual-compatible module)")
-        out = _RewireCombineFn.apply(x3, y_inner.reshape(-1, self.n, C), M, hpre, hpost)
+        odt = torch.float32
+        if self.output_dtype == "input" and x.dtype in _HALF:
+            odt = x.dtype
+        out = _RewireCombineFn.apply(x3, y_inner.reshape(-1, self.n, C), M, hpre, hpost, odt)
         return out.reshape(x.shape)

@@ -410,4 +410,23 @@ def residual_add_agg_metal(x: torch.Tensor, res: torch.Tensor, H_pre: torch.Tens
     if x.dtype != res.dtype:
         x, res = x.float(), res.float()
     _maybe_print("mhc_residual_add_agg", verbose)
-    return K.residual_add_agg(x, res, H_pre, out_dtype)
+    return _ResidualAddAggFn.apply(x, res, H_pre, out_dtype)
+
+
+class _ResidualAddAggFn(torch.autograd.Function):
+    """Adds the VJP the reference lacks: dx = dres = d_out + H_pre (x) d_y,
+    dH_pre = sum d_y * out."""
+
+    @staticmethod
+    def forward(ctx, x, res, H_pre, out_dtype):
+        out, y = K.residual_add_agg(x, res, H_pre, out_dtype)
+        ctx.save_for_backward(out, H_pre)
+        ctx.dtypes = (x.dtype, res.dtype)
+        return out, y
+
+    @staticmethod
+    def backward(ctx, d_out, d_y):
+        out, H_pre = ctx.saved_tensors
+        dx, dpre = K.residual_add_agg_bwd(out, d_out, d_y, H_pre, ctx.dtypes[0])
+        dres = dx if ctx.dtypes[1] == ctx.dtypes[0] else dx.to(ctx.dtypes[1])
+        return dx, dres, dpre, None

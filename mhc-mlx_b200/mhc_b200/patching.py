@@ -17,8 +17,10 @@ from .quantized import QuantizedLinear
 
 class AutoPatcher:
     @staticmethod
-    def patch(model: nn.Module, n_streams: int = 32, verbose: bool = True, **mhc_kwargs) -> int:
-        """Patch `model` in place; returns the number of wrapped modules."""
+    def patch(model: nn.Module, n_streams: int = 32, verbose: bool = True, output_dtype=None,
+              **mhc_kwargs) -> int:
+        """Patch `model` in place; returns the number of wrapped modules.
+        output_dtype and mhc_kwargs are passed to every MHCRewire."""
         count = 0
         # snapshot first: the tree is mutated while walking
         modules = list(model.named_modules())
@@ -34,7 +36,8 @@ class AutoPatcher:
             dims = AutoPatcher._get_dims(module)
             if verbose:
                 print(f"[AutoPatcher] Rewiring {name} (dims={dims}, streams={n_streams})")
-            wrapped = MHCRewire(module, dims=dims, n=n_streams, **mhc_kwargs)
+            wrapped = MHCRewire(module, dims=dims, n=n_streams, output_dtype=output_dtype,
+                                **mhc_kwargs)
             p = next(module.parameters(), None) if hasattr(module, "parameters") else None
             if p is not None:
                 wrapped.mhc.to(p.device)

@@ -250,3 +250,26 @@ def test_generic_path_matches_fast_path():
         del os.environ["MHC_B200_GENERIC"]
     for a, b in zip(fast, gen):
         assert rel_err(a, b) < 1e-5
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n,C", [(4, 4096), (4, 1000), (2, 2048), (1, 512)])
+def test_backward_16bit_dout(dt, n, C):
+    """16-bit x and d_out (return_dtype = x's dtype) through the fused
+    backward, including a C that leaves the last CTA columns partly empty."""
+    g = torch.Generator().manual_seed(n * 7 + C)
+    T = 300
+    x = torch.randn(T, n, C, generator=g).to(dt)
+    params = [0.5 * torch.randn(n, generator=g), 0.5 * torch.randn(n, generator=g),
+              torch.randn(n, n, generator=g), 1 + 0.1 * torch.randn(C, generator=g)]
+    d_out = torch.randn(T, n, C, generator=g).to(dt)
+    ref = O.layer_grads(x, *params, d_out.float(), 20, 1e-5, dtype=F64)
+    ref32 = O.layer_grads(x, *params, d_out.float(), 20, 1e-5, dtype=torch.float32)
+    got = _layer_grads(cu(x, dt), [cu(p) for p in params], cu(d_out, dt), 20, 1e-5,
+                       return_dtype=dt)
+    half_tol = 2e-2 if dt == torch.bfloat16 else 5e-3
+    for k, name in enumerate(("out", "dx", "dH_pre", "dH_post", "dH_res", "d_w")):
+        if name in ("out", "dx"):
+            assert rel_err(got[k], ref[k]) < half_tol, (name, rel_err(got[k], ref[k]))
+        else:
+            assert_close_to_reference(name, got[k], ref[k], ref32[k])

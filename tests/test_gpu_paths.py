@@ -310,3 +310,32 @@ def test_full_size_properties(dt):
     for full, a, b in zip(pg, pa, pb):
         assert rel_err(full, a + b) < 1e-5
         assert torch.isfinite(full).all()
+
+
+@pytest.mark.parametrize("B,n,C,dt", [(3, 4, 256, torch.float32), (2, 4, 129, torch.float32),
+                                      (4, 4, 1024, torch.bfloat16), (2, 32, 64, torch.float32),
+                                      (2, 3, 40, torch.float32)])
+def test_residual_add_agg_backward_matches_oracle(B, n, C, dt):
+    """The VJP this build adds to residual_add_agg (the reference has none)."""
+    g = torch.Generator().manual_seed(B * C + n)
+    x = torch.randn(B, n, C, generator=g).to(dt)
+    r = torch.randn(B, n, C, generator=g).to(dt)
+    h = torch.rand(n, generator=g)
+    d_out, d_y = torch.randn(B, n, C, generator=g), torch.randn(B, C, generator=g)
+    leaves = [t.double().requires_grad_(True) for t in (x, r, h)]
+    o_ref, y_ref = O.residual_add_agg_reference(*leaves, dtype=F64)
+    g_ref = torch.autograd.grad((o_ref * d_out.double()).sum() + (y_ref * d_y.double()).sum(),
+                                leaves)
+    xs = [cu(x, dt).requires_grad_(True), cu(r, dt).requires_grad_(True), cu(h).requires_grad_(True)]
+    o, y = mhc_b200.residual_add_agg(*xs)
+    torch.autograd.backward([o, y], [cu(d_out), cu(d_y)])
+    tol = 1e-5 if dt == torch.float32 else 1e-2
+    assert rel_err(xs[0].grad, g_ref[0]) < tol and rel_err(xs[1].grad, g_ref[1]) < tol
+    assert rel_err(xs[2].grad, g_ref[2]) < 1e-5
+    # only one of the two outputs used
+    xs2 = [cu(x, dt).requires_grad_(True), cu(r, dt), cu(h).requires_grad_(True)]
+    _, y2 = mhc_b200.residual_add_agg(*xs2)
+    (y2 * cu(d_y)).sum().backward()
+    g2 = torch.autograd.grad((O.residual_add_agg_reference(*leaves, dtype=F64)[1]
+                              * d_y.double()).sum(), [leaves[0], leaves[2]])
+    assert rel_err(xs2[0].grad, g2[0]) < tol and rel_err(xs2[2].grad, g2[1]) < 1e-5

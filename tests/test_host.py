@@ -218,3 +218,27 @@ def test_reference_import_names():
 
     assert mlx_mhc.__version__ == mhc_mlx.__version__ == mhc_b200.__version__
     assert mlx_mhc.MHCLayer is MHCLayer and mhc_mlx.metal is metal
+
+
+def _llama_mock():
+    import sys as _sys
+    ex = str(Path(__file__).resolve().parent.parent / "mhc-mlx_b200" / "examples")
+    if ex not in _sys.path:
+        _sys.path.insert(0, ex)
+    import llama_mock
+
+    return llama_mock
+
+
+def test_llama_mock_patch_structure():
+    """BASELINE config 5 wiring: the reference's patch rule wraps the square
+    projections (wq, wk, wv, wo) of every block; wrapped weights are frozen."""
+    lm = _llama_mock()
+    model = lm.build(layers=2, dims=64, num_heads=4, mlp_dims=172, vocab=100, n_streams=4,
+                     dtype=torch.float32, device="cpu")
+    wrapped = [n for n, m in model.named_modules() if isinstance(m, MHCRewire)]
+    assert sorted(wrapped) == sorted(f"layers.{b}.attention.{w}" for b in range(2)
+                                     for w in ("wq", "wk", "wv", "wo"))
+    trainable = [n for n, p in model.named_parameters() if p.requires_grad]
+    assert trainable and all(".mhc." in n for n in trainable)
+    assert not isinstance(model.layers[0].feed_forward.w1, MHCRewire)
