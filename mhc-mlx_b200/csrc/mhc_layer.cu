@@ -600,6 +600,7 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
       const float* Ts = tape;
       if (stage_sk) {  // dynamic shared memory holds [tape | logits]
         const size_t tf = (size_t)iters * sk_tape_stride(n);
+#pragma unroll 8
         for (size_t e = tid; e < tf; e += kFinBD) s_fin[e] = tape[e];
         for (int e = tid; e < n * n; e += kFinBD) s_fin[tf + e] = hres_raw[e];
         Ts = s_fin;

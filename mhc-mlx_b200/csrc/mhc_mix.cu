@@ -482,32 +482,36 @@ k_residual_bwd(const OT* __restrict__ out, const DT* __restrict__ dout,
 //   mode 1 (rewire):   dM_ij = hpost_i hpre_j Q_ij, dhpre_j = sum_i hpost_i M_ij Q_ij,
 //                      dhpost_i = R_i + sum_j M_ij hpre_j Q_ij
 //   mode 2 (prescale): dhpre = R
-// The partial rows are summed in 8 interleaved slices per entry (slice r
-// takes rows r, r + 8, ...), then the slices in order: a fixed order for a
-// given row count, with 8x fewer dependent loads per thread.
-__global__ void __launch_bounds__(256)
+// The partial rows are summed in 32 interleaved slices per entry (slice r
+// takes rows r, r + 32, ...), then the slices in order: a fixed order for a
+// given row count, with 32x fewer dependent loads per thread (a one-CTA
+// kernel is a latency chain).
+constexpr int kCFinBD = 1024;
+constexpr int kCFinSlices = kCFinBD / 32;
+
+__global__ void __launch_bounds__(kCFinBD)
 k_combine_finalize(const char* __restrict__ ws, int n, const float* __restrict__ M,
                    const float* __restrict__ hpre, const float* __restrict__ hpost, int mode,
                    float* __restrict__ dM, float* __restrict__ dhpre, float* __restrict__ dhpost) {
   __shared__ float sQ[kMaxN * kMaxN + kMaxN];
-  __shared__ float part[8][32];
+  __shared__ float part[kCFinSlices][32];
   const int G = *reinterpret_cast<const int*>(ws);
   const int P = n * n + 2 * n;
   const float* wp = reinterpret_cast<const float*>(ws + WsLayout::params_off());
-  const int lane = threadIdx.x & 31, r0 = threadIdx.x >> 5;  // blockDim = 256
+  const int lane = threadIdx.x & 31, r0 = threadIdx.x >> 5;
   for (int e0 = 0; e0 < n * n + n; e0 += 32) {
     const int e = e0 + lane;
     float s = 0.f;
     if (e < n * n + n) {
 #pragma unroll 4
-      for (int g = r0; g < G; g += 8) s += wp[(size_t)g * P + e];
+      for (int g = r0; g < G; g += kCFinSlices) s += wp[(size_t)g * P + e];
     }
     part[r0][lane] = s;
     __syncthreads();
     if (r0 == 0 && e < n * n + n) {
       float t = 0.f;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) t += part[q][lane];
+      for (int q = 0; q < kCFinSlices; ++q) t += part[q][lane];
       sQ[e] = t;
     }
     __syncthreads();
@@ -696,7 +700,7 @@ static int combine_bwd(const void* x, int xdt, const void* y, int ydt, const voi
     default: r = combine_bwd_x<f16>(x, xdt, y, ydt, d, ddt, M, hpre, hpost, dx, dy, T, n, C, ws, st); break;
   }
   if (r != MHC_OK) return r;
-  k_combine_finalize<<<1, 256, 0, st>>>(static_cast<const char*>(ws), n, M, hpre, hpost, mode,
+  k_combine_finalize<<<1, kCFinBD, 0, st>>>(static_cast<const char*>(ws), n, M, hpre, hpost, mode,
                                         dM, dhpre, dhpost);
   return check_launch("combine_finalize");
 }
@@ -807,7 +811,7 @@ int launch_prescale_bwd(const void* x, int xdt, const void* d, int ddt, const fl
       break;
   }
   if (r != MHC_OK) return r;
-  k_combine_finalize<<<1, 256, 0, st>>>(static_cast<const char*>(ws), n, nullptr, nullptr, nullptr,
+  k_combine_finalize<<<1, kCFinBD, 0, st>>>(static_cast<const char*>(ws), n, nullptr, nullptr, nullptr,
                                         2, nullptr, dhpre, nullptr);
   return check_launch("prescale_finalize");
 }
@@ -915,7 +919,7 @@ int launch_residual_add_agg_bwd(const void* out, int odt, const void* dout, int 
     default: r = residual_bwd_o<f16>(out, dout, ddt, dy, hpre, dx, dxdt, T, n, C, ws, st, odt); break;
   }
   if (r != MHC_OK) return r;
-  k_combine_finalize<<<1, 256, 0, st>>>(static_cast<const char*>(ws), n, nullptr, nullptr, nullptr,
+  k_combine_finalize<<<1, kCFinBD, 0, st>>>(static_cast<const char*>(ws), n, nullptr, nullptr, nullptr,
                                         2, nullptr, dhpre, nullptr);
   return check_launch("residual_add_agg_bwd_finalize");
 }

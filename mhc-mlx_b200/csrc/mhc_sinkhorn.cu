@@ -59,6 +59,7 @@ k_params_bwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost
       const float* Ts = tape;
       if (stage) {
         const size_t tf = (size_t)iters * sk_tape_stride(n);
+#pragma unroll 8
         for (size_t e = tid; e < tf; e += blockDim.x) s_stage_sk[e] = tape[e];
         for (int e = tid; e < n * n; e += blockDim.x) s_stage_sk[tf + e] = hres_raw[e];
         Ts = s_stage_sk;

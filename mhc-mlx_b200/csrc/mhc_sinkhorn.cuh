@@ -89,6 +89,7 @@ __device__ inline SkTape sk_stage_tape(const float* __restrict__ tape, int n, in
                                        float* smem) {
   const int nn = n * n, ld = sk_ld(n);
   const size_t gs = sk_tape_stride(n), ss = (size_t)n * ld + 2 * n;
+#pragma unroll 8
   for (size_t e = threadIdx.x; e < (size_t)iters * gs; e += blockDim.x) {
     const size_t k = e / gs, r = e - k * gs;
     const size_t dst = r < (size_t)nn ? (r / n) * ld + r % n : (size_t)n * ld + (r - nn);
