@@ -7,6 +7,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "mhc_b200.h"
 
 namespace mhc {
@@ -44,6 +46,26 @@ __device__ __forceinline__ uint4 ldu4(const uint4* p) {
   else return __ldg(p);
 }
 
+// Unpack one 16-byte chunk holding V elements of T into fp32.
+// bf16 is the high half of an fp32, so each 32-bit word gives its two values
+// with one shift (element 2k, the low half) and one mask (element 2k + 1).
+template <typename T, int V>
+__device__ __forceinline__ void unpack16(const uint4& u, float (&o)[V]) {
+  static_assert(V * sizeof(T) == 16, "one 16-byte chunk");
+  if constexpr (std::is_same<T, bf16>::value) {
+    const unsigned wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      o[2 * k] = __uint_as_float(wd[k] << 16);
+      o[2 * k + 1] = __uint_as_float(wd[k] & 0xffff0000u);
+    }
+  } else {
+    const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int k = 0; k < V; ++k) o[k] = to_f(h[k]);
+  }
+}
+
 template <typename T, int V, bool Stream = true>
 __device__ __forceinline__ void load_vec(const T* __restrict__ p, float (&o)[V]) {
   if constexpr (V == 1) {
@@ -62,10 +84,7 @@ __device__ __forceinline__ void load_vec(const T* __restrict__ p, float (&o)[V])
     for (int k = 0; k < 4; ++k) o[k] = to_f(h[k]);
   } else {
     static_assert(V == 8, "16-bit vector width is 4 or 8");
-    uint4 u = ldu4<Stream>(reinterpret_cast<const uint4*>(p));
-    const T* h = reinterpret_cast<const T*>(&u);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) o[k] = to_f(h[k]);
+    unpack16<T, 8>(ldu4<Stream>(reinterpret_cast<const uint4*>(p)), o);
   }
 }
 
@@ -116,14 +135,43 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+// Wait until at most K of this thread's most recent commit groups are pending.
+template <int K>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(K) : "memory");
+}
 
-// Unpack one 16-byte chunk holding V elements of T into fp32.
-template <typename T, int V>
-__device__ __forceinline__ void unpack16(const uint4& u, float (&o)[V]) {
-  static_assert(V * sizeof(T) == 16, "one 16-byte chunk");
-  const T* h = reinterpret_cast<const T*>(&u);
-#pragma unroll
-  for (int k = 0; k < V; ++k) o[k] = to_f(h[k]);
+// ------------------------------------------------ warp-level tensor cores --
+// ldmatrix.x4: lanes 8q..8q+7 give the row addresses (16 bytes each) of 8x8
+// b16 matrix q; r[q] receives this lane's pair of that matrix: row lane/4,
+// elements 2*(lane%4) and 2*(lane%4)+1.
+__device__ __forceinline__ void ldmatrix_x4(unsigned (&r)[4], const void* smem_row) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem_row));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(s)
+               : "memory");
+}
+
+// D += A * B for a 16x16 (row) A and a 16x8 (col) B of 16-bit T, fp32
+// accumulators.  Products of 16-bit values are exact in fp32.
+template <typename T>
+__device__ __forceinline__ void mma_16816(float (&d)[4], const unsigned (&a)[4], unsigned b0,
+                                          unsigned b1) {
+  if constexpr (sizeof(T) == 2 && std::is_same<T, bf16>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    static_assert(std::is_same<T, f16>::value, "16-bit operands");
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
 }
 
 // Plain fp32 vector load for parameter vectors (w) of width V.

@@ -387,6 +387,227 @@ k_bwd_fast(const XT* __restrict__ x, const DT* __restrict__ dout, const float* _
   if (blockIdx.x == 0 && threadIdx.x == 0) ws_hdr[0] = gridDim.x;
 }
 
+// Full-row backward for 16-bit rows: x, d_out and dx share one 16-bit type T
+// and C = 8 * BD, so thread t owns columns 8t..8t+7 of every stream with no
+// tail.  Same math and partial-row output as k_bwd_fast; the differences:
+//   - NBUF = 2 double-buffers the staging slots: token t + G's x and d_out
+//     rows are requested (cp.async, 16 bytes per thread and row) before token
+//     t is processed.  NBUF = 1 refills the single buffer once the first pass
+//     has read it, as k_bwd_fast does;
+//   - y and dyn of the first pass stay in registers for the second; w is
+//     staged once in shared memory and M is kept transposed there, so the
+//     per-token parameter reads are shared-memory vector loads;
+//   - MMA (n = 4): dM = sum d x^T runs on the tensor cores from the staged
+//     rows.  Per warp and 64-column group, ldmatrix gives A = d_out rows
+//     (stream i, 16-column block b) and B = x columns (stream j, block b'),
+//     and two m16n8k16 products accumulate D[(i,b)][(j,b')]; only the
+//     b == b' entries are dM partials (the others are never read).  Rows of A
+//     and columns of B are ordered, and stream rows padded by one 16-byte
+//     chunk, so that each 8x8 matrix load touches 8 distinct bank groups.
+//     bf16 x bf16 (or f16 x f16) products are exact in fp32.
+// Dynamic shared layout: w as [2][BD] float4 (thread t's columns 8t..8t+3
+// and 8t+4..8t+7, conflict-free), then [NBUF][x rows N | d_out rows N][SB
+// chunks of 16 bytes].
+template <int N, typename T, int BD, bool MMA, int NBUF>
+__global__ void __launch_bounds__(BD, 512 / BD)
+k_bwd_rows(const T* __restrict__ x, const T* __restrict__ dout, const float* __restrict__ Mg,
+           const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
+           const float* __restrict__ w, T* __restrict__ dx, int64_t T_, float eps,
+           float* __restrict__ ws_p, float* __restrict__ ws_c, int* __restrict__ ws_hdr) {
+  static_assert(sizeof(T) == 2, "16-bit rows");
+  static_assert(!MMA || N == 4, "the tensor-core dM layout is for n = 4");
+  static_assert(NBUF == 1 || NBUF == 2, "one or two staging buffers");
+  constexpr int C = 8 * BD, P = N * N + 2 * N, NW = BD / 32;
+  constexpr int SB = BD + (MMA ? 1 : 0);  // chunks per staged stream row
+  constexpr int BUF = 2 * N * SB;         // chunks per buffer
+  constexpr int64_t RS = (int64_t)N * C;  // elements per token
+  extern __shared__ uint4 s_dyn[];
+  float4* s_w = reinterpret_cast<float4*>(s_dyn);
+  uint4* s_stage = s_dyn + 2 * BD;
+  __shared__ __align__(16) float sMT[N * N];  // sMT[j * N + i] = M[i][j]
+  __shared__ float red[2][64];
+  __shared__ float sacc[NW * P];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < N * N; e += BD) sMT[(e % N) * N + e / N] = Mg[e];
+  s_w[tid] = __ldg(reinterpret_cast<const float4*>(w) + 2 * tid);
+  s_w[BD + tid] = __ldg(reinterpret_cast<const float4*>(w) + 2 * tid + 1);
+  float hpre[N], hpost[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) { hpre[i] = __ldg(hpre_g + i); hpost[i] = __ldg(hpost_g + i); }
+  __syncthreads();
+  auto load_w = [&](float (&wv)[8]) {
+    const float4 a = s_w[tid], b = s_w[BD + tid];
+    wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
+    wv[4] = b.x; wv[5] = b.y; wv[6] = b.z; wv[7] = b.w;
+  };
+
+  const int col = tid * 8;
+  float aM[MMA ? 1 : N][MMA ? 1 : N], aPre[N], aPost[N], aW[8];
+  float accA[4] = {0.f, 0.f, 0.f, 0.f}, accB[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < N; ++i) { aPre[i] = 0.f; aPost[i] = 0.f; }
+#pragma unroll
+  for (int i = 0; i < (MMA ? 1 : N); ++i)
+#pragma unroll
+    for (int j = 0; j < (MMA ? 1 : N); ++j) aM[i][j] = 0.f;
+#pragma unroll
+  for (int v = 0; v < 8; ++v) aW[v] = 0.f;
+
+  auto prefetch = [&](int64_t tp, int buf) {
+    uint4* s = s_stage + buf * BUF + tid;
+    const T* xs = x + tp * RS + col;
+    const T* ds = dout + tp * RS + col;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      cp_async16(s + i * SB, xs + (int64_t)i * C);
+      cp_async16(s + (N + i) * SB, ds + (int64_t)i * C);
+    }
+  };
+  const int64_t G = gridDim.x;
+  if ((int64_t)blockIdx.x < T_) prefetch(blockIdx.x, 0);
+  cp_async_commit();
+  int par = 0, buf = 0;
+  for (int64_t t = blockIdx.x; t < T_; t += G) {
+    if constexpr (NBUF == 2) {
+      // the other buffer was last read before the previous token's barrier
+      if (t + G < T_) prefetch(t + G, buf ^ 1);
+      cp_async_commit();
+      cp_async_wait_group<1>();
+    } else {
+      cp_async_wait_all();
+    }
+    const uint4* sb = s_stage + buf * BUF;
+    if constexpr (MMA) {
+      __syncwarp();  // every lane's chunks of this buffer are visible to the warp
+      const int q = lane >> 3, rr = lane & 7, wbase = tid & ~31;
+      // A: row (stream rr&3, block 2*(rr>>2) + (q&1)), k-half q>>1
+      // B: col (stream rr&3, block 2*(rr>>2) + (q>>1)), k-half q&1
+      const uint4* pa = sb + (N + (rr & 3)) * SB + wbase + 2 * (2 * (rr >> 2) + (q & 1)) + (q >> 1);
+      const uint4* pb = sb + (rr & 3) * SB + wbase + 2 * (2 * (rr >> 2) + (q >> 1)) + (q & 1);
+#pragma unroll
+      for (int g64 = 0; g64 < 4; ++g64) {
+        unsigned a[4], b[4];
+        ldmatrix_x4(a, pa + 8 * g64);
+        ldmatrix_x4(b, pb + 8 * g64);
+        mma_16816<T>(accA, a, b[0], b[1]);
+        mma_16816<T>(accB, a, b[2], b[3]);
+      }
+    }
+    float xr[N][8], dr[N][8];
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      unpack16<T, 8>(sb[i * SB + tid], xr[i]);
+      unpack16<T, 8>(sb[(N + i) * SB + tid], dr[i]);
+    }
+    if constexpr (NBUF == 1) {
+      if constexpr (MMA) __syncwarp();  // the warp's ldmatrix reads precede the refill
+      if (t + G < T_) prefetch(t + G, 0);
+      cp_async_commit();
+    } else {
+      buf ^= 1;
+    }
+    float yk[8], dk[8], ss = 0.f, pd = 0.f;
+    {
+      float wv[8];
+      load_w(wv);
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        float y = 0.f, dyn = 0.f;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          y = fmaf(hpre[i], xr[i][v], y);
+          dyn = fmaf(hpost[i], dr[i][v], dyn);
+        }
+        yk[v] = y;
+        dk[v] = dyn;
+        ss = fmaf(y, y, ss);
+        pd = fmaf(dyn * wv[v], y, pd);
+      }
+    }
+    const float2 red2 = block_sum2(ss, pd, red[par]);
+    par ^= 1;
+    const float inv = inv_rms(red2.x, C, eps);
+    const float k2 = (red2.y * (inv * inv * inv)) * (1.0f / (float)C);
+
+    float dya[8];
+    {
+      float wv[8];
+      load_w(wv);
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        const float yi = yk[v] * inv;
+        const float yn = yi * wv[v];
+        aW[v] = fmaf(dk[v], yi, aW[v]);
+        const float g = (dk[v] * wv[v]) * inv - k2 * yk[v];
+        dya[v] = g;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          aPost[i] = fmaf(dr[i][v], yn, aPost[i]);
+          aPre[i] = fmaf(g, xr[i][v], aPre[i]);
+          if constexpr (!MMA) {
+#pragma unroll
+            for (int j = 0; j < N; ++j) aM[i][j] = fmaf(dr[i][v], xr[j][v], aM[i][j]);
+          }
+        }
+      }
+    }
+    T* dxt = dx + t * RS + col;
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      float mc[N];
+#pragma unroll
+      for (int i = 0; i < N; ++i) mc[i] = sMT[j * N + i];
+      float o[8];
+#pragma unroll
+      for (int v = 0; v < 8; ++v) o[v] = hpre[j] * dya[v];
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+#pragma unroll
+        for (int v = 0; v < 8; ++v) o[v] = fmaf(mc[i], dr[i][v], o[v]);
+      store_vec<T, 8>(dxt + (int64_t)j * C, o);
+    }
+  }
+  cp_async_wait_all();  // only empty groups can remain; nothing is left in flight at exit
+
+  // ---- per-CTA partials: fixed-order warp reductions + ordered warp sum ----
+  if constexpr (MMA) {
+    // lane (g, t) holds D[g][2t..2t+1] (accA) and D[g+8][2t..2t+1] (accB):
+    // dM partials where (g < 4) == (t < 2), for i = g & 3, j = (2t + e) & 3;
+    // lane (g + 4, t + 2) = lane + 18 holds the other half of the same (i, j)
+    float v0 = accA[0] + accB[2], v1 = accA[1] + accB[3];
+    v0 += __shfl_down_sync(0xffffffffu, v0, 18);
+    v1 += __shfl_down_sync(0xffffffffu, v1, 18);
+    const int g = lane >> 2, tq = lane & 3;
+    if (g < 4 && tq < 2) {
+      sacc[warp * P + g * N + 2 * tq] = v0;
+      sacc[warp * P + g * N + 2 * tq + 1] = v1;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        const float v = warp_sum(aM[i][j]);
+        if (lane == 0) sacc[warp * P + i * N + j] = v;
+      }
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const float a = warp_sum(aPre[i]);
+    const float b = warp_sum(aPost[i]);
+    if (lane == 0) { sacc[warp * P + N * N + i] = a; sacc[warp * P + N * N + N + i] = b; }
+  }
+  __syncthreads();
+  for (int e = tid; e < P; e += BD) {
+    float s = 0.f;
+#pragma unroll 4
+    for (int q = 0; q < NW; ++q) s += sacc[q * P + e];
+    ws_p[(size_t)blockIdx.x * P + e] = s;
+  }
+  store_vec<float, 8, false>(ws_c + (size_t)blockIdx.x * C + col, aW);
+  if (blockIdx.x == 0 && tid == 0) ws_hdr[0] = gridDim.x;
+}
+
 // Generic backward: any n <= 64, any C.  Pass 1 reduces ss and pd for the
 // row; pass 2 walks the row in tiles of blockDim columns: each thread stages
 // its column of x and d_out in shared memory (plus two extra rows: y inv w
@@ -801,6 +1022,50 @@ static BwdPtrs ws_ptrs(void* ws, int G, int n) {
           reinterpret_cast<float*>(b + WsLayout::cols_off(G, n)), reinterpret_cast<int*>(b)};
 }
 
+// Full-row 16-bit backward (k_bwd_rows) for C = 8 * BD, BD in {128, 256,
+// 512}.  Returns -1 when the shape has no instantiation.
+template <int N, typename T, int BD>
+static int launch_bwd_rows(const T* x, const T* d, const float* M, const float* hpre,
+                           const float* hpost, const float* w, T* dx, int64_t T_, float eps,
+                           void* ws, cudaStream_t st) {
+  constexpr bool kMma = N == 4;
+  auto go = [&](auto kern, size_t dyn) -> int {
+    cudaError_t e = allow_dyn_smem(kern, dyn);
+    if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_bwd: %s", cudaGetErrorString(e));
+    const int G = persistent_grid(kern, BD, dyn, T_, max_partial_rows(T_));
+    BwdPtrs p = ws_ptrs(ws, G, N);
+    kern<<<G, BD, dyn, st>>>(x, d, M, hpre, hpost, w, dx, T_, eps, p.p, p.c, p.hdr);
+    return check_launch("mhc_bwd");
+  };
+  // w (2 float4 per thread), then NBUF buffers of 2N staged rows
+  const size_t wb = (size_t)BD * 32, row = 16;
+  const bool two = env_int("MHC_B200_NBUF", 1) == 2;
+  if constexpr (kMma) {
+    if (env_int("MHC_B200_MMA", 1)) {
+      const size_t rows = (size_t)2 * N * (BD + 1) * row;
+      if (two) return go(k_bwd_rows<N, T, BD, true, 2>, wb + 2 * rows);
+      return go(k_bwd_rows<N, T, BD, true, 1>, wb + rows);
+    }
+  }
+  const size_t rows = (size_t)2 * N * BD * row;
+  if (two) return go(k_bwd_rows<N, T, BD, false, 2>, wb + 2 * rows);
+  return go(k_bwd_rows<N, T, BD, false, 1>, wb + rows);
+}
+
+template <int N, typename T>
+static int bwd_rows(const T* x, const T* d, const float* M, const float* hpre, const float* hpost,
+                    const float* w, T* dx, int64_t T_, int C, float eps, void* ws,
+                    cudaStream_t st) {
+  if (!env_int("MHC_B200_FULL", 1) || !env_int("MHC_B200_PIPE", 1)) return -1;
+  if (!(aligned16(x) && aligned16(d) && aligned16(dx) && aligned16(w))) return -1;
+  switch (C) {
+    case 1024: return launch_bwd_rows<N, T, 128>(x, d, M, hpre, hpost, w, dx, T_, eps, ws, st);
+    case 2048: return launch_bwd_rows<N, T, 256>(x, d, M, hpre, hpost, w, dx, T_, eps, ws, st);
+    case 4096: return launch_bwd_rows<N, T, 512>(x, d, M, hpre, hpost, w, dx, T_, eps, ws, st);
+    default: return -1;
+  }
+}
+
 template <int N, typename XT, typename DT, typename DXT, int VEC, int ITEMS>
 static int try_bwd_items(const XT* x, const DT* d, const float* M, const float* hpre,
                          const float* hpost, const float* w, DXT* dx, int64_t T, int C, float eps,
@@ -861,6 +1126,11 @@ static int bwd_fast(const XT* x, const DT* d, const float* M, const float* hpre,
   constexpr int VX = VecOf<XT>::value, VD = VecOf<DT>::value;
   // one vector width for both streams: the wider element count is used
   // only if both dtypes share it (f32/f32 -> 4, 16-bit/16-bit -> 8)
+  if constexpr (sizeof(XT) == 2 && std::is_same<XT, DT>::value && std::is_same<XT, DXT>::value &&
+                N <= 4) {
+    const int r = bwd_rows<N, XT>(x, d, M, hpre, hpost, w, dx, T, C, eps, ws, st);
+    if (r >= 0) return r;
+  }
   if constexpr (VX == VD && VecOf<DXT>::value == VX) {
     const bool vec_ok = (C % VX == 0) && aligned16(x) && aligned16(d) && aligned16(dx) &&
                         aligned16(w);

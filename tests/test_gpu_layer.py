@@ -253,10 +253,12 @@ def test_generic_path_matches_fast_path():
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("n,C", [(4, 4096), (4, 1000), (2, 2048), (1, 512)])
+@pytest.mark.parametrize("n,C", [(4, 4096), (4, 2048), (4, 1024), (4, 1000), (2, 2048), (1, 512)])
 def test_backward_16bit_dout(dt, n, C):
     """16-bit x and d_out (return_dtype = x's dtype) through the fused
-    backward, including a C that leaves the last CTA columns partly empty."""
+    backward, including a C that leaves the last CTA columns partly empty.
+    n = 4 with C = 1024 / 2048 / 4096 runs the full-row kernel with the
+    tensor-core dM (block sizes 128 / 256 / 512)."""
     g = torch.Generator().manual_seed(n * 7 + C)
     T = 300
     x = torch.randn(T, n, C, generator=g).to(dt)
