@@ -6,7 +6,9 @@
 // metal.py:1610-1616).
 #include <cstdarg>
 #include <cstdio>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "mhc_internal.h"
 
@@ -56,6 +58,36 @@ int max_smem_optin() {
   const int d = current_device();
   std::call_once(g_once[d], query, d);
   return g_smem[d];
+}
+
+// Launch-attribute caches keyed on (kernel, device[, block, shared bytes]).
+namespace {
+std::mutex g_attr_mu;
+std::map<std::pair<const void*, int>, size_t> g_dyn;  // largest dynamic smem allowed so far
+std::map<std::tuple<const void*, int, int, size_t>, int> g_occ;  // resident blocks per SM
+}  // namespace
+
+bool dyn_smem_cached(const void* kernel, size_t dyn) {
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  auto it = g_dyn.find({kernel, current_device()});
+  return it != g_dyn.end() && it->second >= dyn;
+}
+
+void dyn_smem_remember(const void* kernel, size_t dyn) {
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  size_t& v = g_dyn[{kernel, current_device()}];
+  if (dyn > v) v = dyn;
+}
+
+int occupancy_cached(const void* kernel, int threads, size_t smem) {
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  auto it = g_occ.find({kernel, current_device(), threads, smem});
+  return it == g_occ.end() ? -1 : it->second;
+}
+
+void occupancy_remember(const void* kernel, int threads, size_t smem, int per_sm) {
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  g_occ[{kernel, current_device(), threads, smem}] = per_sm;
 }
 
 }  // namespace mhc

@@ -22,13 +22,38 @@ int max_smem_optin();
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Launch-attribute caches (mhc_capi.cu): the attribute call and the
+// occupancy query cost microseconds of host time, so each is made once per
+// kernel, device and shape and remembered.  Thread-safe.
+bool dyn_smem_cached(const void* kernel, size_t dyn);
+void dyn_smem_remember(const void* kernel, size_t dyn);
+int occupancy_cached(const void* kernel, int threads, size_t smem);  // -1: unknown
+void occupancy_remember(const void* kernel, int threads, size_t smem, int per_sm);
+
 // Allow `dyn` bytes of dynamic shared memory for `kernel`.  Needed whenever
-// static + dynamic shared memory exceeds the 48 KB default, so it is set for
-// every launch that uses dynamic shared memory.
+// static + dynamic shared memory exceeds the 48 KB default; the attribute is
+// per kernel and device, so it is set again only when a launch needs more.
 template <typename K>
 inline cudaError_t allow_dyn_smem(K kernel, size_t dyn) {
   if (dyn == 0) return cudaSuccess;
-  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+  const void* k = reinterpret_cast<const void*>(kernel);
+  if (dyn_smem_cached(k, dyn)) return cudaSuccess;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+  if (e == cudaSuccess) dyn_smem_remember(k, dyn);
+  return e;
+}
+
+// Resident blocks per SM of `kernel` at this block size and shared memory.
+template <typename K>
+inline int blocks_per_sm(K kernel, int threads, size_t smem) {
+  const void* k = reinterpret_cast<const void*>(kernel);
+  int per_sm = occupancy_cached(k, threads, smem);
+  if (per_sm >= 0) return per_sm;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess)
+    return 1;  // not remembered: the query is retried on the next launch
+  occupancy_remember(k, threads, smem, per_sm);
+  return per_sm;
 }
 
 inline int dtype_size(int dt) { return dt == MHC_F32 ? 4 : 2; }

@@ -866,10 +866,8 @@ int max_partial_rows(int64_t T) {
 
 template <typename K>
 static int persistent_grid(K kernel, int threads, size_t smem, int64_t T, int cap) {
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
-      per_sm < 1)
-    per_sm = 1;
+  int per_sm = blocks_per_sm(kernel, threads, smem);
+  if (per_sm < 1) per_sm = 1;
   int64_t g = (int64_t)per_sm * sm_count();
   if (g > cap) g = cap;
   if (g > T) g = T;

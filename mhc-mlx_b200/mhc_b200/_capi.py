@@ -137,11 +137,19 @@ def dtype_code(dt: torch.dtype) -> int:
 
 
 def ptr(t: torch.Tensor | None):
-    return None if t is None else c_void_p(t.data_ptr())
+    """Device address as a plain int (argtypes convert it to void*); None -> NULL."""
+    return None if t is None else t.data_ptr()
 
 
-def stream_of(t: torch.Tensor) -> c_void_p:
-    return c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+# The raw current-stream handle without building a torch Stream object (a
+# few microseconds per call on the B=1 path); the public API otherwise.
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def stream_of(t: torch.Tensor) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(t.device.index)
+    return torch.cuda.current_stream(t.device).cuda_stream
 
 
 def require_cuda(*ts: torch.Tensor | None) -> torch.device:

@@ -9,6 +9,7 @@ only contiguity, dtype and device are normalised here.
 from __future__ import annotations
 
 import contextlib
+import functools
 
 import torch
 
@@ -56,13 +57,36 @@ def _io(t: torch.Tensor) -> torch.Tensor:
     return _c(t)
 
 
+_NULL = contextlib.nullcontext()
+
+
+def _on(dev: torch.device):
+    """Make `dev` current around a C-ABI call (kernels launch on the current
+    device); a no-op context when it already is."""
+    if dev.index is None or dev.index == torch.cuda.current_device():
+        return _NULL
+    return torch.cuda.device(dev)
+
+
 def _ws(nbytes: int, dev: torch.device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=dev)
 
 
 # ------------------------------------------------------------ parameters --
+@functools.lru_cache(maxsize=256)
 def tape_floats(n: int, iters: int) -> int:
     return int(C.query("mhc_sinkhorn_tape_floats", n, iters))
+
+
+@functools.lru_cache(maxsize=4096)
+def _ws_query(name: str, device_index: int, *args) -> int:
+    """Workspace sizes depend on the shape and on the device's SM count (the
+    current device, made current by the caller), hence the device key."""
+    return int(C.query(name, *args))
+
+
+def _ws_bytes(name: str, dev: torch.device, *args) -> int:
+    return _ws_query(name, dev.index if dev.index is not None else -1, *args)
 
 
 def params_fwd(H_pre_raw, H_post_raw, H_res_raw, iters: int, eps: float, want_tape: bool):
@@ -70,7 +94,7 @@ def params_fwd(H_pre_raw, H_post_raw, H_res_raw, iters: int, eps: float, want_ta
     ref = next(t for t in (H_res_raw, H_pre_raw, H_post_raw) if t is not None)
     dev = C.require_cuda(H_pre_raw, H_post_raw, H_res_raw)
     n = ref.shape[0]
-    with torch.cuda.device(dev):
+    with _on(dev):
         pre = _f32(H_pre_raw) if H_pre_raw is not None else None
         post = _f32(H_post_raw) if H_post_raw is not None else None
         res = _f32(H_res_raw) if H_res_raw is not None else None
@@ -90,7 +114,7 @@ def params_bwd(H_pre_raw, H_post_raw, H_res_raw, tape, iters: int, eps: float, d
     ref = next(t for t in (H_res_raw, H_pre_raw, H_post_raw) if t is not None)
     dev = C.require_cuda(H_pre_raw, H_post_raw, H_res_raw)
     n = ref.shape[0]
-    with torch.cuda.device(dev):
+    with _on(dev):
         pre = _f32(H_pre_raw) if (H_pre_raw is not None and dhpre is not None) else None
         post = _f32(H_post_raw) if (H_post_raw is not None and dhpost is not None) else None
         res = _f32(H_res_raw) if (H_res_raw is not None and dM is not None) else None
@@ -108,7 +132,7 @@ def params_bwd(H_pre_raw, H_post_raw, H_res_raw, tape, iters: int, eps: float, d
 def sinkhorn_batched_fwd(H: torch.Tensor, iters: int, eps: float) -> torch.Tensor:
     dev = C.require_cuda(H)
     B, n, _ = H.shape
-    with torch.cuda.device(dev):
+    with _on(dev):
         Hc = _f32(H)
         M = torch.empty(B, n, n, dtype=F32, device=dev)
         _call("mhc_sinkhorn_batched_fwd", Hc, C.ptr(Hc), B, n, int(iters), float(eps), C.ptr(M),
@@ -119,10 +143,10 @@ def sinkhorn_batched_fwd(H: torch.Tensor, iters: int, eps: float) -> torch.Tenso
 def sinkhorn_batched_bwd(H: torch.Tensor, dM: torch.Tensor, iters: int, eps: float) -> torch.Tensor:
     dev = C.require_cuda(H, dM)
     B, n, _ = H.shape
-    with torch.cuda.device(dev):
+    with _on(dev):
         Hc, dMc = _f32(H), _f32(dM)
         dH = torch.empty(B, n, n, dtype=F32, device=dev)
-        nb = int(C.query("mhc_sinkhorn_batched_workspace_bytes", B, n, int(iters)))
+        nb = _ws_bytes("mhc_sinkhorn_batched_workspace_bytes", dev, B, n, int(iters))
         ws = _ws(nb, dev) if nb else None
         _call("mhc_sinkhorn_batched_bwd", Hc, C.ptr(Hc), C.ptr(dMc), B, n, int(iters), float(eps),
                C.ptr(dH), C.ptr(ws), nb, C.stream_of(Hc))
@@ -133,7 +157,7 @@ def sinkhorn_batched_bwd(H: torch.Tensor, dM: torch.Tensor, iters: int, eps: flo
 def layer_fwd(x, M, hpre, hpost, w, eps: float, out_dtype: torch.dtype) -> torch.Tensor:
     dev = C.require_cuda(x, M, hpre, hpost, w)
     T, n, Cc = x.shape
-    with torch.cuda.device(dev):
+    with _on(dev):
         xc = _io(x)
         out = torch.empty(T, n, Cc, dtype=out_dtype, device=dev)
         args = (C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(_f32(M)), C.ptr(_f32(hpre)),
@@ -150,11 +174,11 @@ def layer_bwd(x, dout, M, hpre, hpost, w, eps: float, raw=None):
     finalize launch."""
     dev = C.require_cuda(x, dout, M, hpre, hpost, w)
     T, n, Cc = x.shape
-    with torch.cuda.device(dev):
+    with _on(dev):
         xc = _io(x)
         dc = _c(dout) if dout.dtype in (F32, xc.dtype) else dout.float().contiguous()
         dx = torch.empty(T, n, Cc, dtype=xc.dtype, device=dev)
-        nb = int(C.query("mhc_bwd_workspace_bytes", T, n, Cc))
+        nb = _ws_bytes("mhc_bwd_workspace_bytes", dev, T, n, Cc)
         ws = _ws(nb, dev)
         st = C.stream_of(xc)
         args = (C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(dc), C.dtype_code(dc.dtype),
@@ -184,7 +208,7 @@ def layer_bwd(x, dout, M, hpre, hpost, w, eps: float, raw=None):
 def mix_add_fwd(x, M, y, out_dtype=F32) -> torch.Tensor:
     dev = C.require_cuda(x, M, y)
     T, n, Cc = x.shape
-    with torch.cuda.device(dev):
+    with _on(dev):
         xc = _io(x)
         yc = _c(y) if y.dtype in (F32, xc.dtype) else y.float().contiguous()
         out = torch.empty(T, n, Cc, dtype=out_dtype, device=dev)
@@ -197,12 +221,12 @@ def mix_add_fwd(x, M, y, out_dtype=F32) -> torch.Tensor:
 def mix_add_bwd(x, M, dout):
     dev = C.require_cuda(x, M, dout)
     T, n, Cc = x.shape
-    with torch.cuda.device(dev):
+    with _on(dev):
         xc = _io(x)
         dc = _c(dout) if dout.dtype in (F32, xc.dtype) else dout.float().contiguous()
         dx = torch.empty(T, n, Cc, dtype=xc.dtype, device=dev)
         dM = torch.empty(n, n, dtype=F32, device=dev)
-        nb = int(C.query("mhc_mix_bwd_workspace_bytes", T, n, Cc))
+        nb = _ws_bytes("mhc_mix_bwd_workspace_bytes", dev, T, n, Cc)
         ws = _ws(nb, dev)
         _call("mhc_mix_add_bwd", xc, C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(_f32(M)), C.ptr(dc),
                C.dtype_code(dc.dtype), C.ptr(dx), C.dtype_code(dx.dtype), C.ptr(dM), T, n, Cc,
@@ -213,7 +237,7 @@ def mix_add_bwd(x, M, dout):
 def rewire_fwd(x, y, M, hpre, hpost, out_dtype=F32) -> torch.Tensor:
     dev = C.require_cuda(x, y, M, hpre, hpost)
     T, n, Cc = x.shape
-    with torch.cuda.device(dev):
+    with _on(dev):
         xc = _io(x)
         yc = _c(y) if y.dtype in (F32, xc.dtype) else y.float().contiguous()
         out = torch.empty(T, n, Cc, dtype=out_dtype, device=dev)
@@ -226,7 +250,7 @@ def rewire_fwd(x, y, M, hpre, hpost, out_dtype=F32) -> torch.Tensor:
 def rewire_bwd(x, y, dout, M, hpre, hpost):
     dev = C.require_cuda(x, y, dout, M, hpre, hpost)
     T, n, Cc = x.shape
-    with torch.cuda.device(dev):
+    with _on(dev):
         xc = _io(x)
         yc = _c(y) if y.dtype in (F32, xc.dtype) else y.float().contiguous()
         dc = _c(dout) if dout.dtype in (F32, xc.dtype) else dout.float().contiguous()
@@ -235,7 +259,7 @@ def rewire_bwd(x, y, dout, M, hpre, hpost):
         dM = torch.empty(n, n, dtype=F32, device=dev)
         dpre = torch.empty(n, dtype=F32, device=dev)
         dpost = torch.empty(n, dtype=F32, device=dev)
-        nb = int(C.query("mhc_rewire_bwd_workspace_bytes", T, n, Cc))
+        nb = _ws_bytes("mhc_rewire_bwd_workspace_bytes", dev, T, n, Cc)
         ws = _ws(nb, dev)
         _call("mhc_rewire_combine_bwd", xc, C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(yc),
                C.dtype_code(yc.dtype), C.ptr(dc), C.dtype_code(dc.dtype), C.ptr(_f32(M)),
@@ -248,7 +272,7 @@ def rewire_bwd(x, y, dout, M, hpre, hpost):
 def prescale_fwd(x, hpre, out_dtype=None) -> torch.Tensor:
     dev = C.require_cuda(x, hpre)
     T, n, Cc = x.shape
-    with torch.cuda.device(dev):
+    with _on(dev):
         xc = _io(x)
         odt = out_dtype or xc.dtype
         out = torch.empty(T, n, Cc, dtype=odt, device=dev)
@@ -260,12 +284,12 @@ def prescale_fwd(x, hpre, out_dtype=None) -> torch.Tensor:
 def prescale_bwd(x, d, hpre):
     dev = C.require_cuda(x, d, hpre)
     T, n, Cc = x.shape
-    with torch.cuda.device(dev):
+    with _on(dev):
         xc = _io(x)
         dc = _c(d) if d.dtype in (F32, xc.dtype) else d.float().contiguous()
         dx = torch.empty(T, n, Cc, dtype=xc.dtype, device=dev)
         dpre = torch.empty(n, dtype=F32, device=dev)
-        nb = int(C.query("mhc_mix_bwd_workspace_bytes", T, n, Cc))
+        nb = _ws_bytes("mhc_mix_bwd_workspace_bytes", dev, T, n, Cc)
         ws = _ws(nb, dev)
         _call("mhc_prescale_bwd", xc, C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(dc),
                C.dtype_code(dc.dtype), C.ptr(_f32(hpre)), C.ptr(dx), C.dtype_code(dx.dtype),
@@ -276,7 +300,7 @@ def prescale_bwd(x, d, hpre):
 def residual_add_agg(x, res, hpre, out_dtype=F32):
     dev = C.require_cuda(x, res, hpre)
     T, n, Cc = x.shape
-    with torch.cuda.device(dev):
+    with _on(dev):
         xc = _io(x)
         rc = _c(res.to(xc.dtype))
         out = torch.empty(T, n, Cc, dtype=out_dtype, device=dev)
@@ -291,13 +315,13 @@ def residual_add_agg_bwd(out, d_out, d_y, hpre, dx_dtype):
     """(dx, dH_pre) for out = x + res, y_agg = sum_i hpre_i out_i; d_out or d_y may be None."""
     dev = C.require_cuda(out, d_out, d_y, hpre)
     T, n, Cc = out.shape
-    with torch.cuda.device(dev):
+    with _on(dev):
         oc = _c(out)
         dc = None if d_out is None else _c(d_out.to(oc.dtype))
         yc = None if d_y is None else _f32(d_y)
         dx = torch.empty(T, n, Cc, dtype=dx_dtype, device=dev)
         dpre = torch.empty(n, dtype=F32, device=dev)
-        nb = int(C.query("mhc_mix_bwd_workspace_bytes", T, n, Cc))
+        nb = _ws_bytes("mhc_mix_bwd_workspace_bytes", dev, T, n, Cc)
         ws = _ws(nb, dev)
         _call("mhc_residual_add_agg_bwd", oc, C.ptr(oc), C.dtype_code(oc.dtype), C.ptr(dc),
               C.dtype_code(oc.dtype), C.ptr(yc), C.ptr(_f32(hpre)), C.ptr(dx),
