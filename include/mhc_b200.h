@@ -55,6 +55,12 @@ MHC_API const char* mhc_last_error(void);
 MHC_API int mhc_version(void);
 /* Number of SMs of the current device (used to size workspaces). */
 MHC_API int mhc_device_sm_count(int* sm_count);
+/* Self-test of the reciprocal the Sinkhorn kernels use for their row and
+ * column scales (a hardware approximation refined by one Newton-Raphson
+ * step, instead of an IEEE division): y[i] = 1 / x[i] for count floats.  No
+ * counterpart in the reference; it exists so that tests can bound the
+ * reciprocal against CUDA's division (within 1 ulp). */
+MHC_API int mhc_selftest_reciprocal(const float* x, float* y, int64_t count, void* stream);
 
 /* ---- parameters: activations + Sinkhorn-Knopp (single n x n matrix) ----
  * Replaces reference.py:51-55 activate_pre_post and reference.py:58-69

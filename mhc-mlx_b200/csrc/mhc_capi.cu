@@ -130,6 +130,15 @@ int mhc_device_sm_count(int* out) {
   return MHC_OK;
 }
 
+int mhc_selftest_reciprocal(const float* x, float* y, int64_t count, void* stream) {
+  MHC_TRY_BEGIN
+  MHC_REQ(count >= 0, "mhc_selftest_reciprocal: count must be >= 0");
+  MHC_REQ(count == 0 || (x && y), "mhc_selftest_reciprocal: NULL pointer");
+  if (count == 0) return MHC_OK;
+  return launch_selftest_reciprocal(x, y, count, as_stream(stream));
+  MHC_TRY_END
+}
+
 size_t mhc_sinkhorn_tape_floats(int n, int iters) {
   if (n < 1 || n > 64 || iters < 0) return 0;
   return sk_tape_floats(n, iters);

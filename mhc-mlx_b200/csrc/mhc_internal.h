@@ -65,6 +65,7 @@ int max_partial_rows(int64_t T);
 
 // ---- Sinkhorn / parameters (mhc_sinkhorn.cu) ----------------------------
 size_t sk_tape_floats(int n, int iters);
+int launch_selftest_reciprocal(const float* x, float* y, int64_t count, cudaStream_t st);
 int launch_params_fwd(const float* hpre_raw, const float* hpost_raw, const float* hres_raw,
                       int n, int iters, float eps, float* hpre, float* hpost, float* M,
                       float* tape, cudaStream_t st);

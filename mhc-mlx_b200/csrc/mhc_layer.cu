@@ -790,20 +790,43 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
   __shared__ float sP[kMaxN * kMaxN + 2 * kMaxN];
   __shared__ float D[kMaxN * (kMaxN + 1)];
   extern __shared__ float s_fin[];  // optional staged copy of tape + logits
-  for (int e0 = 0; e0 < P; e0 += 32) {
-    const int e = e0 + lane;
-    part[r0][lane] = (e < P) ? sliced_row_sum(wp + e, P, G, r0) : 0.f;
-    __syncthreads();
-    if (r0 == 0 && e < P) {
+  auto emit = [&](int e, float s) {
+    sP[e] = s;
+    if (e < n * n) { if (dM) dM[e] = s; }
+    else if (e < n * n + n) { if (dhpre) dhpre[e - n * n] = s; }
+    else if (dhpost) dhpost[e - n * n - n] = s;
+  };
+  if (2 * P <= kFinBD) {
+    // every thread of the block: S = kFinBD / P slices of the G rows per
+    // entry, consecutive threads on consecutive entries of a row
+    float* flat = &part[0][0];
+    const int S = kFinBD / P, e = tid % P, q = tid / P;
+    if (q < S) {
       float s = 0.f;
-#pragma unroll
-      for (int q = 0; q < kFinSlices; ++q) s += part[q][lane];
-      sP[e] = s;
-      if (e < n * n) { if (dM) dM[e] = s; }
-      else if (e < n * n + n) { if (dhpre) dhpre[e - n * n] = s; }
-      else if (dhpost) dhpost[e - n * n - n] = s;
+#pragma unroll 8
+      for (int g = q; g < G; g += S) s += wp[(size_t)g * P + e];
+      flat[q * P + e] = s;
     }
     __syncthreads();
+    if (tid < P) {
+      float s = 0.f;
+      for (int k = 0; k < S; ++k) s += flat[k * P + tid];
+      emit(tid, s);
+    }
+    __syncthreads();
+  } else {
+    for (int e0 = 0; e0 < P; e0 += 32) {
+      const int e = e0 + lane;
+      part[r0][lane] = (e < P) ? sliced_row_sum(wp + e, P, G, r0) : 0.f;
+      __syncthreads();
+      if (r0 == 0 && e < P) {
+        float s = 0.f;
+#pragma unroll
+        for (int q = 0; q < kFinSlices; ++q) s += part[q][lane];
+        emit(e, s);
+      }
+      __syncthreads();
+    }
   }
   if (tid < n) {
     if (hpre_raw && dhpre_raw) {
@@ -828,6 +851,16 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
         Hs = s_fin + tf;
       }
       __syncthreads();
+      if (sk_lane_ok(n)) {
+        if (tid < 32) {
+          MHC_SK_LANE_SWITCH(n, ({
+            const bool act = tid < SK_N * SK_N;
+            const float d = sk_backward_lane<SK_N>(Hs, Ts, iters, eps, act ? sP[tid] : 0.f);
+            if (act) dhres_raw[tid] = d;
+          }))
+        }
+        return;
+      }
       if (tid < 32) {
         const int row = tid % n;
         MHC_SK_WARP_SWITCH(n, ({

@@ -25,6 +25,10 @@ k_params_fwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost
     if (hpost_raw) hpost[tid] = 2.0f * sigmoidf_(hpost_raw[tid]);
   }
   if (!hres_raw) return;
+  if (sk_lane_ok(n)) {
+    if (tid < 32) MHC_SK_LANE_SWITCH(n, (sk_forward_lane<SK_N>(hres_raw, iters, eps, tape, M)))
+    return;
+  }
   if (sk_warp_ok(n)) {
     if (threadIdx.x < 32) MHC_SK_WARP_SWITCH(n, (sk_forward_warp<SK_N>(hres_raw, iters, eps, tape, M)))
     return;
@@ -66,6 +70,16 @@ k_params_bwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost
         Hs = s_stage_sk + tf;
       }
       __syncthreads();
+      if (sk_lane_ok(n)) {
+        if (tid < 32) {
+          MHC_SK_LANE_SWITCH(n, ({
+            const bool act = tid < SK_N * SK_N;
+            const float d = sk_backward_lane<SK_N>(Hs, Ts, iters, eps, act ? dM[tid] : 0.f);
+            if (act) dhres_raw[tid] = d;
+          }))
+        }
+        return;
+      }
       if (threadIdx.x < 32) {
         const int row = threadIdx.x % n;
         MHC_SK_WARP_SWITCH(n, ({
@@ -93,6 +107,20 @@ int launch_params_fwd(const float* hpre_raw, const float* hpost_raw, const float
   k_params_fwd<<<1, threads, 0, st>>>(hpre_raw, hpost_raw, hres_raw, n, iters, eps, hpre,
                                       hpost, M, tape);
   return check_launch("params_fwd");
+}
+
+__global__ void k_selftest_reciprocal(const float* __restrict__ x, float* __restrict__ y,
+                                      int64_t count) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count;
+       i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = rcp_nr(x[i]);
+}
+
+int launch_selftest_reciprocal(const float* x, float* y, int64_t count, cudaStream_t st) {
+  const int64_t blocks = (count + 255) / 256;
+  const int grid = (int)(blocks < 4096 ? blocks : 4096);
+  k_selftest_reciprocal<<<grid, 256, 0, st>>>(x, y, count);
+  return check_launch("selftest_reciprocal");
 }
 
 int launch_params_bwd(const float* hpre_raw, const float* hpost_raw, const float* hres_raw,
@@ -228,13 +256,13 @@ k_sk_batched_bwd(const float* __restrict__ H, const float* __restrict__ dM, int6
       pb[j] = pa[j] * rs;
       const float c = group_sum<N>(pb[j]);
       const float dcs = group_sum<N>(d[j] * pb[j]);
-      const float dc = c > eps ? -dcs / (c * c) : 0.f;
-      d[j] = d[j] * col_scale(c, eps) + dc;
+      const float cs = col_scale(c, eps);
+      d[j] = d[j] * cs + recip_grad(dcs, c, cs, eps);
     }
     float drs = 0.f;
 #pragma unroll
     for (int j = 0; j < N; ++j) drs += d[j] * pa[j];
-    const float dr = r > eps ? -drs / (r * r) : 0.f;
+    const float dr = recip_grad(drs, r, rs, eps);
 #pragma unroll
     for (int j = 0; j < N; ++j) d[j] = d[j] * rs + dr;
   }

@@ -120,7 +120,7 @@ __device__ inline void sk_backward_block(const float* __restrict__ H, SkTape tap
       for (int i = lane; i < n; i += 32)
         dcs += D[i * ld + j] * (tk[i * tp + j] * row_scale(tk[rofs + i], eps));
       dcs = warp_sum(dcs);
-      const float dc = c > eps ? -dcs / (c * c) : 0.f;
+      const float dc = recip_grad(dcs, c, cs, eps);
       for (int i = lane; i < n; i += 32) D[i * ld + j] = D[i * ld + j] * cs + dc;
     }
     __syncthreads();
@@ -131,7 +131,7 @@ __device__ inline void sk_backward_block(const float* __restrict__ H, SkTape tap
       float drs = 0.f;
       for (int j = lane; j < n; j += 32) drs += D[i * ld + j] * tk[i * tp + j];
       drs = warp_sum(drs);
-      const float dr = r > eps ? -drs / (r * r) : 0.f;
+      const float dr = recip_grad(drs, r, rs, eps);
       for (int j = lane; j < n; j += 32) D[i * ld + j] = D[i * ld + j] * rs + dr;
     }
     __syncthreads();
@@ -225,13 +225,13 @@ __device__ __forceinline__ void sk_backward_warp(const float* __restrict__ H,
     for (int j = 0; j < N; ++j) {
       const float c = __shfl_sync(0xffffffffu, cown, gbase + j);
       const float dcs = group_sum<N>(d[j] * (pa[j] * rs));
-      const float dc = c > eps ? -dcs / (c * c) : 0.f;
-      d[j] = d[j] * col_scale(c, eps) + dc;
+      const float cs = col_scale(c, eps);
+      d[j] = d[j] * cs + recip_grad(dcs, c, cs, eps);
     }
     float drs = 0.f;
 #pragma unroll
     for (int j = 0; j < N; ++j) drs += d[j] * pa[j];
-    const float dr = r > eps ? -drs / (r * r) : 0.f;
+    const float dr = recip_grad(drs, r, rs, eps);
 #pragma unroll
     for (int j = 0; j < N; ++j) d[j] = d[j] * rs + dr;
   }
@@ -252,6 +252,105 @@ __device__ __forceinline__ void sk_backward_warp(const float* __restrict__ H,
 #pragma unroll
   for (int j = 0; j < N; ++j) d[j] -= (h[j] == m) ? share : 0.f;
 }
+
+// ---------------------------------------------------------------------------
+// Element-per-lane Sinkhorn for n in {1, 2, 4}: lane L < n^2 of one warp holds
+// entry (i, j) = (L / n, L % n).  A row sum is a butterfly over the n
+// consecutive lanes of the row (xor 1 .. n/2), a column sum one over the lanes
+// n apart (xor n .. n^2/2), so a half-step is one butterfly, one reciprocal
+// and one multiply per lane: the 2 * iters long dependency chain carries a
+// few instructions per half-step instead of a loop over a whole row.  Lanes
+// >= n^2 run the same steps on their own (unused) values, which keeps every
+// shuffle full-warp.  Tape layout as sk_forward_warp: per iteration the n^2
+// values before the row scaling (row-major = lane order), the n row sums,
+// the n column sums.
+__host__ __device__ inline bool sk_lane_ok(int n) { return n == 1 || n == 2 || n == 4; }
+
+template <int N>
+__device__ __forceinline__ float sk_col_sum(float v) {
+#pragma unroll
+  for (int o = N * N / 2; o >= N; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int N>
+__device__ __forceinline__ float sk_row_max(float v) {
+#pragma unroll
+  for (int o = N / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <int N>
+__device__ __forceinline__ void sk_forward_lane(const float* __restrict__ H, int iters, float eps,
+                                                float* __restrict__ tape, float* __restrict__ M) {
+  constexpr int NN = N * N, TS = NN + 2 * N;
+  const int lane = threadIdx.x & 31;
+  const bool act = lane < NN;
+  const int i = (lane / N) % N, j = lane % N;
+  const float h = act ? H[lane] : 0.f;
+  float p = expf(h - sk_row_max<N>(h));
+  for (int k = 0; k < iters; ++k) {
+    float* tk = tape ? tape + (size_t)k * TS : nullptr;
+    const float s = group_sum<N>(p);
+    if (tk && act) {
+      tk[lane] = p;
+      if (j == 0) tk[NN + i] = s;
+    }
+    p *= row_scale(s, eps);
+    const float c = sk_col_sum<N>(p);
+    if (tk && act && i == 0) tk[NN + N + j] = c;
+    p *= col_scale(c, eps);
+  }
+  if (M && act) M[lane] = p;
+}
+
+// d: this lane's entry of dM on entry, of dH_res on exit.  The next
+// iteration's tape entries are loaded before the current one is processed.
+template <int N>
+__device__ __forceinline__ float sk_backward_lane(const float* __restrict__ H,
+                                                  const float* __restrict__ tape, int iters,
+                                                  float eps, float d) {
+  constexpr int NN = N * N, TS = NN + 2 * N;
+  const int lane = threadIdx.x & 31;
+  const bool act = lane < NN;
+  const int i = (lane / N) % N, j = lane % N;
+  auto ld = [&](int k, float& pa, float& r, float& c) {
+    const float* tk = tape + (size_t)k * TS;
+    pa = act ? tk[lane] : 0.f;
+    r = tk[NN + i];
+    c = tk[NN + N + j];
+  };
+  float pa = 0.f, r = 0.f, c = 0.f;
+  if (iters > 0) ld(iters - 1, pa, r, c);
+  for (int k = iters - 1; k >= 0; --k) {
+    float pn = 0.f, rn = 0.f, cn = 0.f;
+    if (k > 0) ld(k - 1, pn, rn, cn);
+    const float rs = row_scale(r, eps), cs = col_scale(c, eps);
+    const float dcs = sk_col_sum<N>(d * (pa * rs));
+    d = d * cs + recip_grad(dcs, c, cs, eps);
+    const float drs = group_sum<N>(d * pa);
+    d = d * rs + recip_grad(drs, r, rs, eps);
+    pa = pn;
+    r = rn;
+    c = cn;
+  }
+  // exp and the row-max shift (the max's gradient is split over ties)
+  const float h = act ? H[lane] : 0.f;
+  const float m = sk_row_max<N>(h);
+  d *= expf(h - m);
+  const float S = group_sum<N>(d);
+  const float cnt = group_sum<N>(h == m ? 1.f : 0.f);
+  return d - (h == m ? S / cnt : 0.f);
+}
+
+// Expand BODY with SK_N = n for the element-per-lane path (n in {1, 2, 4}).
+#define MHC_SK_LANE_SWITCH(n, BODY)                    \
+  switch (n) {                                         \
+    case 1: { constexpr int SK_N = 1; BODY; } break;   \
+    case 2: { constexpr int SK_N = 2; BODY; } break;   \
+    case 4: { constexpr int SK_N = 4; BODY; } break;   \
+    default: break;                                    \
+  }
 
 // Expand BODY with the compile-time constant SK_N equal to n (n | 32).
 #define MHC_SK_WARP_SWITCH(n, BODY)                 \

@@ -26,6 +26,7 @@ _P = c_void_p
 SIGNATURES: dict[str, tuple] = {
     "mhc_last_error": (ctypes.c_char_p, []),
     "mhc_version": (c_int, []),
+    "mhc_selftest_reciprocal": (c_int, [_P, _P, c_int64, _P]),
     "mhc_device_sm_count": (c_int, [ctypes.POINTER(c_int)]),
     "mhc_sinkhorn_tape_floats": (c_size_t, [c_int, c_int]),
     "mhc_params_fwd": (c_int, [_P, _P, _P, c_int, c_int, c_float, _P, _P, _P, _P, _P]),

@@ -52,7 +52,28 @@ def test_sinkhorn_stability_bomb():
     assert (M.sum(1) - 1).abs().max() < 1e-3 and (M.sum(0) - 1).abs().max() < 1e-3
 
 
-@pytest.mark.parametrize("n,iters", [(4, 20), (16, 10), (32, 20), (64, 20), (3, 7), (4, 0), (1, 5)])
+def test_sinkhorn_reciprocal_within_one_ulp():
+    """The row / column scales use a branch-free reciprocal (hardware
+    approximation plus one Newton-Raphson step) instead of an IEEE division;
+    against CUDA's 1/x (torch on the GPU) it is within 1 ulp over positive
+    normal floats with normal reciprocals, and exact at 0 / inf results."""
+    from mhc_b200 import _capi as C
+
+    g = torch.Generator().manual_seed(0)
+    wide = torch.pow(10.0, torch.rand(1 << 20, generator=g, dtype=F64) * 74 - 37)
+    sums = torch.rand(1 << 20, generator=g, dtype=F64) * 8 + 1e-5  # the range Sinkhorn sees
+    special = torch.tensor([1.0, 2.0, 0.5, 3.0, 4.0, 1e-5, float("inf")], dtype=F64)
+    x = torch.cat([wide, sums, special]).float().to(DEV)
+    y = torch.empty_like(x)
+    C.call("mhc_selftest_reciprocal", C.ptr(x), C.ptr(y), x.numel(), C.stream_of(x))
+    ref = 1.0 / x
+    ulps = (y.view(torch.int32).long() - ref.view(torch.int32).long()).abs()
+    assert int(ulps.max()) <= 1, int(ulps.max())
+    assert float(y[-1]) == 0.0
+
+
+@pytest.mark.parametrize("n,iters", [(4, 20), (2, 20), (8, 20), (16, 10), (32, 20), (64, 20),
+                                     (3, 7), (4, 0), (1, 5)])
 def test_sinkhorn_backward_matches_oracle(n, iters):
     g = torch.Generator().manual_seed(n * 100 + iters)
     H = torch.randn(n, n, generator=g)
