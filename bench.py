@@ -280,9 +280,30 @@ def e2e_measure(layer, T, n, C, iodt, rdt, dev, steps, world, chunks=8):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t)
     s_x, s_o = x_h.element_size(), out_h.element_size()
+    per_dir = T * n * C * (s_x + s_o)
+    # the link's own ceiling on this box: one chunk copied in and one out at
+    # the same time (pinned host memory, the same streams)
+    def bidir():
+        with torch.cuda.stream(s_in):
+            xd[0].copy_(x_h[0], non_blocking=True)
+        with torch.cuda.stream(s_out):
+            d_h[1].copy_(dd[1], non_blocking=True)
+    bidir()
+    torch.cuda.synchronize(dev)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(comp)
+    for _ in range(4):
+        bidir()
+    comp.wait_stream(s_in)
+    comp.wait_stream(s_out)
+    c1.record(comp)
+    torch.cuda.synchronize(dev)
+    link = 4 * (xd[0].nbytes + dd[1].nbytes) / 2 / (c0.elapsed_time(c1) * 1e-3) / 1e9
+    achieved = per_dir / (ms * 1e-3) / 1e9
     return {"value": world * T / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms,
-            "h2d_bytes_per_step": T * n * C * (s_x + s_o),
-            "d2h_bytes_per_step": T * n * C * (s_o + s_x),
+            "h2d_bytes_per_step": per_dir, "d2h_bytes_per_step": per_dir,
+            "link": {"bound": "pcie", "achieved_gbs_per_direction": achieved,
+                     "measured_bidirectional_gbs_per_direction": link, "frac": achieved / link},
             "path": f"MHCLayer forward+backward on pinned host tensors, {chunks} token chunks, "
                     "H2D/compute/D2H overlapped on 3 streams"}
 
