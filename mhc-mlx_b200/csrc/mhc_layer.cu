@@ -840,37 +840,53 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
   }
   if (hres_raw && dhres_raw && (tape || iters == 0)) {
     if (sk_warp_ok(n)) {
-      const float* Hs = hres_raw;
-      const float* Ts = tape;
+      // one call site per address space of the tape (shared when staged,
+      // global otherwise), so its loads are not generic
+      auto run = [&](const float* Hs, const float* Ts) {
+        if (sk_lane_ok(n)) {
+          if (tid < 32) {
+            MHC_SK_LANE_SWITCH(n, ({
+              const bool act = tid < SK_N * SK_N;
+              const float d = sk_backward_lane<SK_N>(Hs, Ts, iters, eps, act ? sP[tid] : 0.f);
+              if (act) dhres_raw[tid] = d;
+            }))
+          }
+          return;
+        }
+        if (tid < 32) {
+          const int row = tid % n;
+          MHC_SK_WARP_SWITCH(n, ({
+            float d[SK_N];
+            for (int j = 0; j < SK_N; ++j) d[j] = sP[row * SK_N + j];
+            sk_backward_warp<SK_N>(Hs, Ts, iters, eps, d);
+            if (tid < SK_N)
+              for (int j = 0; j < SK_N; ++j) dhres_raw[row * SK_N + j] = d[j];
+          }))
+        }
+      };
       if (stage_sk) {  // dynamic shared memory holds [tape | logits]
         const size_t tf = (size_t)iters * sk_tape_stride(n);
 #pragma unroll 8
         for (size_t e = tid; e < tf; e += kFinBD) s_fin[e] = tape[e];
         for (int e = tid; e < n * n; e += kFinBD) s_fin[tf + e] = hres_raw[e];
-        Ts = s_fin;
-        Hs = s_fin + tf;
+        __syncthreads();
+        run(s_fin + tf, s_fin);
+      } else {
+        run(hres_raw, tape);
       }
-      __syncthreads();
-      if (sk_lane_ok(n)) {
-        if (tid < 32) {
-          MHC_SK_LANE_SWITCH(n, ({
-            const bool act = tid < SK_N * SK_N;
-            const float d = sk_backward_lane<SK_N>(Hs, Ts, iters, eps, act ? sP[tid] : 0.f);
-            if (act) dhres_raw[tid] = d;
-          }))
+      return;
+    }
+    if (sk_elem_ok(n)) {  // kFinBD threads: n^2 / kFinBD entries per thread
+      MHC_SK_ELEM_SWITCH(n, ({
+        if (stage_sk) {
+          const SkTape tp = sk_stage_tape_fixed<SK_N>(tape, iters, s_fin);
+          __syncthreads();  // staged tape complete
+          sk_backward_elem<SK_N, kFinBD>(hres_raw, tp, iters, eps, sP, D, dhres_raw);
+        } else {
+          sk_backward_elem<SK_N, kFinBD>(hres_raw, SkTape{tape, SK_N, sk_tape_stride(SK_N)},
+                                         iters, eps, sP, D, dhres_raw);
         }
-        return;
-      }
-      if (tid < 32) {
-        const int row = tid % n;
-        MHC_SK_WARP_SWITCH(n, ({
-          float d[SK_N];
-          for (int j = 0; j < SK_N; ++j) d[j] = sP[row * SK_N + j];
-          sk_backward_warp<SK_N>(Hs, Ts, iters, eps, d);
-          if (tid < SK_N)
-            for (int j = 0; j < SK_N; ++j) dhres_raw[row * SK_N + j] = d[j];
-        }))
-      }
+      }))
       return;
     }
     const SkTape tp = stage_sk ? sk_stage_tape(tape, n, iters, s_fin)

@@ -33,6 +33,13 @@ k_params_fwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost
     if (threadIdx.x < 32) MHC_SK_WARP_SWITCH(n, (sk_forward_warp<SK_N>(hres_raw, iters, eps, tape, M)))
     return;
   }
+  if (sk_elem_ok(n)) {
+    if (tape)
+      MHC_SK_ELEM_SWITCH(n, (sk_forward_elem<SK_N, SK_N * SK_N, true>(hres_raw, iters, eps, P, tape, M)))
+    else
+      MHC_SK_ELEM_SWITCH(n, (sk_forward_elem<SK_N, SK_N * SK_N, false>(hres_raw, iters, eps, P, tape, M)))
+    return;
+  }
   sk_forward_block(hres_raw, n, iters, eps, P, tape, M);
 }
 
@@ -59,37 +66,53 @@ k_params_bwd(const float* __restrict__ hpre_raw, const float* __restrict__ hpost
   }
   if (hres_raw && dM) {
     if (sk_warp_ok(n)) {
-      const float* Hs = hres_raw;
-      const float* Ts = tape;
+      // one call site per address space of the tape (shared when staged,
+      // global otherwise), so its loads are not generic
+      auto run = [&](const float* Hs, const float* Ts) {
+        if (sk_lane_ok(n)) {
+          if (tid < 32) {
+            MHC_SK_LANE_SWITCH(n, ({
+              const bool act = tid < SK_N * SK_N;
+              const float d = sk_backward_lane<SK_N>(Hs, Ts, iters, eps, act ? dM[tid] : 0.f);
+              if (act) dhres_raw[tid] = d;
+            }))
+          }
+          return;
+        }
+        if (tid < 32) {
+          const int row = tid % n;
+          MHC_SK_WARP_SWITCH(n, ({
+            float d[SK_N];
+            for (int j = 0; j < SK_N; ++j) d[j] = dM[row * SK_N + j];
+            sk_backward_warp<SK_N>(Hs, Ts, iters, eps, d);
+            if (tid < SK_N)
+              for (int j = 0; j < SK_N; ++j) dhres_raw[row * SK_N + j] = d[j];
+          }))
+        }
+      };
       if (stage) {
         const size_t tf = (size_t)iters * sk_tape_stride(n);
 #pragma unroll 8
         for (size_t e = tid; e < tf; e += blockDim.x) s_stage_sk[e] = tape[e];
         for (int e = tid; e < n * n; e += blockDim.x) s_stage_sk[tf + e] = hres_raw[e];
-        Ts = s_stage_sk;
-        Hs = s_stage_sk + tf;
+        __syncthreads();
+        run(s_stage_sk + tf, s_stage_sk);
+      } else {
+        run(hres_raw, tape);
       }
-      __syncthreads();
-      if (sk_lane_ok(n)) {
-        if (tid < 32) {
-          MHC_SK_LANE_SWITCH(n, ({
-            const bool act = tid < SK_N * SK_N;
-            const float d = sk_backward_lane<SK_N>(Hs, Ts, iters, eps, act ? dM[tid] : 0.f);
-            if (act) dhres_raw[tid] = d;
-          }))
+      return;
+    }
+    if (sk_elem_ok(n)) {  // launched with n^2 threads
+      MHC_SK_ELEM_SWITCH(n, ({
+        if (stage) {
+          const SkTape tp = sk_stage_tape_fixed<SK_N>(tape, iters, s_stage_sk);
+          __syncthreads();  // staged tape complete
+          sk_backward_elem<SK_N, SK_N * SK_N>(hres_raw, tp, iters, eps, dM, D, dhres_raw);
+        } else {
+          sk_backward_elem<SK_N, SK_N * SK_N>(hres_raw, SkTape{tape, SK_N, sk_tape_stride(SK_N)},
+                                              iters, eps, dM, D, dhres_raw);
         }
-        return;
-      }
-      if (threadIdx.x < 32) {
-        const int row = threadIdx.x % n;
-        MHC_SK_WARP_SWITCH(n, ({
-          float d[SK_N];
-          for (int j = 0; j < SK_N; ++j) d[j] = dM[row * SK_N + j];
-          sk_backward_warp<SK_N>(Hs, Ts, iters, eps, d);
-          if (threadIdx.x < SK_N)
-            for (int j = 0; j < SK_N; ++j) dhres_raw[row * SK_N + j] = d[j];
-        }))
-      }
+      }))
       return;
     }
     const SkTape tp = stage ? sk_stage_tape(tape, n, iters, s_stage_sk)

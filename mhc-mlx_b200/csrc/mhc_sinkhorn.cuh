@@ -352,6 +352,163 @@ __device__ __forceinline__ float sk_backward_lane(const float* __restrict__ H,
     default: break;                                    \
   }
 
+// ---------------------------------------------------------------------------
+// Element-per-thread Sinkhorn for n in {16, 32} with BD threads (R = n^2 / BD
+// entries per thread, e = tid + BD * r).  Row phase: entry e is (e / n, e % n),
+// so a row is n consecutive e and its sum a butterfly within one warp.  Column
+// phase: entry e is (e % n, e / n), so a column is n consecutive e.  Between
+// the phases the values go through the padded shared buffer P [n][n + 1]:
+// every thread writes exactly the slots it read last, so one barrier per
+// transpose orders all reads and writes.  Compile-time n: no loops over a
+// runtime line length and no integer division on the chain.
+__host__ __device__ inline bool sk_elem_ok(int n) { return n == 16 || n == 32; }
+
+template <int N, int BD>
+__device__ __forceinline__ void sk_elem_to_col(float (&v)[N * N / BD], float* P) {
+  constexpr int R = N * N / BD, LD = N + 1;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int e = threadIdx.x + BD * r;
+    P[(e / N) * LD + e % N] = v[r];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int e = threadIdx.x + BD * r;
+    v[r] = P[(e % N) * LD + e / N];
+  }
+}
+
+template <int N, int BD>
+__device__ __forceinline__ void sk_elem_to_row(float (&v)[N * N / BD], float* P) {
+  constexpr int R = N * N / BD, LD = N + 1;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int e = threadIdx.x + BD * r;
+    P[(e % N) * LD + e / N] = v[r];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int e = threadIdx.x + BD * r;
+    v[r] = P[(e / N) * LD + e % N];
+  }
+}
+
+// P: shared [N][N + 1] scratch.  Requires blockDim.x == BD.  TAPE: record
+// the tape (tape non-null); the variant without it has no tape code at all.
+template <int N, int BD, bool TAPE>
+__device__ __forceinline__ void sk_forward_elem(const float* __restrict__ H, int iters, float eps,
+                                                float* P, float* __restrict__ tape,
+                                                float* __restrict__ M) {
+  constexpr int R = N * N / BD, NN = N * N, TS = NN + 2 * N;
+  static_assert(R * BD == NN && N <= 32 && 32 % N == 0, "rows within one warp");
+  float p[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const float h = H[threadIdx.x + BD * r];
+    p[r] = expf(h - sk_row_max<N>(h));
+  }
+  for (int k = 0; k < iters; ++k) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int e = threadIdx.x + BD * r;
+      const float s = group_sum<N>(p[r]);
+      if constexpr (TAPE) {
+        float* tk = tape + (size_t)k * TS;
+        tk[e] = p[r];
+        if (e % N == 0) tk[NN + e / N] = s;
+      }
+      p[r] *= row_scale(s, eps);
+    }
+    sk_elem_to_col<N, BD>(p, P);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int e = threadIdx.x + BD * r;
+      const float c = group_sum<N>(p[r]);
+      if constexpr (TAPE) {
+        if (e % N == 0) tape[(size_t)k * TS + NN + N + e / N] = c;
+      }
+      p[r] *= col_scale(c, eps);
+    }
+    sk_elem_to_row<N, BD>(p, P);
+  }
+  if (M)
+#pragma unroll
+    for (int r = 0; r < R; ++r) M[threadIdx.x + BD * r] = p[r];
+}
+
+// dM (row-major, global or shared) in, dH (global) out; P: shared [N][N + 1]
+// scratch.  Same phases in reverse: per iteration the column step (column
+// phase), then the row step (row phase).
+template <int N, int BD>
+__device__ __forceinline__ void sk_backward_elem(const float* __restrict__ H, SkTape tape,
+                                                 int iters, float eps, const float* dM, float* P,
+                                                 float* __restrict__ dH) {
+  constexpr int R = N * N / BD, NN = N * N;
+  static_assert(R * BD == NN && N <= 32 && 32 % N == 0, "rows within one warp");
+  const int tp = tape.tp, rofs = N * tp, cofs = N * tp + N;
+  float d[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) d[r] = dM[threadIdx.x + BD * r];
+  for (int k = iters - 1; k >= 0; --k) {
+    const float* tk = tape.it(k);
+    sk_elem_to_col<N, BD>(d, P);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int e = threadIdx.x + BD * r, i = e % N, j = e / N;
+      const float rs = row_scale(tk[rofs + i], eps);
+      const float c = tk[cofs + j], cs = col_scale(c, eps);
+      const float dcs = group_sum<N>(d[r] * (tk[i * tp + j] * rs));
+      d[r] = d[r] * cs + recip_grad(dcs, c, cs, eps);
+    }
+    sk_elem_to_row<N, BD>(d, P);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int e = threadIdx.x + BD * r, i = e / N, j = e % N;
+      const float rr = tk[rofs + i], rs = row_scale(rr, eps);
+      const float drs = group_sum<N>(d[r] * tk[i * tp + j]);
+      d[r] = d[r] * rs + recip_grad(drs, rr, rs, eps);
+    }
+  }
+  // exp and the row-max shift (the max's gradient is split over ties)
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int e = threadIdx.x + BD * r;
+    const float h = H[e];
+    const float m = sk_row_max<N>(h);
+    float v = d[r] * expf(h - m);
+    const float S = group_sum<N>(v);
+    const float cnt = group_sum<N>(h == m ? 1.f : 0.f);
+    dH[e] = v - (h == m ? S / cnt : 0.f);
+  }
+}
+
+// sk_stage_tape with n a compile-time constant: the index arithmetic of the
+// copy is constant division (multiply-shift), not 64-bit division by a
+// runtime n, which dominated the staging of a 32 x 32 tape.
+template <int N>
+__device__ __forceinline__ SkTape sk_stage_tape_fixed(const float* __restrict__ tape, int iters,
+                                                     float* smem) {
+  constexpr int NN = N * N, LD = N + 1, GS = NN + 2 * N, SS = N * LD + 2 * N;
+  const int total = iters * GS;
+#pragma unroll 8
+  for (int e = threadIdx.x; e < total; e += blockDim.x) {
+    const int k = e / GS, r = e - k * GS;
+    const int dst = r < NN ? (r / N) * LD + r % N : N * LD + (r - NN);
+    smem[k * SS + dst] = tape[e];
+  }
+  return SkTape{smem, LD, (size_t)SS};
+}
+
+// Expand BODY with SK_N = n for the element-per-thread path (n in {16, 32}).
+#define MHC_SK_ELEM_SWITCH(n, BODY)                     \
+  switch (n) {                                          \
+    case 16: { constexpr int SK_N = 16; BODY; } break;  \
+    case 32: { constexpr int SK_N = 32; BODY; } break;  \
+    default: break;                                     \
+  }
+
 // Expand BODY with the compile-time constant SK_N equal to n (n | 32).
 #define MHC_SK_WARP_SWITCH(n, BODY)                 \
   switch (n) {                                      \
@@ -376,6 +533,8 @@ __host__ __device__ inline size_t sk_stage_floats(int n, int iters) {
   return sk_warp_ok(n) ? (size_t)iters * sk_tape_stride(n) + (size_t)n * n
                        : sk_staged_tape_floats(n, iters);
 }
-__host__ __device__ inline int sk_threads(int n) { return sk_warp_ok(n) ? 32 : 32 * (n < 32 ? n : 32); }
+__host__ __device__ inline int sk_threads(int n) {
+  return sk_warp_ok(n) ? 32 : sk_elem_ok(n) ? n * n : 32 * (n < 32 ? n : 32);
+}
 
 }  // namespace mhc
