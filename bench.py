@@ -605,6 +605,30 @@ def run_configs(args):
                     "config": {"workload": "config 2 op sweep", "n": 4,
                                "note": "median of 200 calls, CUDA events; graph = replay of one "
                                        "captured fwd+bwd"}})
+        # the shapes the reference publishes MHCLayer forward timings for
+        # (BENCHMARKS.csv: n=32, fp32, B=1 latency and B=32 per-call time),
+        # with its Apple M4 Pro numbers beside ours as context only
+        published = {(1, 256): 514.33, (1, 512): 430.67, (1, 1024): 437.08, (1, 2048): 520.04,
+                     (1, 4096): 406.88, (32, 512): 117.73, (32, 2048): 1529.09,
+                     (32, 4096): 2078.89}
+        rows = []
+        for (B, C), ref_us in published.items():
+            layer = make_layer(32, C, dev)
+            x = torch.randn(B, 32, C, device=dev)
+
+            def fo():
+                with torch.no_grad():
+                    layer(x)
+
+            rows.append({"B": B, "C": C, "fwd_us": _median_us(fo, dev),
+                         "fwd_graph_us": _graph_us(fo, dev),
+                         "reference_m4pro_fwd_us": ref_us})
+        out.append({"metric": "MHCLayer forward per-call time at the reference's published "
+                              "shapes (n=32, fp32)",
+                    "unit": "us", "higher_is_better": False, "rows": rows,
+                    "config": {"workload": "BENCHMARKS.csv MHCLayer rows", "n": 32,
+                               "note": "reference_m4pro_fwd_us: the reference's published Apple "
+                                       "M4 Pro Metal timings, other hardware, context only"}})
     if w in ("sinkhorn", "all"):
         # config 3: 65,536 independent 4x4 logits, 20 iterations, fwd + bwd
         from mhc_b200 import _kernels as K

@@ -17,6 +17,8 @@
 // The "generic" kernels cover any n <= 64 and any C with two passes per row.
 #include <cstdlib>
 
+#include <cooperative_groups.h>
+
 #include "mhc_common.cuh"
 #include "mhc_sinkhorn.cuh"
 #include "mhc_internal.h"
@@ -186,6 +188,73 @@ k_fwd_generic(const InT* __restrict__ x, const float* __restrict__ Mg,
       }
     }
   }
+}
+
+// Cluster-split forward for n in {16, 32, 64}: the columns of one token are
+// split over the CTAs of a thread-block cluster (cluster size cs = 1..8,
+// chosen at launch so that a few CTAs per SM are in flight even when there
+// are few tokens).  Each CTA reduces sum(y^2) over its columns; the cs
+// partials are summed through distributed shared memory between two cluster
+// barriers (the second keeps every CTA's partial alive until all have read
+// it), then each CTA writes its columns: out_i = sum_j M_ij x_j + hpost_i yn,
+// with the slice of x re-read from L2.  No workspace and no atomics; the
+// partials are summed in rank order, so results are deterministic.
+template <int N, typename InT, typename OutT>
+__global__ void __launch_bounds__(256)
+k_fwd_split(const InT* __restrict__ x, const float* __restrict__ Mg,
+            const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
+            const float* __restrict__ w, OutT* __restrict__ out, int64_t T, int C, float eps) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  const int cs = (int)cl.num_blocks(), rank = (int)cl.block_rank();
+  __shared__ __align__(16) float sM[N * N];
+  __shared__ float shpre[N], shpost[N];
+  __shared__ float red[2][32];
+  __shared__ float s_part;
+  for (int e = threadIdx.x; e < N * N; e += blockDim.x) sM[e] = Mg[e];
+  for (int e = threadIdx.x; e < N; e += blockDim.x) { shpre[e] = hpre_g[e]; shpost[e] = hpost_g[e]; }
+  __syncthreads();
+  const int64_t t = blockIdx.x / cs;
+  const int chunk = (C + cs - 1) / cs, c0 = rank * chunk, c1 = min(C, c0 + chunk);
+  const InT* xt = x + t * (int64_t)N * C;
+  float ss = 0.f;
+  for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
+    float a = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) a = fmaf(shpre[i], to_f(xt[(int64_t)i * C + c]), a);
+    ss = fmaf(a, a, ss);
+  }
+  ss = block_sum(ss, red[0]);
+  if (threadIdx.x == 0) s_part = ss;
+  cl.sync();  // every CTA's partial is written
+  float tot = 0.f;
+  for (int r = 0; r < cs; ++r) tot += *cl.map_shared_rank(&s_part, r);
+  const float inv = inv_rms(tot, C, eps);
+  OutT* ot = out + t * (int64_t)N * C;
+  const float4* sM4 = reinterpret_cast<const float4*>(sM);
+  for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
+    float xc[N], a = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      xc[j] = to_f(xt[(int64_t)j * C + c]);
+      a = fmaf(shpre[j], xc[j], a);
+    }
+    const float yn = (a * inv) * __ldg(w + c);
+#pragma unroll 4
+    for (int i = 0; i < N; ++i) {
+      float m = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; j += 4) {
+        const float4 r4 = sM4[(i * N + j) / 4];
+        m = fmaf(r4.x, xc[j], m);
+        m = fmaf(r4.y, xc[j + 1], m);
+        m = fmaf(r4.z, xc[j + 2], m);
+        m = fmaf(r4.w, xc[j + 3], m);
+      }
+      ot[(int64_t)i * C + c] = from_f<OutT>(m + shpost[i] * yn);
+    }
+  }
+  cl.sync();  // no CTA leaves while another may still read its partial
 }
 
 // ===================================================================== bwd ==
@@ -997,6 +1066,34 @@ static int fwd_fast(const InT* x, const float* M, const float* hpre, const float
   return try_fwd_vec<N, InT, OutT, 1>(x, M, hpre, hpost, w, out, T, C, eps, st);
 }
 
+// Cluster-split forward (k_fwd_split) for n in {16, 32, 64}; the cluster
+// size targets about four CTAs per SM in flight.
+template <int N, typename InT, typename OutT>
+static int launch_fwd_split(const InT* x, const float* M, const float* hpre, const float* hpost,
+                            const float* w, OutT* out, int64_t T, int C, float eps,
+                            cudaStream_t st) {
+  const int64_t want = 4 * (int64_t)sm_count();
+  int cs = 1;
+  while (cs < 8 && T * cs < want && C / (2 * cs) >= 256) cs *= 2;
+  if (T * cs > 0x7fffffffLL) return -1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(T * cs), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e =
+      cudaLaunchKernelEx(&cfg, k_fwd_split<N, InT, OutT>, x, M, hpre, hpost, w, out, T, C, eps);
+  if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_fwd(split): %s", cudaGetErrorString(e));
+  return check_launch("mhc_fwd(split)");
+}
+
 template <typename InT, typename OutT>
 static int fwd_generic(const InT* x, const float* M, const float* hpre, const float* hpost,
                        const float* w, OutT* out, int64_t T, int n, int C, float eps,
@@ -1031,6 +1128,15 @@ static int fwd_typed(const void* xv, const float* M, const float* hpre, const fl
       default: break;
     }
     if (r >= 0) return r;
+    if (env_int("MHC_B200_SPLIT", 1)) {
+      switch (n) {
+        case 16: r = launch_fwd_split<16, InT, OutT>(x, M, hpre, hpost, w, out, T, C, eps, st); break;
+        case 32: r = launch_fwd_split<32, InT, OutT>(x, M, hpre, hpost, w, out, T, C, eps, st); break;
+        case 64: r = launch_fwd_split<64, InT, OutT>(x, M, hpre, hpost, w, out, T, C, eps, st); break;
+        default: break;
+      }
+      if (r >= 0) return r;
+    }
   }
   return fwd_generic<InT, OutT>(x, M, hpre, hpost, w, out, T, n, C, eps, st);
 }
