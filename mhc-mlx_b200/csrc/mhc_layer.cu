@@ -684,6 +684,14 @@ k_bwd_rows(const T* __restrict__ x, const T* __restrict__ dout, const float* __r
 // product D_aug X_aug^T with 4x4 register blocks:
 //   [i<n, j<n] -> dM_ij,  [i<n, j=n] -> dHpost_i,  [i=n, j<n] -> dHpre_j.
 // d_rms_weight accumulates in the CTA's own row of the column partials.
+//
+// Launched as thread-block clusters of cs = 1..8 CTAs: the CTAs of a cluster
+// share each of the cluster's tokens, one column slice each (so a few tokens
+// still fill the GPU), and the per-token sums (ss, pd) of the cs slices are
+// added through distributed shared memory in rank order.  The partial pairs
+// are double-buffered by token parity: a CTA cannot write the same buffer
+// again before passing the next cluster barrier, which the others reach only
+// after reading it.
 constexpr int kGenBD = 128;   // threads per CTA (= tile width)
 constexpr int kGenLD = kGenBD + 1;
 constexpr int kGenRB = 4;     // register block edge
@@ -696,6 +704,12 @@ k_bwd_generic(const XT* __restrict__ x, const DT* __restrict__ dout, const float
               const float* __restrict__ w, DXT* __restrict__ dx, int64_t T, int n, int C,
               float eps, float* __restrict__ ws_p, float* __restrict__ ws_c,
               int* __restrict__ ws_hdr) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  const int cs = (int)cl.num_blocks(), rank = (int)cl.block_rank();
+  const int64_t q0 = blockIdx.x / cs, Q = gridDim.x / cs;  // cluster index / count
+  const int chunk = (C + cs - 1) / cs, cl0 = min(C, rank * chunk), cl1 = min(C, cl0 + chunk);
+  __shared__ float2 s_part[2];
   extern __shared__ float smem[];
   const int na = n + 1;
   float* sM = smem;                       // n*n
@@ -724,11 +738,11 @@ k_bwd_generic(const XT* __restrict__ x, const DT* __restrict__ dout, const float
   const int64_t rs = (int64_t)n * C;
   const float invC = 1.0f / (float)C;
   int par = 0;
-  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+  for (int64_t t = q0; t < T; t += Q) {
     const XT* xt = x + t * rs;
     const DT* dt = dout + t * rs;
     float ss = 0.f, pd = 0.f;
-    for (int c = tid; c < C; c += kGenBD) {
+    for (int c = cl0 + tid; c < cl1; c += kGenBD) {
       float y = 0.f, dyn = 0.f;
       for (int i = 0; i < n; ++i) {
         y = fmaf(shpre[i], to_f(xt[(int64_t)i * C + c]), y);
@@ -737,14 +751,22 @@ k_bwd_generic(const XT* __restrict__ x, const DT* __restrict__ dout, const float
       ss = fmaf(y, y, ss);
       pd = fmaf(dyn * __ldg(w + c), y, pd);
     }
-    const float2 red2 = block_sum2(ss, pd, red[par]);
+    const float2 part = block_sum2(ss, pd, red[par]);
+    if (tid == 0) s_part[par] = part;
+    cl.sync();  // every slice's partial pair of this token is written
+    float2 red2 = make_float2(0.f, 0.f);
+    for (int r = 0; r < cs; ++r) {
+      const float2 v = *cl.map_shared_rank(&s_part[par], r);
+      red2.x += v.x;
+      red2.y += v.y;
+    }
     par ^= 1;
     const float inv = inv_rms(red2.x, C, eps);
     const float k2 = (red2.y * (inv * inv * inv)) * invC;
     DXT* dxt = dx + t * rs;
-    for (int c0 = 0; c0 < C; c0 += kGenBD) {
+    for (int c0 = cl0; c0 < cl1; c0 += kGenBD) {
       const int c = c0 + tid;
-      const bool ok = c < C;
+      const bool ok = c < cl1;
       float y = 0.f, dyn = 0.f;
       for (int i = 0; i < n; ++i) {
         const float xv = ok ? to_f(xt[(int64_t)i * C + c]) : 0.f;
@@ -768,7 +790,7 @@ k_bwd_generic(const XT* __restrict__ x, const DT* __restrict__ dout, const float
         }
       }
       __syncthreads();
-      const int width = min(kGenBD, C - c0);
+      const int width = min(kGenBD, cl1 - c0);
 #pragma unroll
       for (int q = 0; q < kGenMaxBlk; ++q) {
         const int blk = tid + q * kGenBD;
@@ -809,6 +831,7 @@ k_bwd_generic(const XT* __restrict__ x, const DT* __restrict__ dout, const float
       }
   }
   if (blockIdx.x == 0 && tid == 0) ws_hdr[0] = gridDim.x;
+  cl.sync();  // the last token's partial pairs stay readable until every CTA has them
 }
 
 // ================================================================ finalize ==
@@ -978,7 +1001,7 @@ static int env_int(const char* name, int dflt) {
 
 int max_partial_rows(int64_t T) {
   int64_t g = (int64_t)sm_count() * 4;
-  if (g > T) g = T;
+  if (g > 8 * T) g = 8 * T;  // up to 8 column slices per token (cluster-split backward)
   return (int)(g < 1 ? 1 : g);
 }
 
@@ -1320,9 +1343,35 @@ static int bwd_typed(const void* xv, const void* dv, const float* M, const float
     cudaError_t e = allow_dyn_smem(kern, smem);
     if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_bwd(generic): %s", cudaGetErrorString(e));
   }
-  const int G = persistent_grid(kern, kGenBD, smem, T, max_partial_rows(T));
+  // cluster size: split each token's columns while there are few tokens per
+  // resident CTA slot; Q clusters loop over the tokens
+  const int rows = max_partial_rows(T);
+  const int64_t want = 4 * (int64_t)sm_count();
+  int cs = 1;
+  if (env_int("MHC_B200_SPLIT", 1))
+    while (cs < 8 && T * cs < want && C / (2 * cs) >= kGenBD && 2 * cs <= rows) cs *= 2;
+  const int resident = persistent_grid(kern, kGenBD, smem, 1 << 30, 1 << 30);
+  int64_t Q = resident / cs;
+  if (Q > rows / cs) Q = rows / cs;
+  if (Q > T) Q = T;
+  if (Q < 1) Q = 1;
+  const int G = (int)(Q * cs);
   BwdPtrs p = ws_ptrs(ws, G, n);
-  kern<<<G, kGenBD, smem, st>>>(x, d, M, hpre, hpost, w, dx, T, n, C, eps, p.p, p.c, p.hdr);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)G, 1, 1);
+  cfg.blockDim = dim3(kGenBD, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, x, d, M, hpre, hpost, w, dx, T, n, C, eps,
+                                           p.p, p.c, p.hdr);
+  if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_bwd(generic): %s", cudaGetErrorString(e));
   return check_launch("mhc_bwd(generic)");
 }
 
