@@ -612,23 +612,34 @@ def run_configs(args):
                      (1, 4096): 406.88, (32, 512): 117.73, (32, 2048): 1529.09,
                      (32, 4096): 2078.89}
         rows = []
-        for (B, C), ref_us in published.items():
+        for (B, C), ref_us in list(published.items()) + [((256, 4096), None)]:
             layer = make_layer(32, C, dev)
             x = torch.randn(B, 32, C, device=dev)
+            xg = x.clone().requires_grad_(True)
+            d = torch.randn(B, 32, C, device=dev)
 
             def fo():
                 with torch.no_grad():
                     layer(x)
 
+            def fb():
+                xg.grad = None
+                for p_ in layer.parameters():
+                    p_.grad = None
+                layer(xg).backward(d)
+
             rows.append({"B": B, "C": C, "fwd_us": _median_us(fo, dev),
                          "fwd_graph_us": _graph_us(fo, dev),
+                         "fwd_bwd_graph_us": _graph_us(fb, dev),
                          "reference_m4pro_fwd_us": ref_us})
-        out.append({"metric": "MHCLayer forward per-call time at the reference's published "
-                              "shapes (n=32, fp32)",
+        out.append({"metric": "MHCLayer per-call time at the reference's published shapes "
+                              "(n=32, fp32; forward, and forward+backward)",
                     "unit": "us", "higher_is_better": False, "rows": rows,
-                    "config": {"workload": "BENCHMARKS.csv MHCLayer rows", "n": 32,
+                    "config": {"workload": "BENCHMARKS.csv MHCLayer rows (+ B=256, C=4096)",
+                               "n": 32,
                                "note": "reference_m4pro_fwd_us: the reference's published Apple "
-                                       "M4 Pro Metal timings, other hardware, context only"}})
+                                       "M4 Pro Metal forward timings, other hardware, context "
+                                       "only (it publishes no backward timing)"}})
     if w in ("sinkhorn", "all"):
         # config 3: 65,536 independent 4x4 logits, 20 iterations, fwd + bwd
         from mhc_b200 import _kernels as K

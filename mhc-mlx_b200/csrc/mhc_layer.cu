@@ -834,6 +834,210 @@ k_bwd_generic(const XT* __restrict__ x, const DT* __restrict__ dout, const float
   cl.sync();  // the last token's partial pairs stay readable until every CTA has them
 }
 
+// Backward for n in {16, 32}: the structure of k_bwd_generic (cluster column
+// slices, pass 1 per token, tiles of 128 staged columns), with the two n x n
+// contractions of a tile register-tiled for a compile-time N:
+//   dx = M^T d + H_pre dya: thread (jg, cg) owns streams 4jg..4jg+3 of DXC
+//     groups of 4 columns; per stream i one float4 of M[i][4jg..] and DXC
+//     float4s of d[i][cols] feed 16 DXC FMAs;
+//   dM += d x^T: one 8 x 8 register block per thread, the tile's columns
+//     split over SL = 128 / (N/8)^2 slices (16 scalar loads for 64 FMAs);
+//     dH_post_i = sum d_i (y inv w) and dH_pre_j = sum dya x_j ride along,
+//     8 / (N/8) rows and columns per thread.
+// Staged row i starts at wide_row(i) = i * kWideLD + (i / 8) * 8 floats, so
+// the 8-row blocks read by one warp fall on distinct banks and every row
+// start is 16-byte aligned.  The slices' dM blocks are added in slice order
+// at the end (no atomics: bitwise reproducible).
+constexpr int kWideBD = 128;
+constexpr int kWideLD = kWideBD + 4;
+__host__ __device__ constexpr int wide_row(int i) { return i * kWideLD + (i >> 3) * 8; }
+__host__ __device__ constexpr size_t wide_smem_bytes(int n) {
+  return 2 * (size_t)(wide_row(n) + kWideLD) * sizeof(float);
+}
+
+template <int N, typename XT, typename DT, typename DXT>
+__global__ void __launch_bounds__(kWideBD, 3)
+k_bwd_wide(const XT* __restrict__ x, const DT* __restrict__ dout, const float* __restrict__ Mg,
+           const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
+           const float* __restrict__ w, DXT* __restrict__ dx, int64_t T, int C, float eps,
+           int vec_dx, float* __restrict__ ws_p, float* __restrict__ ws_c,
+           int* __restrict__ ws_hdr) {
+  static_assert(N == 16 || N == 32, "register tiling for n = 16 and n = 32");
+  constexpr int NB = N / 8;                 // 8 x 8 blocks per edge
+  constexpr int SL = kWideBD / (NB * NB);   // column slices of the dM product
+  constexpr int HR = 8 / NB;                // dH_post rows / dH_pre columns per thread
+  constexpr int CG = kWideBD / (N / 4);     // 4-column groups in a dx row pass
+  constexpr int DXC = kWideBD / (4 * CG);   // 4-column groups per thread
+  constexpr int P = N * N + 2 * N;
+  static_assert(P <= 2 * (wide_row(N) + kWideLD), "partials fit the staging area");
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  const int cs = (int)cl.num_blocks(), rank = (int)cl.block_rank();
+  const int64_t q0 = blockIdx.x / cs, Q = gridDim.x / cs;
+  const int chunk = (((C + cs - 1) / cs) + 3) & ~3;  // slice starts on 4-column groups
+  const int cl0 = min(C, rank * chunk), cl1 = min(C, cl0 + chunk);
+  __shared__ float2 s_part[2];
+  __shared__ float red[2][64];
+  __shared__ __align__(16) float sM[N * N];
+  __shared__ float shpre[N], shpost[N];
+  extern __shared__ __align__(16) float smem[];
+  float* sx = smem;                         // rows 0..N-1: x, row N: y inv w
+  float* sd = smem + wide_row(N) + kWideLD; // rows 0..N-1: d_out, row N: dya
+  const int tid = threadIdx.x;
+  for (int e = tid; e < N * N; e += kWideBD) sM[e] = Mg[e];
+  if (tid < N) { shpre[tid] = hpre_g[tid]; shpost[tid] = hpost_g[tid]; }
+  float* wc = ws_c + (size_t)blockIdx.x * C;
+  for (int c = tid; c < C; c += kWideBD) wc[c] = 0.f;
+
+  const int jg = tid / CG, cgi = tid % CG;            // dx roles
+  const int sl = tid / (NB * NB), blk = tid % (NB * NB);
+  const int bi = blk / NB, bj = blk % NB;              // dM roles
+  float acc[8][8], hpo[HR], hpr[HR];
+#pragma unroll
+  for (int a = 0; a < 8; ++a)
+#pragma unroll
+    for (int b = 0; b < 8; ++b) acc[a][b] = 0.f;
+#pragma unroll
+  for (int r = 0; r < HR; ++r) { hpo[r] = 0.f; hpr[r] = 0.f; }
+  __syncthreads();
+
+  const int64_t rs = (int64_t)N * C;
+  const float invC = 1.0f / (float)C;
+  int par = 0;
+  for (int64_t t = q0; t < T; t += Q) {
+    const XT* xt = x + t * rs;
+    const DT* dt = dout + t * rs;
+    float ss = 0.f, pd = 0.f;
+    for (int c = cl0 + tid; c < cl1; c += kWideBD) {
+      float y = 0.f, dyn = 0.f;
+#pragma unroll 8
+      for (int i = 0; i < N; ++i) {
+        y = fmaf(shpre[i], to_f(xt[(int64_t)i * C + c]), y);
+        dyn = fmaf(shpost[i], to_f(dt[(int64_t)i * C + c]), dyn);
+      }
+      ss = fmaf(y, y, ss);
+      pd = fmaf(dyn * __ldg(w + c), y, pd);
+    }
+    const float2 part = block_sum2(ss, pd, red[par]);
+    if (tid == 0) s_part[par] = part;
+    cl.sync();  // every slice's partial pair of this token is written
+    float2 red2 = make_float2(0.f, 0.f);
+    for (int r = 0; r < cs; ++r) {
+      const float2 v = *cl.map_shared_rank(&s_part[par], r);
+      red2.x += v.x;
+      red2.y += v.y;
+    }
+    par ^= 1;
+    const float inv = inv_rms(red2.x, C, eps);
+    const float k2 = (red2.y * (inv * inv * inv)) * invC;
+    DXT* dxt = dx + t * rs;
+    for (int c0 = cl0; c0 < cl1; c0 += kWideBD) {
+      const int width = min(kWideBD, cl1 - c0);
+      {  // stage the tile: thread tid owns column c0 + tid
+        const int c = c0 + tid;
+        const bool ok = tid < width;
+        float y = 0.f, dyn = 0.f;
+#pragma unroll 8
+        for (int i = 0; i < N; ++i) {
+          const float xv = ok ? to_f(xt[(int64_t)i * C + c]) : 0.f;
+          const float dv = ok ? to_f(dt[(int64_t)i * C + c]) : 0.f;
+          sx[wide_row(i) + tid] = xv;
+          sd[wide_row(i) + tid] = dv;
+          y = fmaf(shpre[i], xv, y);
+          dyn = fmaf(shpost[i], dv, dyn);
+        }
+        const float wv = ok ? __ldg(w + c) : 0.f;
+        const float yi = y * inv;
+        sx[wide_row(N) + tid] = yi * wv;
+        sd[wide_row(N) + tid] = ok ? (dyn * wv) * inv - k2 * y : 0.f;
+        if (ok) wc[c] = fmaf(dyn, yi, wc[c]);
+      }
+      __syncthreads();
+      // dx for streams 4jg..4jg+3
+#pragma unroll
+      for (int q = 0; q < DXC; ++q) {
+        const int cb = 4 * cgi + 4 * CG * q;
+        if (cb < width) {
+          float o[4][4];
+          const float4 g4 = *reinterpret_cast<const float4*>(sd + wide_row(N) + cb);
+#pragma unroll
+          for (int a = 0; a < 4; ++a) {
+            const float hp = shpre[4 * jg + a];
+            o[a][0] = hp * g4.x; o[a][1] = hp * g4.y; o[a][2] = hp * g4.z; o[a][3] = hp * g4.w;
+          }
+#pragma unroll 8
+          for (int i = 0; i < N; ++i) {
+            const float4 m4 = *reinterpret_cast<const float4*>(sM + i * N + 4 * jg);
+            const float4 d4 = *reinterpret_cast<const float4*>(sd + wide_row(i) + cb);
+            const float mv[4] = {m4.x, m4.y, m4.z, m4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+              for (int v = 0; v < 4; ++v) o[a][v] = fmaf(mv[a], dv[v], o[a][v]);
+          }
+#pragma unroll
+          for (int a = 0; a < 4; ++a) {
+            DXT* dst = dxt + (int64_t)(4 * jg + a) * C + c0 + cb;
+            if (vec_dx && cb + 4 <= width) {
+              store_vec<DXT, 4, true>(dst, o[a]);
+            } else {
+#pragma unroll
+              for (int v = 0; v < 4; ++v)
+                if (cb + v < width) dst[v] = from_f<DXT>(o[a][v]);
+            }
+          }
+        }
+      }
+      // dM block (8bi.., 8bj..) over this slice's columns, plus the
+      // dH_post rows 8bi + HR bj + r and dH_pre columns 8bj + HR bi + r
+      for (int c = sl; c < width; c += SL) {
+        float dv[8], xv[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) {
+          dv[a] = sd[wide_row(8 * bi + a) + c];
+          xv[a] = sx[wide_row(8 * bj + a) + c];
+        }
+#pragma unroll
+        for (int a = 0; a < 8; ++a)
+#pragma unroll
+          for (int b = 0; b < 8; ++b) acc[a][b] = fmaf(dv[a], xv[b], acc[a][b]);
+        const float yw = sx[wide_row(N) + c], ga = sd[wide_row(N) + c];
+#pragma unroll
+        for (int r = 0; r < HR; ++r) {
+          hpo[r] = fmaf(sd[wide_row(8 * bi + HR * bj + r) + c], yw, hpo[r]);
+          hpr[r] = fmaf(ga, sx[wide_row(8 * bj + HR * bi + r) + c], hpr[r]);
+        }
+      }
+      __syncthreads();
+    }
+  }
+  // add the slices' blocks in slice order in the (now free) staging area
+  float* buf = smem;
+  for (int s = 0; s < SL; ++s) {
+    if (sl == s) {
+#pragma unroll
+      for (int a = 0; a < 8; ++a)
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+          float& e = buf[(8 * bi + a) * N + 8 * bj + b];
+          e = (s == 0 ? 0.f : e) + acc[a][b];
+        }
+#pragma unroll
+      for (int r = 0; r < HR; ++r) {
+        float& e1 = buf[N * N + N + 8 * bi + HR * bj + r];  // dH_post_i
+        e1 = (s == 0 ? 0.f : e1) + hpo[r];
+        float& e2 = buf[N * N + 8 * bj + HR * bi + r];      // dH_pre_j
+        e2 = (s == 0 ? 0.f : e2) + hpr[r];
+      }
+    }
+    __syncthreads();
+  }
+  float* pr = ws_p + (size_t)blockIdx.x * P;
+  for (int e = tid; e < P; e += kWideBD) pr[e] = buf[e];
+  if (blockIdx.x == 0 && tid == 0) ws_hdr[0] = gridDim.x;
+  cl.sync();  // the last token's partial pairs stay readable until every CTA has them
+}
+
 // ================================================================ finalize ==
 // Blocks [0, nbc) reduce d_rms_weight, 32 columns per block: thread
 // (slice r, column c) sums partial rows r, r + 8, r + 16, ... and the 8
@@ -1336,43 +1540,56 @@ static int bwd_typed(const void* xv, const void* dv, const float* M, const float
     }
     if (r >= 0) return r;
   }
-  const int na = n + 1;
-  const size_t smem = ((size_t)n * n + 2 * n + 2 * (size_t)na * kGenLD) * sizeof(float);
-  auto kern = k_bwd_generic<XT, DT, DXT>;
-  {
-    cudaError_t e = allow_dyn_smem(kern, smem);
-    if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_bwd(generic): %s", cudaGetErrorString(e));
+  // Cluster launch shared by the wide and generic kernels: split each
+  // token's columns over cs CTAs while there are few tokens per resident
+  // CTA slot; Q clusters loop over the tokens.
+  auto launch_clusters = [&](auto kern, size_t smem, const char* what, auto... tail) -> int {
+    {
+      cudaError_t e = allow_dyn_smem(kern, smem);
+      if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    }
+    const int rows = max_partial_rows(T);
+    const int64_t want = 4 * (int64_t)sm_count();
+    int cs = 1;
+    if (env_int("MHC_B200_SPLIT", 1))
+      while (cs < 8 && T * cs < want && C / (2 * cs) >= kGenBD && 2 * cs <= rows) cs *= 2;
+    const int resident = persistent_grid(kern, kGenBD, smem, 1 << 30, 1 << 30);
+    int64_t Q = resident / cs;
+    if (Q > rows / cs) Q = rows / cs;
+    if (Q > T) Q = T;
+    if (Q < 1) Q = 1;
+    const int G = (int)(Q * cs);
+    BwdPtrs p = ws_ptrs(ws, G, n);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)G, 1, 1);
+    cfg.blockDim = dim3(kGenBD, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, x, d, M, hpre, hpost, w, dx, T, tail...,
+                                             p.p, p.c, p.hdr);
+    if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return check_launch(what);
+  };
+  static_assert(kWideBD == kGenBD, "one cluster launch shape");
+  if (!env_int("MHC_B200_GENERIC", 0) && (n == 16 || n == 32)) {
+    // dx rows as 4-element vectors when every row start is aligned for them
+    const int vec_dx =
+        (C % 4 == 0) && ((reinterpret_cast<uintptr_t>(dx) & (4 * sizeof(DXT) - 1)) == 0);
+    if (n == 16)
+      return launch_clusters(k_bwd_wide<16, XT, DT, DXT>, wide_smem_bytes(16), "mhc_bwd(wide)",
+                             C, eps, vec_dx);
+    return launch_clusters(k_bwd_wide<32, XT, DT, DXT>, wide_smem_bytes(32), "mhc_bwd(wide)", C,
+                           eps, vec_dx);
   }
-  // cluster size: split each token's columns while there are few tokens per
-  // resident CTA slot; Q clusters loop over the tokens
-  const int rows = max_partial_rows(T);
-  const int64_t want = 4 * (int64_t)sm_count();
-  int cs = 1;
-  if (env_int("MHC_B200_SPLIT", 1))
-    while (cs < 8 && T * cs < want && C / (2 * cs) >= kGenBD && 2 * cs <= rows) cs *= 2;
-  const int resident = persistent_grid(kern, kGenBD, smem, 1 << 30, 1 << 30);
-  int64_t Q = resident / cs;
-  if (Q > rows / cs) Q = rows / cs;
-  if (Q > T) Q = T;
-  if (Q < 1) Q = 1;
-  const int G = (int)(Q * cs);
-  BwdPtrs p = ws_ptrs(ws, G, n);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)G, 1, 1);
-  cfg.blockDim = dim3(kGenBD, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cs;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, x, d, M, hpre, hpost, w, dx, T, n, C, eps,
-                                           p.p, p.c, p.hdr);
-  if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_bwd(generic): %s", cudaGetErrorString(e));
-  return check_launch("mhc_bwd(generic)");
+  const size_t smem = ((size_t)n * n + 2 * n + 2 * (size_t)(n + 1) * kGenLD) * sizeof(float);
+  return launch_clusters(k_bwd_generic<XT, DT, DXT>, smem, "mhc_bwd(generic)", n, C, eps);
 }
 
 int launch_bwd(const void* x, int xdt, const void* dout, int ddt, const float* M,

@@ -302,6 +302,208 @@ k_sk_batched_bwd(const float* __restrict__ H, const float* __restrict__ dM, int6
   if (valid) sk_row_store<N>(dH + (m * N + row) * N, d);
 }
 
+// ---------------------------------------------------------------------------
+// Batched, n in {1, 2, 4}: one thread per matrix, the whole n x n matrix in
+// registers.  Row sums are sequential and column sums follow the butterfly
+// order of group_sum<N> ((p0 + p2) + (p1 + p3) for n = 4), so every value is
+// bit-identical to the lane kernels above, without lane exchanges; the n
+// independent rows and columns of a half-step give the instruction-level
+// parallelism.  VEC: H, dM and the output are 16-byte aligned (float4 I/O).
+template <int N>
+__device__ __forceinline__ float sk_tree_sum(float (&t)[N]) {
+#pragma unroll
+  for (int o = N / 2; o > 0; o >>= 1)
+#pragma unroll
+    for (int i = 0; i < o; ++i) t[i] = t[i] + t[i + o];
+  return t[0];
+}
+
+template <int N, bool VEC>
+__device__ __forceinline__ void sk_mat_load(const float* __restrict__ src, float (&p)[N][N]) {
+  if constexpr (VEC) {
+#pragma unroll
+    for (int q = 0; q < N * N / 4; ++q) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(src) + q);
+      const int e = 4 * q;
+      p[e / N][e % N] = v.x; p[(e + 1) / N][(e + 1) % N] = v.y;
+      p[(e + 2) / N][(e + 2) % N] = v.z; p[(e + 3) / N][(e + 3) % N] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < N * N; ++e) p[e / N][e % N] = __ldg(src + e);
+  }
+}
+template <int N, bool VEC>
+__device__ __forceinline__ void sk_mat_store(float* __restrict__ dst, const float (&p)[N][N]) {
+  if constexpr (VEC) {
+#pragma unroll
+    for (int q = 0; q < N * N / 4; ++q) {
+      const int e = 4 * q;
+      reinterpret_cast<float4*>(dst)[q] =
+          make_float4(p[e / N][e % N], p[(e + 1) / N][(e + 1) % N],
+                      p[(e + 2) / N][(e + 2) % N], p[(e + 3) / N][(e + 3) % N]);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < N * N; ++e) dst[e] = p[e / N][e % N];
+  }
+}
+
+// exp(h - rowmax) (reference.py:67), row maxima kept for the backward.
+template <int N>
+__device__ __forceinline__ void sk_mat_exp(const float (&h)[N][N], float (&p)[N][N],
+                                           float (&mx)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    mx[i] = h[i][0];
+#pragma unroll
+    for (int j = 1; j < N; ++j) mx[i] = fmaxf(mx[i], h[i][j]);
+#pragma unroll
+    for (int j = 0; j < N; ++j) p[i][j] = expf(h[i][j] - mx[i]);
+  }
+}
+
+// One Sinkhorn iteration (reference.py:36-46): row step, then column step.
+template <int N>
+__device__ __forceinline__ void sk_mat_iter(float (&p)[N][N], float eps) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) s += p[i][j];
+    const float rs = row_scale(s, eps);
+#pragma unroll
+    for (int j = 0; j < N; ++j) p[i][j] *= rs;
+  }
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    float t[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) t[i] = p[i][j];
+    const float cs = col_scale(sk_tree_sum<N>(t), eps);
+#pragma unroll
+    for (int i = 0; i < N; ++i) p[i][j] *= cs;
+  }
+}
+
+template <int N, bool VEC>
+__global__ void __launch_bounds__(128)
+k_sk_mat_fwd(const float* __restrict__ H, int64_t batch, int iters, float eps,
+             float* __restrict__ M) {
+  const int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= batch) return;
+  float h[N][N], p[N][N], mx[N];
+  sk_mat_load<N, VEC>(H + m * N * N, h);
+  sk_mat_exp<N>(h, p, mx);
+  for (int k = 0; k < iters; ++k) sk_mat_iter<N>(p, eps);
+  sk_mat_store<N, VEC>(M + m * N * N, p);
+}
+
+// Backward with checkpoints: the forward replay stores P before every S-th
+// iteration in shared memory ([ceil(iters / S)][N * N][blockDim], thread
+// index fastest: conflict-free); the reverse sweep then re-runs each segment
+// of S iterations from its checkpoint into a register tape and reverses it.
+// Every recomputed P_k is bit-identical to the forward's (same operations in
+// the same order).  Shared memory per thread is ceil(iters / S) * N * N * 4
+// bytes instead of iters * N * N * 4, which keeps a whole 65,536-matrix batch
+// resident at once; the price is a second forward replay.
+template <int N, int S, bool VEC>
+__global__ void __launch_bounds__(128, 4)
+k_sk_mat_bwd(const float* __restrict__ H, const float* __restrict__ dM, int64_t batch,
+             int iters, float eps, float* __restrict__ dH) {
+  extern __shared__ float s_ck[];
+  const int bd = blockDim.x, tid = threadIdx.x;
+  const int64_t m = (int64_t)blockIdx.x * bd + tid;
+  if (m >= batch) return;  // no block-wide synchronisation below
+  auto CK = [&](int seg, int e) -> float& { return s_ck[((size_t)seg * N * N + e) * bd + tid]; };
+
+  float p[N][N], mx[N];
+  {
+    float h[N][N];
+    sk_mat_load<N, VEC>(H + m * N * N, h);
+    sk_mat_exp<N>(h, p, mx);
+  }
+  for (int k = 0; k < iters; ++k) {
+    if (k % S == 0) {
+#pragma unroll
+      for (int e = 0; e < N * N; ++e) CK(k / S, e) = p[e / N][e % N];
+    }
+    sk_mat_iter<N>(p, eps);
+  }
+
+  float d[N][N];
+  sk_mat_load<N, VEC>(dM + m * N * N, d);
+  for (int seg = (iters + S - 1) / S - 1; seg >= 0; --seg) {
+    const int k0 = seg * S, len = min(S, iters - k0);
+    float tp[S][N][N];
+#pragma unroll
+    for (int e = 0; e < N * N; ++e) p[e / N][e % N] = CK(seg, e);
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      if (s < len) {
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+#pragma unroll
+          for (int j = 0; j < N; ++j) tp[s][i][j] = p[i][j];
+        if (s + 1 < len) sk_mat_iter<N>(p, eps);
+      }
+    }
+#pragma unroll
+    for (int s = S - 1; s >= 0; --s) {
+      if (s >= len) continue;
+      // reverse of iteration k0 + s; tp[s] = P before its row step
+      float r[N], rs[N], pb[N][N];
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        r[i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < N; ++j) r[i] += tp[s][i][j];
+        rs[i] = row_scale(r[i], eps);
+#pragma unroll
+        for (int j = 0; j < N; ++j) pb[i][j] = tp[s][i][j] * rs[i];
+      }
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float tc[N], td[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) { tc[i] = pb[i][j]; td[i] = d[i][j] * pb[i][j]; }
+        const float c = sk_tree_sum<N>(tc);
+        const float dcs = sk_tree_sum<N>(td);
+        const float cs = col_scale(c, eps);
+        const float g = recip_grad(dcs, c, cs, eps);
+#pragma unroll
+        for (int i = 0; i < N; ++i) d[i][j] = d[i][j] * cs + g;
+      }
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        float drs = 0.f;
+#pragma unroll
+        for (int j = 0; j < N; ++j) drs += d[i][j] * tp[s][i][j];
+        const float dr = recip_grad(drs, r[i], rs[i], eps);
+#pragma unroll
+        for (int j = 0; j < N; ++j) d[i][j] = d[i][j] * rs[i] + dr;
+      }
+    }
+  }
+  // through exp(h - rowmax): the max's gradient is split over ties
+  float h[N][N];
+  sk_mat_load<N, VEC>(H + m * N * N, h);
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float Ssum = 0.f, cnt = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      d[i][j] *= expf(h[i][j] - mx[i]);
+      Ssum += d[i][j];
+      cnt += (h[i][j] == mx[i]) ? 1.f : 0.f;
+    }
+    const float share = Ssum / cnt;
+#pragma unroll
+    for (int j = 0; j < N; ++j) d[i][j] -= (h[i][j] == mx[i]) ? share : 0.f;
+  }
+  sk_mat_store<N, VEC>(dH + m * N * N, d);
+}
+
 // Batched fallback for n that does not divide 32 (or a tape too large for
 // shared memory): persistent CTAs, one matrix at a time, tape in the
 // workspace (one tape region per CTA).
@@ -381,14 +583,67 @@ static int sk_bwd_small(const float* H, const float* dM, int64_t batch, int iter
   return check_launch("sinkhorn_batched_bwd");
 }
 
+// One thread per matrix (n in {1, 2, 4}); float4 I/O when every pointer is
+// 16-byte aligned (a matrix of n * n floats then starts on a 16-byte boundary
+// for n in {2, 4}).
+constexpr int kSkMatThreads = 128;
+template <int N> constexpr int sk_mat_seg() { return N == 4 ? 4 : (N == 2 ? 10 : 20); }
+static size_t sk_mat_ck_bytes(int n, int iters) {
+  const int S = n == 4 ? sk_mat_seg<4>() : (n == 2 ? sk_mat_seg<2>() : sk_mat_seg<1>());
+  return (size_t)((iters + S - 1) / S) * n * n * sizeof(float) * kSkMatThreads;
+}
+// The checkpoint path keeps its checkpoints within 96 KB of shared memory
+// per CTA (iters <= 48 for n = 4, two CTAs per SM still resident); longer
+// chains use the lane kernels' full tape or the workspace path.
+static bool sk_mat_bwd_ok(int n, int iters) {
+  return (n == 1 || n == 2 || n == 4) && sk_mat_ck_bytes(n, iters) <= 96 * 1024;
+}
+static bool aligned16(const void* a, const void* b, const void* c) {
+  return ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+           reinterpret_cast<uintptr_t>(c)) & 15) == 0;
+}
+
+template <int N>
+static int sk_mat_fwd(const float* H, int64_t batch, int iters, float eps, float* M,
+                      cudaStream_t st) {
+  const int64_t blocks = (batch + kSkMatThreads - 1) / kSkMatThreads;
+  if (N > 1 && aligned16(H, M, M))
+    k_sk_mat_fwd<N, N != 1><<<(unsigned)blocks, kSkMatThreads, 0, st>>>(H, batch, iters, eps, M);
+  else
+    k_sk_mat_fwd<N, false><<<(unsigned)blocks, kSkMatThreads, 0, st>>>(H, batch, iters, eps, M);
+  return check_launch("sinkhorn_batched_fwd");
+}
+
+template <int N>
+static int sk_mat_bwd(const float* H, const float* dM, int64_t batch, int iters, float eps,
+                      float* dH, cudaStream_t st) {
+  constexpr int S = sk_mat_seg<N>();
+  const size_t smem = sk_mat_ck_bytes(N, iters);
+  const int64_t blocks = (batch + kSkMatThreads - 1) / kSkMatThreads;
+  const bool vec = N > 1 && aligned16(H, dM, dH);
+  {
+    const cudaError_t e = vec ? allow_dyn_smem(k_sk_mat_bwd<N, S, N != 1>, smem)
+                              : allow_dyn_smem(k_sk_mat_bwd<N, S, false>, smem);
+    if (e != cudaSuccess)
+      return set_error(MHC_ERR_CUDA, "sinkhorn_batched_bwd: %s", cudaGetErrorString(e));
+  }
+  if (vec)
+    k_sk_mat_bwd<N, S, N != 1><<<(unsigned)blocks, kSkMatThreads, smem, st>>>(H, dM, batch, iters,
+                                                                             eps, dH);
+  else
+    k_sk_mat_bwd<N, S, false><<<(unsigned)blocks, kSkMatThreads, smem, st>>>(H, dM, batch, iters,
+                                                                            eps, dH);
+  return check_launch("sinkhorn_batched_bwd");
+}
+
 int launch_sk_batched_fwd(const float* H, int64_t batch, int n, int iters, float eps, float* M,
                           void* ws, size_t ws_bytes, cudaStream_t st) {
   (void)ws; (void)ws_bytes;
   if (batch == 0) return MHC_OK;
   switch (n) {
-    case 1: return sk_fwd_small<1>(H, batch, iters, eps, M, st);
-    case 2: return sk_fwd_small<2>(H, batch, iters, eps, M, st);
-    case 4: return sk_fwd_small<4>(H, batch, iters, eps, M, st);
+    case 1: return sk_mat_fwd<1>(H, batch, iters, eps, M, st);
+    case 2: return sk_mat_fwd<2>(H, batch, iters, eps, M, st);
+    case 4: return sk_mat_fwd<4>(H, batch, iters, eps, M, st);
     case 8: return sk_fwd_small<8>(H, batch, iters, eps, M, st);
     case 16: return sk_fwd_small<16>(H, batch, iters, eps, M, st);
     case 32: return sk_fwd_small<32>(H, batch, iters, eps, M, st);
@@ -402,6 +657,14 @@ int launch_sk_batched_fwd(const float* H, int64_t batch, int n, int iters, float
 int launch_sk_batched_bwd(const float* H, const float* dM, int64_t batch, int n, int iters,
                           float eps, float* dH, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (batch == 0) return MHC_OK;
+  if (sk_mat_bwd_ok(n, iters)) {
+    switch (n) {
+      case 1: return sk_mat_bwd<1>(H, dM, batch, iters, eps, dH, st);
+      case 2: return sk_mat_bwd<2>(H, dM, batch, iters, eps, dH, st);
+      case 4: return sk_mat_bwd<4>(H, dM, batch, iters, eps, dH, st);
+      default: break;
+    }
+  }
   if (sk_small_path(n) && sk_bwd_threads(n, iters) > 0) {
     switch (n) {
       case 1: return sk_bwd_small<1>(H, dM, batch, iters, eps, dH, st);

@@ -320,3 +320,46 @@ def test_backward_16bit_dout(dt, n, C):
             assert rel_err(got[k], ref[k]) < half_tol, (name, rel_err(got[k], ref[k]))
         else:
             assert_close_to_reference(name, got[k], ref[k], ref32[k])
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("T,n,C", [(600, 32, 512), (257, 16, 129), (3, 32, 4), (64, 16, 4096),
+                                   (40, 32, 1030), (0, 32, 256)])
+def test_wide_backward_matches_oracle_and_generic(dt, T, n, C):
+    """n = 16 / 32 run the register-tiled backward (8 x 8 dM blocks over
+    column slices, 4 x 4(8) dx blocks): many tokens per CTA, ragged tiles and
+    odd C (scalar dx stores), a row narrower than one tile, a cluster split
+    with a C that is not a multiple of the slice, and T = 0.  x, d_out and dx
+    share dtype dt.  Results match the float64 oracle and the any-n kernel."""
+    g = torch.Generator().manual_seed(T * 31 + n + C)
+    x = torch.randn(T, n, C, generator=g).to(dt)
+    params = [0.5 * torch.randn(n, generator=g), 0.5 * torch.randn(n, generator=g),
+              torch.randn(n, n, generator=g), 1 + 0.1 * torch.randn(C, generator=g)]
+    d_out = torch.randn(T, n, C, generator=g).to(dt)
+    rd = None if dt == torch.float32 else dt
+    got = _layer_grads(cu(x, dt), [cu(p) for p in params], cu(d_out, dt), 20, 1e-5,
+                       return_dtype=rd)
+    os.environ["MHC_B200_GENERIC"] = "1"
+    try:
+        gen = _layer_grads(cu(x, dt), [cu(p) for p in params], cu(d_out, dt), 20, 1e-5,
+                           return_dtype=rd)
+    finally:
+        del os.environ["MHC_B200_GENERIC"]
+    names = ("out", "dx", "dH_pre", "dH_post", "dH_res", "d_w")
+    if T == 0:
+        for name, a in zip(names[2:], got[2:]):
+            assert torch.count_nonzero(a) == 0, name
+        return
+    ref = O.layer_grads(x, *params, d_out.float(), 20, 1e-5, dtype=F64)
+    ref32 = O.layer_grads(x, *params, d_out.float(), 20, 1e-5, dtype=torch.float32)
+    half_tol = {torch.bfloat16: 2e-2, torch.float16: 5e-3}.get(dt)
+    for k, name in enumerate(names):
+        if half_tol is not None and name in ("out", "dx"):
+            assert rel_err(got[k], ref[k]) < half_tol, (name, rel_err(got[k], ref[k]))
+        else:
+            assert_close_to_reference(name, got[k], ref[k], ref32[k])
+        # the any-n kernel: same math, another summation order
+        if half_tol is not None and name in ("out", "dx"):
+            assert rel_err(got[k], gen[k]) < half_tol, (name, rel_err(got[k], gen[k]))
+        else:
+            assert_close_to_reference(name, got[k], gen[k].double(), ref32[k])

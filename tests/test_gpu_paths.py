@@ -41,6 +41,47 @@ def test_batched_sinkhorn_matches_oracle(n):
     assert max_abs(M1, M[0]) < 1e-6
 
 
+@pytest.mark.parametrize("n", [1, 2, 4])
+@pytest.mark.parametrize("iters", [0, 1, 7, 20, 37, 64])
+def test_batched_sinkhorn_iteration_counts(n, iters):
+    """n <= 4 runs one thread per matrix with checkpointed replay: iteration
+    counts that are not a multiple of the checkpoint spacing, counts whose
+    checkpoints need more than the default 48 KB of shared memory, and a
+    count beyond the checkpoint path's limit (64: lane kernels' full tape)."""
+    g = torch.Generator().manual_seed(100 * n + iters)
+    B = 300
+    H = torch.randn(B, n, n, generator=g)
+    dM = torch.randn(B, n, n, generator=g)
+    M_ref, dH_ref = O.sinkhorn_grads(H, dM, iters, 1e-5, dtype=F64)
+    Hc = cu(H).requires_grad_(True)
+    M = metal.sinkhorn_knopp_batched(Hc, iters, 1e-5)
+    (dH,) = torch.autograd.grad(M, [Hc], cu(dM))
+    assert max_abs(M, M_ref) < 2e-6
+    assert rel_err(dH, dH_ref) < 1e-5
+
+
+@pytest.mark.parametrize("n", [2, 4])
+def test_batched_sinkhorn_unaligned_pointers(n):
+    """Inputs that start 4 bytes past a 16-byte boundary take the scalar-load
+    variant and give the same bits as aligned inputs."""
+    g = torch.Generator().manual_seed(7 + n)
+    B = 129
+    H = torch.randn(B, n, n, generator=g)
+    dM = torch.randn(B, n, n, generator=g)
+    bh = torch.empty(B * n * n + 1, device=DEV)
+    bd = torch.empty(B * n * n + 1, device=DEV)
+    Hu = bh[1:].view(B, n, n)
+    dMu = bd[1:].view(B, n, n)
+    Hu.copy_(cu(H))
+    dMu.copy_(cu(dM))
+    assert Hu.data_ptr() % 16 != 0 and dMu.data_ptr() % 16 != 0
+    from mhc_b200 import _kernels as K
+    M_a, M_u = K.sinkhorn_batched_fwd(cu(H), 20, 1e-5), K.sinkhorn_batched_fwd(Hu, 20, 1e-5)
+    dH_a = K.sinkhorn_batched_bwd(cu(H), cu(dM), 20, 1e-5)
+    dH_u = K.sinkhorn_batched_bwd(Hu, dMu, 20, 1e-5)
+    assert torch.equal(M_a, M_u) and torch.equal(dH_a, dH_u)
+
+
 def test_batched_sinkhorn_config3_sums_and_stability():
     """65,536 4x4 logits ~ N(0,1), 20 iterations.
     Column sums are 1; row/col sums equal the oracle's to 1e-6; the result
