@@ -628,9 +628,11 @@ def run_configs(args):
                     p_.grad = None
                 layer(xg).backward(d)
 
+            _, per32 = _kernel_us_per_step(fb, dev)
             rows.append({"B": B, "C": C, "fwd_us": _median_us(fo, dev),
                          "fwd_graph_us": _graph_us(fo, dev),
                          "fwd_bwd_graph_us": _graph_us(fb, dev),
+                         "fwd_bwd_kernels_us": {k: round(v, 1) for k, v in per32.items()},
                          "reference_m4pro_fwd_us": ref_us})
         out.append({"metric": "MHCLayer per-call time at the reference's published shapes "
                               "(n=32, fp32; forward, and forward+backward)",

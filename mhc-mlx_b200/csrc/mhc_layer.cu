@@ -834,55 +834,77 @@ k_bwd_generic(const XT* __restrict__ x, const DT* __restrict__ dout, const float
   cl.sync();  // the last token's partial pairs stay readable until every CTA has them
 }
 
-// Backward for n in {16, 32}: the structure of k_bwd_generic (cluster column
-// slices, pass 1 per token, tiles of 128 staged columns), with the two n x n
-// contractions of a tile register-tiled for a compile-time N:
-//   dx = M^T d + H_pre dya: thread (jg, cg) owns streams 4jg..4jg+3 of DXC
-//     groups of 4 columns; per stream i one float4 of M[i][4jg..] and DXC
-//     float4s of d[i][cols] feed 16 DXC FMAs;
-//   dM += d x^T: one 8 x 8 register block per thread, the tile's columns
-//     split over SL = 128 / (N/8)^2 slices (16 scalar loads for 64 FMAs);
-//     dH_post_i = sum d_i (y inv w) and dH_pre_j = sum dya x_j ride along,
-//     8 / (N/8) rows and columns per thread.
+// Backward for n in {16, 32}: cluster column slices like k_bwd_generic, in
+// two passes over a token's slice with compile-time N, so that the two
+// n x n contractions are register-tiled and d_out is the only tensor read
+// twice:
+//   pass 1, per tile of 128 columns: stage x and d_out; per column y = sum
+//     H_pre x, dyn = sum H_post d (kept in shared memory for pass 2) and the
+//     token sums ss, pd; dM += d x^T as one 8 x 8 register block per thread
+//     over SL = 128 / (N/8)^2 column slices (16 scalar loads for 64 FMAs);
+//     and per-token sums that do not need inv yet:
+//       U_i = sum d_i y w,  A_j = sum dyn w x_j,  B_j = sum y x_j,
+//     since dH_post_i = inv U_i and dH_pre_j = sum dya x_j = inv A_j - k2 B_j
+//     (dya = dyn w inv - k2 y), folded in once the token's inv and k2 are
+//     known (8 / (N/8) rows and columns per thread);
+//   pass 2, per tile: stage d_out and dya, then dx = M^T d + H_pre dya with
+//     thread (jg, cg) owning streams 4jg..4jg+3 of DXC groups of 4 columns
+//     (one float4 of M and DXC float4s of d per stream feed 16 DXC FMAs).
+// PIPE (fp32 x and d_out, 16-byte aligned rows): two staging buffers; the
+// next tile (of either pass, or of the next token) is copied with cp.async
+// while the current one is computed, so load latency overlaps the
+// contractions.  Otherwise each thread loads its column of the tile.
 // Staged row i starts at wide_row(i) = i * kWideLD + (i / 8) * 8 floats, so
 // the 8-row blocks read by one warp fall on distinct banks and every row
-// start is 16-byte aligned.  The slices' dM blocks are added in slice order
-// at the end (no atomics: bitwise reproducible).
+// start is 16-byte aligned.  A slice holds at most kWideSlice columns (the
+// launcher picks the cluster size).  The slices' dM blocks are added in slice
+// order at the end (no atomics: bitwise reproducible).
 constexpr int kWideBD = 128;
 constexpr int kWideLD = kWideBD + 4;
+constexpr int kWideSlice = 4096;
 __host__ __device__ constexpr int wide_row(int i) { return i * kWideLD + (i >> 3) * 8; }
-__host__ __device__ constexpr size_t wide_smem_bytes(int n) {
-  return 2 * (size_t)(wide_row(n) + kWideLD) * sizeof(float);
+// [NBUF buffers: x rows | d rows][3 extra rows: y w, dyn w or dya, y][y, dyn per slice column]
+__host__ __device__ constexpr int wide_ex_off(int n, int nbuf) { return nbuf * 2 * wide_row(n); }
+__host__ __device__ constexpr size_t wide_smem_bytes(int n, int nbuf) {
+  return ((size_t)wide_ex_off(n, nbuf) + 3 * kWideLD + 2 * (size_t)kWideSlice) * sizeof(float);
 }
 
-template <int N, typename XT, typename DT, typename DXT>
-__global__ void __launch_bounds__(kWideBD, 3)
+template <int N, typename XT, typename DT, typename DXT, bool PIPE>
+__global__ void __launch_bounds__(kWideBD, PIPE ? 2 : 3)
 k_bwd_wide(const XT* __restrict__ x, const DT* __restrict__ dout, const float* __restrict__ Mg,
            const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
            const float* __restrict__ w, DXT* __restrict__ dx, int64_t T, int C, float eps,
            int vec_dx, float* __restrict__ ws_p, float* __restrict__ ws_c,
            int* __restrict__ ws_hdr) {
   static_assert(N == 16 || N == 32, "register tiling for n = 16 and n = 32");
+  static_assert(!PIPE || (std::is_same<XT, float>::value && std::is_same<DT, float>::value),
+                "cp.async staging copies fp32 rows");
+  constexpr int NBUF = PIPE ? 2 : 1;
   constexpr int NB = N / 8;                 // 8 x 8 blocks per edge
   constexpr int SL = kWideBD / (NB * NB);   // column slices of the dM product
-  constexpr int HR = 8 / NB;                // dH_post rows / dH_pre columns per thread
+  constexpr int HR = 8 / NB;                // dH rows / columns per thread
   constexpr int CG = kWideBD / (N / 4);     // 4-column groups in a dx row pass
   constexpr int DXC = kWideBD / (4 * CG);   // 4-column groups per thread
   constexpr int P = N * N + 2 * N;
-  static_assert(P <= 2 * (wide_row(N) + kWideLD), "partials fit the staging area");
+  constexpr int BUFSZ = 2 * wide_row(N);
+  static_assert(P <= wide_ex_off(N, 1), "partials fit the staging area");
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
   const int cs = (int)cl.num_blocks(), rank = (int)cl.block_rank();
   const int64_t q0 = blockIdx.x / cs, Q = gridDim.x / cs;
   const int chunk = (((C + cs - 1) / cs) + 3) & ~3;  // slice starts on 4-column groups
   const int cl0 = min(C, rank * chunk), cl1 = min(C, cl0 + chunk);
+  const int K = (cl1 - cl0 + kWideBD - 1) / kWideBD;  // tiles per pass
   __shared__ float2 s_part[2];
   __shared__ float red[2][64];
   __shared__ __align__(16) float sM[N * N];
   __shared__ float shpre[N], shpost[N];
   extern __shared__ __align__(16) float smem[];
-  float* sx = smem;                         // rows 0..N-1: x, row N: y inv w
-  float* sd = smem + wide_row(N) + kWideLD; // rows 0..N-1: d_out, row N: dya
+  float* ex_yw = smem + wide_ex_off(N, NBUF);  // y w
+  float* ex_dw = ex_yw + kWideLD;              // dyn w (pass 1) / dya (pass 2)
+  float* ex_y = ex_dw + kWideLD;               // y
+  float* sy = ex_y + kWideLD;                  // y of the slice's columns
+  float* sdy = sy + kWideSlice;                // dyn of the slice's columns
   const int tid = threadIdx.x;
   for (int e = tid; e < N * N; e += kWideBD) sM[e] = Mg[e];
   if (tid < N) { shpre[tid] = hpre_g[tid]; shpost[tid] = hpost_g[tid]; }
@@ -903,20 +925,108 @@ k_bwd_wide(const XT* __restrict__ x, const DT* __restrict__ dout, const float* _
 
   const int64_t rs = (int64_t)N * C;
   const float invC = 1.0f / (float)C;
+
+  // cp.async of the next tile in the CTA's order (token, pass, tile) into
+  // buffer b: pass 0 copies x and d_out rows, pass 1 d_out rows only.  The
+  // slice and C are multiples of 4 columns, so a tile is whole 16-byte
+  // chunks.  Every call commits one group (empty past the last tile).
+  int64_t nt = q0;
+  int npass = 0, nk = 0;
+  auto issue_next = [&](int b) {
+    if constexpr (PIPE) {
+      if (K > 0 && nt < T) {
+        float* bx = smem + b * BUFSZ;
+        float* bd = bx + wide_row(N);
+        const int c0 = cl0 + nk * kWideBD, nch = min(kWideBD, cl1 - c0) / 4;
+        const float* xs = reinterpret_cast<const float*>(x) + nt * rs + c0;
+        const float* ds = reinterpret_cast<const float*>(dout) + nt * rs + c0;
+        const int rows = npass == 0 ? 2 * N : N;
+        for (int e = tid; e < rows * (kWideBD / 4); e += kWideBD) {
+          const int r = e / (kWideBD / 4), ch = e % (kWideBD / 4);
+          if (ch < nch) {
+            if (npass == 0 && r < N) {
+              cp_async16(bx + wide_row(r) + 4 * ch, xs + (int64_t)r * C + 4 * ch);
+            } else {
+              const int i = npass == 0 ? r - N : r;
+              cp_async16(bd + wide_row(i) + 4 * ch, ds + (int64_t)i * C + 4 * ch);
+            }
+          }
+        }
+      }
+      cp_async_commit();
+      if (++nk >= K) { nk = 0; if (++npass == 2) { npass = 0; nt += Q; } }
+    }
+  };
+  int buf = 0;
+  issue_next(0);
+
   int par = 0;
   for (int64_t t = q0; t < T; t += Q) {
     const XT* xt = x + t * rs;
     const DT* dt = dout + t * rs;
-    float ss = 0.f, pd = 0.f;
-    for (int c = cl0 + tid; c < cl1; c += kWideBD) {
+    float ss = 0.f, pd = 0.f, U[HR], A[HR], B[HR];
+#pragma unroll
+    for (int r = 0; r < HR; ++r) { U[r] = 0.f; A[r] = 0.f; B[r] = 0.f; }
+    // ---- pass 1 ----
+    for (int k = 0; k < K; ++k) {
+      const int c0 = cl0 + k * kWideBD, width = min(kWideBD, cl1 - c0);
+      float* bx = smem + buf * BUFSZ;
+      float* bd = bx + wide_row(N);
+      const int c = c0 + tid;
+      const bool ok = tid < width;
       float y = 0.f, dyn = 0.f;
+      if constexpr (PIPE) {
+        issue_next(buf ^ 1);
+        cp_async_wait_group<1>();
+        __syncthreads();  // this tile's copies from every thread have landed
+        if (ok) {
 #pragma unroll 8
-      for (int i = 0; i < N; ++i) {
-        y = fmaf(shpre[i], to_f(xt[(int64_t)i * C + c]), y);
-        dyn = fmaf(shpost[i], to_f(dt[(int64_t)i * C + c]), dyn);
+          for (int i = 0; i < N; ++i) {
+            y = fmaf(shpre[i], bx[wide_row(i) + tid], y);
+            dyn = fmaf(shpost[i], bd[wide_row(i) + tid], dyn);
+          }
+        }
+      } else {
+#pragma unroll 8
+        for (int i = 0; i < N; ++i) {
+          const float xv = ok ? to_f(xt[(int64_t)i * C + c]) : 0.f;
+          const float dv = ok ? to_f(dt[(int64_t)i * C + c]) : 0.f;
+          bx[wide_row(i) + tid] = xv;
+          bd[wide_row(i) + tid] = dv;
+          y = fmaf(shpre[i], xv, y);
+          dyn = fmaf(shpost[i], dv, dyn);
+        }
       }
+      const float wv = ok ? __ldg(w + c) : 0.f;
       ss = fmaf(y, y, ss);
-      pd = fmaf(dyn * __ldg(w + c), y, pd);
+      pd = fmaf(dyn * wv, y, pd);
+      ex_yw[tid] = y * wv;
+      ex_dw[tid] = dyn * wv;
+      ex_y[tid] = y;
+      if (ok) { sy[c - cl0] = y; sdy[c - cl0] = dyn; }
+      __syncthreads();
+      for (int cc = sl; cc < width; cc += SL) {
+        float dv[8], xv[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) {
+          dv[a] = bd[wide_row(8 * bi + a) + cc];
+          xv[a] = bx[wide_row(8 * bj + a) + cc];
+        }
+#pragma unroll
+        for (int a = 0; a < 8; ++a)
+#pragma unroll
+          for (int b = 0; b < 8; ++b) acc[a][b] = fmaf(dv[a], xv[b], acc[a][b]);
+        const float yw = ex_yw[cc], dw = ex_dw[cc], yv = ex_y[cc];
+#pragma unroll
+        for (int r = 0; r < HR; ++r) {
+          U[r] = fmaf(bd[wide_row(8 * bi + HR * bj + r) + cc], yw, U[r]);
+          const float xj = bx[wide_row(8 * bj + HR * bi + r) + cc];
+          A[r] = fmaf(dw, xj, A[r]);
+          B[r] = fmaf(yv, xj, B[r]);
+        }
+      }
+      __syncthreads();
+      if constexpr (PIPE) buf ^= 1;
     }
     const float2 part = block_sum2(ss, pd, red[par]);
     if (tid == 0) s_part[par] = part;
@@ -930,36 +1040,39 @@ k_bwd_wide(const XT* __restrict__ x, const DT* __restrict__ dout, const float* _
     par ^= 1;
     const float inv = inv_rms(red2.x, C, eps);
     const float k2 = (red2.y * (inv * inv * inv)) * invC;
+#pragma unroll
+    for (int r = 0; r < HR; ++r) {
+      hpo[r] = fmaf(inv, U[r], hpo[r]);
+      hpr[r] += inv * A[r] - k2 * B[r];
+    }
+    // ---- pass 2: dx ----
     DXT* dxt = dx + t * rs;
-    for (int c0 = cl0; c0 < cl1; c0 += kWideBD) {
-      const int width = min(kWideBD, cl1 - c0);
-      {  // stage the tile: thread tid owns column c0 + tid
-        const int c = c0 + tid;
-        const bool ok = tid < width;
-        float y = 0.f, dyn = 0.f;
-#pragma unroll 8
-        for (int i = 0; i < N; ++i) {
-          const float xv = ok ? to_f(xt[(int64_t)i * C + c]) : 0.f;
-          const float dv = ok ? to_f(dt[(int64_t)i * C + c]) : 0.f;
-          sx[wide_row(i) + tid] = xv;
-          sd[wide_row(i) + tid] = dv;
-          y = fmaf(shpre[i], xv, y);
-          dyn = fmaf(shpost[i], dv, dyn);
-        }
-        const float wv = ok ? __ldg(w + c) : 0.f;
-        const float yi = y * inv;
-        sx[wide_row(N) + tid] = yi * wv;
-        sd[wide_row(N) + tid] = ok ? (dyn * wv) * inv - k2 * y : 0.f;
-        if (ok) wc[c] = fmaf(dyn, yi, wc[c]);
+    for (int k = 0; k < K; ++k) {
+      const int c0 = cl0 + k * kWideBD, width = min(kWideBD, cl1 - c0);
+      float* bd = smem + buf * BUFSZ + wide_row(N);
+      const int c = c0 + tid;
+      const bool ok = tid < width;
+      if constexpr (PIPE) {
+        issue_next(buf ^ 1);
+        cp_async_wait_group<1>();
+      } else {
+#pragma unroll 16
+        for (int i = 0; i < N; ++i) bd[wide_row(i) + tid] = ok ? to_f(dt[(int64_t)i * C + c]) : 0.f;
+      }
+      if (ok) {
+        const float y = sy[c - cl0], dyn = sdy[c - cl0], wv = __ldg(w + c);
+        ex_dw[tid] = (dyn * wv) * inv - k2 * y;
+        wc[c] = fmaf(dyn, y * inv, wc[c]);
+      } else {
+        ex_dw[tid] = 0.f;
       }
       __syncthreads();
-      // dx for streams 4jg..4jg+3
 #pragma unroll
       for (int q = 0; q < DXC; ++q) {
         const int cb = 4 * cgi + 4 * CG * q;
         if (cb < width) {
           float o[4][4];
-          const float4 g4 = *reinterpret_cast<const float4*>(sd + wide_row(N) + cb);
+          const float4 g4 = *reinterpret_cast<const float4*>(ex_dw + cb);
 #pragma unroll
           for (int a = 0; a < 4; ++a) {
             const float hp = shpre[4 * jg + a];
@@ -968,7 +1081,7 @@ k_bwd_wide(const XT* __restrict__ x, const DT* __restrict__ dout, const float* _
 #pragma unroll 8
           for (int i = 0; i < N; ++i) {
             const float4 m4 = *reinterpret_cast<const float4*>(sM + i * N + 4 * jg);
-            const float4 d4 = *reinterpret_cast<const float4*>(sd + wide_row(i) + cb);
+            const float4 d4 = *reinterpret_cast<const float4*>(bd + wide_row(i) + cb);
             const float mv[4] = {m4.x, m4.y, m4.z, m4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
             for (int a = 0; a < 4; ++a)
@@ -988,52 +1101,34 @@ k_bwd_wide(const XT* __restrict__ x, const DT* __restrict__ dout, const float* _
           }
         }
       }
-      // dM block (8bi.., 8bj..) over this slice's columns, plus the
-      // dH_post rows 8bi + HR bj + r and dH_pre columns 8bj + HR bi + r
-      for (int c = sl; c < width; c += SL) {
-        float dv[8], xv[8];
-#pragma unroll
-        for (int a = 0; a < 8; ++a) {
-          dv[a] = sd[wide_row(8 * bi + a) + c];
-          xv[a] = sx[wide_row(8 * bj + a) + c];
-        }
-#pragma unroll
-        for (int a = 0; a < 8; ++a)
-#pragma unroll
-          for (int b = 0; b < 8; ++b) acc[a][b] = fmaf(dv[a], xv[b], acc[a][b]);
-        const float yw = sx[wide_row(N) + c], ga = sd[wide_row(N) + c];
-#pragma unroll
-        for (int r = 0; r < HR; ++r) {
-          hpo[r] = fmaf(sd[wide_row(8 * bi + HR * bj + r) + c], yw, hpo[r]);
-          hpr[r] = fmaf(ga, sx[wide_row(8 * bj + HR * bi + r) + c], hpr[r]);
-        }
-      }
       __syncthreads();
+      if constexpr (PIPE) buf ^= 1;
     }
   }
+  if constexpr (PIPE) cp_async_wait_all();  // only empty groups can remain
   // add the slices' blocks in slice order in the (now free) staging area
-  float* buf = smem;
+  float* sbuf = smem;
   for (int s = 0; s < SL; ++s) {
     if (sl == s) {
 #pragma unroll
       for (int a = 0; a < 8; ++a)
 #pragma unroll
         for (int b = 0; b < 8; ++b) {
-          float& e = buf[(8 * bi + a) * N + 8 * bj + b];
+          float& e = sbuf[(8 * bi + a) * N + 8 * bj + b];
           e = (s == 0 ? 0.f : e) + acc[a][b];
         }
 #pragma unroll
       for (int r = 0; r < HR; ++r) {
-        float& e1 = buf[N * N + N + 8 * bi + HR * bj + r];  // dH_post_i
+        float& e1 = sbuf[N * N + N + 8 * bi + HR * bj + r];  // dH_post_i
         e1 = (s == 0 ? 0.f : e1) + hpo[r];
-        float& e2 = buf[N * N + 8 * bj + HR * bi + r];      // dH_pre_j
+        float& e2 = sbuf[N * N + 8 * bj + HR * bi + r];      // dH_pre_j
         e2 = (s == 0 ? 0.f : e2) + hpr[r];
       }
     }
     __syncthreads();
   }
   float* pr = ws_p + (size_t)blockIdx.x * P;
-  for (int e = tid; e < P; e += kWideBD) pr[e] = buf[e];
+  for (int e = tid; e < P; e += kWideBD) pr[e] = sbuf[e];
   if (blockIdx.x == 0 && tid == 0) ws_hdr[0] = gridDim.x;
   cl.sync();  // the last token's partial pairs stay readable until every CTA has them
 }
@@ -1111,18 +1206,28 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
     }
     __syncthreads();
   } else {
-    for (int e0 = 0; e0 < P; e0 += 32) {
-      const int e = e0 + lane;
-      part[r0][lane] = (e < P) ? sliced_row_sum(wp + e, P, G, r0) : 0.f;
-      __syncthreads();
-      if (r0 == 0 && e < P) {
-        float s = 0.f;
+    // Larger n: thread tid owns entries tid + k * kFinBD and adds their G
+    // partial rows in row order, KE entries at a time, so each row step
+    // issues KE independent loads (and the unrolled steps several rows'
+    // worth) instead of one dependent load per 32-entry group.
+    constexpr int KE = 5;
+    for (int base = 0; base < P; base += KE * kFinBD) {
+      float s[KE];
+      int ee[KE];
 #pragma unroll
-        for (int q = 0; q < kFinSlices; ++q) s += part[q][lane];
-        emit(e, s);
+      for (int k = 0; k < KE; ++k) { ee[k] = base + tid + k * kFinBD; s[k] = 0.f; }
+#pragma unroll 4
+      for (int g = 0; g < G; ++g) {
+        const float* row = wp + (size_t)g * P;
+#pragma unroll
+        for (int k = 0; k < KE; ++k)
+          if (ee[k] < P) s[k] += row[ee[k]];
       }
-      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < KE; ++k)
+        if (ee[k] < P) emit(ee[k], s[k]);
     }
+    __syncthreads();
   }
   if (tid < n) {
     if (hpre_raw && dhpre_raw) {
@@ -1543,21 +1648,33 @@ static int bwd_typed(const void* xv, const void* dv, const float* M, const float
   // Cluster launch shared by the wide and generic kernels: split each
   // token's columns over cs CTAs while there are few tokens per resident
   // CTA slot; Q clusters loop over the tokens.
-  auto launch_clusters = [&](auto kern, size_t smem, const char* what, auto... tail) -> int {
+  auto launch_clusters = [&](auto kern, size_t smem, int cs_min, const char* what,
+                             auto... tail) -> int {
     {
       cudaError_t e = allow_dyn_smem(kern, smem);
       if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
     }
     const int rows = max_partial_rows(T);
-    const int64_t want = 4 * (int64_t)sm_count();
-    int cs = 1;
-    if (env_int("MHC_B200_SPLIT", 1))
-      while (cs < 8 && T * cs < want && C / (2 * cs) >= kGenBD && 2 * cs <= rows) cs *= 2;
     const int resident = persistent_grid(kern, kGenBD, smem, 1 << 30, 1 << 30);
-    int64_t Q = resident / cs;
-    if (Q > rows / cs) Q = rows / cs;
-    if (Q > T) Q = T;
-    if (Q < 1) Q = 1;
+    auto clusters = [&](int c) -> int64_t {
+      int64_t q = resident / c;
+      if (q > rows / c) q = rows / c;
+      if (q > T) q = T;
+      return q < 1 ? 1 : q;
+    };
+    // cluster size with the least work for the busiest CTA: token rounds
+    // ceil(T / Q) times slice width ceil(C / cs); the smaller cs on ties
+    int cs = cs_min;
+    if (env_int("MHC_B200_SPLIT", 1)) {
+      int64_t best = -1;
+      for (int c = cs_min; c <= 8; c *= 2) {
+        if (c > cs_min && (C / c < kGenBD || c > rows)) break;
+        const int64_t q = clusters(c);
+        const int64_t work = ((T + q - 1) / q) * ((C + c - 1) / c);
+        if (best < 0 || work < best) { best = work; cs = c; }
+      }
+    }
+    const int64_t Q = clusters(cs);
     const int G = (int)(Q * cs);
     BwdPtrs p = ws_ptrs(ws, G, n);
     cudaLaunchConfig_t cfg = {};
@@ -1578,18 +1695,33 @@ static int bwd_typed(const void* xv, const void* dv, const float* M, const float
     return check_launch(what);
   };
   static_assert(kWideBD == kGenBD, "one cluster launch shape");
-  if (!env_int("MHC_B200_GENERIC", 0) && (n == 16 || n == 32)) {
+  // the wide kernel keeps y and dyn of its column slice in shared memory: at
+  // most kWideSlice columns per CTA, so wider rows need a cluster split
+  int wide_cs = 1;
+  while (wide_cs <= 8 && ((((C + wide_cs - 1) / wide_cs) + 3) & ~3) > kWideSlice) wide_cs *= 2;
+  if (!env_int("MHC_B200_GENERIC", 0) && (n == 16 || n == 32) && T > 0 && wide_cs <= 8 &&
+      wide_cs <= max_partial_rows(T)) {
     // dx rows as 4-element vectors when every row start is aligned for them
     const int vec_dx =
         (C % 4 == 0) && ((reinterpret_cast<uintptr_t>(dx) & (4 * sizeof(DXT) - 1)) == 0);
+    // fp32 rows staged with cp.async when every row start is 16-byte aligned
+    if constexpr (std::is_same<XT, float>::value && std::is_same<DT, float>::value) {
+      if (C % 4 == 0 && aligned16(x) && aligned16(d) && env_int("MHC_B200_PIPE", 1)) {
+        if (n == 16)
+          return launch_clusters(k_bwd_wide<16, XT, DT, DXT, true>, wide_smem_bytes(16, 2),
+                                 wide_cs, "mhc_bwd(wide)", C, eps, vec_dx);
+        return launch_clusters(k_bwd_wide<32, XT, DT, DXT, true>, wide_smem_bytes(32, 2),
+                               wide_cs, "mhc_bwd(wide)", C, eps, vec_dx);
+      }
+    }
     if (n == 16)
-      return launch_clusters(k_bwd_wide<16, XT, DT, DXT>, wide_smem_bytes(16), "mhc_bwd(wide)",
-                             C, eps, vec_dx);
-    return launch_clusters(k_bwd_wide<32, XT, DT, DXT>, wide_smem_bytes(32), "mhc_bwd(wide)", C,
-                           eps, vec_dx);
+      return launch_clusters(k_bwd_wide<16, XT, DT, DXT, false>, wide_smem_bytes(16, 1), wide_cs,
+                             "mhc_bwd(wide)", C, eps, vec_dx);
+    return launch_clusters(k_bwd_wide<32, XT, DT, DXT, false>, wide_smem_bytes(32, 1), wide_cs,
+                           "mhc_bwd(wide)", C, eps, vec_dx);
   }
   const size_t smem = ((size_t)n * n + 2 * n + 2 * (size_t)(n + 1) * kGenLD) * sizeof(float);
-  return launch_clusters(k_bwd_generic<XT, DT, DXT>, smem, "mhc_bwd(generic)", n, C, eps);
+  return launch_clusters(k_bwd_generic<XT, DT, DXT>, smem, 1, "mhc_bwd(generic)", n, C, eps);
 }
 
 int launch_bwd(const void* x, int xdt, const void* dout, int ddt, const float* M,
