@@ -1134,25 +1134,26 @@ k_bwd_wide(const XT* __restrict__ x, const DT* __restrict__ dout, const float* _
 }
 
 // ================================================================ finalize ==
-// Blocks [0, nbc) reduce d_rms_weight, 32 columns per block: thread
-// (slice r, column c) sums partial rows r, r + 8, r + 16, ... and the 8
-// slice sums are added in slice order -- a fixed order for a given row count,
-// with 8x fewer dependent loads per thread than a plain column walk.  The
-// last block reduces the n*n + 2n parameter partials the same way and
-// optionally runs the parameter chain (Sinkhorn backward from a staged tape
-// + sigmoid derivatives).
-constexpr int kFinBD = 256;
-constexpr int kFinSlices = kFinBD / 32;
-
+// Blocks of BD threads (256, or 1024 for n = 32 so that its Sinkhorn
+// backward runs one matrix entry per thread).  Blocks [0, nbc) reduce
+// d_rms_weight, 32 columns per block: thread (slice r, column c) sums partial
+// rows r, r + S, r + 2S, ... (S = BD / 32 slices) and the slice sums are
+// added in slice order -- a fixed order for a given row count, with S times
+// fewer dependent loads per thread than a plain column walk.  The last block
+// reduces the n*n + 2n parameter partials (sliced the same way when 2P <= BD,
+// else whole rows per entry) and optionally runs the parameter chain
+// (Sinkhorn backward from a staged tape + sigmoid derivatives).
+template <int BD>
 __device__ __forceinline__ float sliced_row_sum(const float* __restrict__ base, size_t stride,
                                                 int G, int r0) {
   float s = 0.f;
 #pragma unroll 4
-  for (int g = r0; g < G; g += kFinSlices) s += base[(size_t)g * stride];
+  for (int g = r0; g < G; g += BD / 32) s += base[(size_t)g * stride];
   return s;
 }
 
-__global__ void __launch_bounds__(kFinBD)
+template <int BD>
+__global__ void __launch_bounds__(BD)
 k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
            float* __restrict__ dhpre, float* __restrict__ dhpost, float* __restrict__ dw,
            const float* __restrict__ hpre_raw, const float* __restrict__ hpost_raw,
@@ -1165,15 +1166,15 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
   const float* wc = reinterpret_cast<const float*>(ws + WsLayout::cols_off(G, n));
   const int nbc = (C + 31) / 32;
   const int tid = threadIdx.x, lane = tid & 31, r0 = tid >> 5;
-  __shared__ float part[kFinSlices][32];
+  __shared__ float part[(BD / 32)][32];
   if ((int)blockIdx.x < nbc) {
     const int c = blockIdx.x * 32 + lane;
-    part[r0][lane] = (c < C) ? sliced_row_sum(wc + c, C, G, r0) : 0.f;
+    part[r0][lane] = (c < C) ? sliced_row_sum<BD>(wc + c, C, G, r0) : 0.f;
     __syncthreads();
     if (r0 == 0 && c < C && dw) {
       float s = 0.f;
 #pragma unroll
-      for (int q = 0; q < kFinSlices; ++q) s += part[q][lane];
+      for (int q = 0; q < (BD / 32); ++q) s += part[q][lane];
       dw[c] = s;
     }
     return;
@@ -1187,11 +1188,11 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
     else if (e < n * n + n) { if (dhpre) dhpre[e - n * n] = s; }
     else if (dhpost) dhpost[e - n * n - n] = s;
   };
-  if (2 * P <= kFinBD) {
-    // every thread of the block: S = kFinBD / P slices of the G rows per
+  if (2 * P <= BD) {
+    // every thread of the block: S = BD / P slices of the G rows per
     // entry, consecutive threads on consecutive entries of a row
     float* flat = &part[0][0];
-    const int S = kFinBD / P, e = tid % P, q = tid / P;
+    const int S = BD / P, e = tid % P, q = tid / P;
     if (q < S) {
       float s = 0.f;
 #pragma unroll 8
@@ -1206,16 +1207,16 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
     }
     __syncthreads();
   } else {
-    // Larger n: thread tid owns entries tid + k * kFinBD and adds their G
+    // Larger n: thread tid owns entries tid + k * BD and adds their G
     // partial rows in row order, KE entries at a time, so each row step
     // issues KE independent loads (and the unrolled steps several rows'
     // worth) instead of one dependent load per 32-entry group.
     constexpr int KE = 5;
-    for (int base = 0; base < P; base += KE * kFinBD) {
+    for (int base = 0; base < P; base += KE * BD) {
       float s[KE];
       int ee[KE];
 #pragma unroll
-      for (int k = 0; k < KE; ++k) { ee[k] = base + tid + k * kFinBD; s[k] = 0.f; }
+      for (int k = 0; k < KE; ++k) { ee[k] = base + tid + k * BD; s[k] = 0.f; }
 #pragma unroll 4
       for (int g = 0; g < G; ++g) {
         const float* row = wp + (size_t)g * P;
@@ -1268,8 +1269,8 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
       if (stage_sk) {  // dynamic shared memory holds [tape | logits]
         const size_t tf = (size_t)iters * sk_tape_stride(n);
 #pragma unroll 8
-        for (size_t e = tid; e < tf; e += kFinBD) s_fin[e] = tape[e];
-        for (int e = tid; e < n * n; e += kFinBD) s_fin[tf + e] = hres_raw[e];
+        for (size_t e = tid; e < tf; e += BD) s_fin[e] = tape[e];
+        for (int e = tid; e < n * n; e += BD) s_fin[tf + e] = hres_raw[e];
         __syncthreads();
         run(s_fin + tf, s_fin);
       } else {
@@ -1277,15 +1278,17 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
       }
       return;
     }
-    if (sk_elem_ok(n)) {  // kFinBD threads: n^2 / kFinBD entries per thread
+    if (sk_elem_ok(n)) {  // BD threads: n^2 / BD entries per thread
       MHC_SK_ELEM_SWITCH(n, ({
-        if (stage_sk) {
-          const SkTape tp = sk_stage_tape_fixed<SK_N>(tape, iters, s_fin);
-          __syncthreads();  // staged tape complete
-          sk_backward_elem<SK_N, kFinBD>(hres_raw, tp, iters, eps, sP, D, dhres_raw);
-        } else {
-          sk_backward_elem<SK_N, kFinBD>(hres_raw, SkTape{tape, SK_N, sk_tape_stride(SK_N)},
-                                         iters, eps, sP, D, dhres_raw);
+        if constexpr (SK_N * SK_N >= BD) {  // the launcher pairs BD = 1024 with n = 32 only
+          if (stage_sk) {
+            const SkTape tp = sk_stage_tape_fixed<SK_N>(tape, iters, s_fin);
+            __syncthreads();  // staged tape complete
+            sk_backward_elem<SK_N, BD>(hres_raw, tp, iters, eps, sP, D, dhres_raw);
+          } else {
+            sk_backward_elem<SK_N, BD>(hres_raw, SkTape{tape, SK_N, sk_tape_stride(SK_N)},
+                                       iters, eps, sP, D, dhres_raw);
+          }
         }
       }))
       return;
@@ -1293,7 +1296,7 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
     const SkTape tp = stage_sk ? sk_stage_tape(tape, n, iters, s_fin)
                                : SkTape{tape, n, sk_tape_stride(n)};
     const int ld = sk_ld(n);
-    for (int e = tid; e < n * n; e += kFinBD) D[(e / n) * ld + e % n] = sP[e];
+    for (int e = tid; e < n * n; e += BD) D[(e / n) * ld + e % n] = sP[e];
     __syncthreads();
     sk_backward_block(hres_raw, tp, n, iters, eps, D, dhres_raw);
   }
@@ -1758,11 +1761,15 @@ int launch_finalize(const void* ws, int n, int C, float* dM, float* dhpre, float
     const size_t b = sk_stage_floats(n, iters) * sizeof(float);
     if (b <= 160 * 1024) smem = b;
   }
-  if (allow_dyn_smem(k_finalize, smem) != cudaSuccess) smem = 0;
-  k_finalize<<<nbc + 1, kFinBD, smem, st>>>(static_cast<const char*>(ws), n, C, dM, dhpre, dhpost,
-                                            dw, hpre_raw, hpost_raw, hres_raw, tape, iters, eps,
-                                            dhpre_raw, dhpost_raw, dhres_raw, smem > 0);
-  return check_launch("mhc_bwd_finalize");
+  auto go = [&](auto kern, int bd) {
+    if (allow_dyn_smem(kern, smem) != cudaSuccess) smem = 0;
+    kern<<<nbc + 1, bd, smem, st>>>(static_cast<const char*>(ws), n, C, dM, dhpre, dhpost, dw,
+                                    hpre_raw, hpost_raw, hres_raw, tape, iters, eps, dhpre_raw,
+                                    dhpost_raw, dhres_raw, smem > 0);
+    return check_launch("mhc_bwd_finalize");
+  };
+  if (n == 32) return go(k_finalize<1024>, 1024);
+  return go(k_finalize<256>, 256);
 }
 
 }  // namespace mhc
