@@ -854,6 +854,7 @@ k_bwd_generic(const XT* __restrict__ x, const DT* __restrict__ dout, const float
 // next tile (of either pass, or of the next token) is copied with cp.async
 // while the current one is computed, so load latency overlaps the
 // contractions.  Otherwise each thread loads its column of the tile.
+// Both contractions issue packed two-lane FMAs (fma2: bit-identical to fmaf).
 // Staged row i starts at wide_row(i) = i * kWideLD + (i / 8) * 8 floats, so
 // the 8-row blocks read by one warp fall on distinct banks and every row
 // start is 16-byte aligned.  A slice holds at most kWideSlice columns (the
@@ -1015,7 +1016,8 @@ k_bwd_wide(const XT* __restrict__ x, const DT* __restrict__ dout, const float* _
 #pragma unroll
         for (int a = 0; a < 8; ++a)
 #pragma unroll
-          for (int b = 0; b < 8; ++b) acc[a][b] = fmaf(dv[a], xv[b], acc[a][b]);
+          for (int b = 0; b < 8; b += 2)
+            fma2(acc[a][b], acc[a][b + 1], dv[a], dv[a], xv[b], xv[b + 1]);
         const float yw = ex_yw[cc], dw = ex_dw[cc], yv = ex_y[cc];
 #pragma unroll
         for (int r = 0; r < HR; ++r) {
@@ -1082,11 +1084,12 @@ k_bwd_wide(const XT* __restrict__ x, const DT* __restrict__ dout, const float* _
           for (int i = 0; i < N; ++i) {
             const float4 m4 = *reinterpret_cast<const float4*>(sM + i * N + 4 * jg);
             const float4 d4 = *reinterpret_cast<const float4*>(bd + wide_row(i) + cb);
-            const float mv[4] = {m4.x, m4.y, m4.z, m4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+            const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
-#pragma unroll
-              for (int v = 0; v < 4; ++v) o[a][v] = fmaf(mv[a], dv[v], o[a][v]);
+            for (int a = 0; a < 4; ++a) {
+              fma2(o[a][0], o[a][1], mv[a], mv[a], d4.x, d4.y);
+              fma2(o[a][2], o[a][3], mv[a], mv[a], d4.z, d4.w);
+            }
           }
 #pragma unroll
           for (int a = 0; a < 4; ++a) {
@@ -1211,13 +1214,13 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
     // partial rows in row order, KE entries at a time, so each row step
     // issues KE independent loads (and the unrolled steps several rows'
     // worth) instead of one dependent load per 32-entry group.
-    constexpr int KE = 5;
+    constexpr int KE = BD >= 1024 ? 2 : 5;
     for (int base = 0; base < P; base += KE * BD) {
       float s[KE];
       int ee[KE];
 #pragma unroll
       for (int k = 0; k < KE; ++k) { ee[k] = base + tid + k * BD; s[k] = 0.f; }
-#pragma unroll 4
+#pragma unroll 8
       for (int g = 0; g < G; ++g) {
         const float* row = wp + (size_t)g * P;
 #pragma unroll
