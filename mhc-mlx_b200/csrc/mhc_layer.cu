@@ -207,11 +207,11 @@ k_fwd_split(const InT* __restrict__ x, const float* __restrict__ Mg,
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
   const int cs = (int)cl.num_blocks(), rank = (int)cl.block_rank();
-  __shared__ __align__(16) float sM[N * N];
+  __shared__ __align__(16) float sMT[N * N];  // sMT[j * N + i] = M[i][j]
   __shared__ float shpre[N], shpost[N];
   __shared__ float red[2][32];
   __shared__ float s_part;
-  for (int e = threadIdx.x; e < N * N; e += blockDim.x) sM[e] = Mg[e];
+  for (int e = threadIdx.x; e < N * N; e += blockDim.x) sMT[(e % N) * N + e / N] = Mg[e];
   for (int e = threadIdx.x; e < N; e += blockDim.x) { shpre[e] = hpre_g[e]; shpost[e] = hpost_g[e]; }
   __syncthreads();
   const int64_t t = blockIdx.x / cs;
@@ -231,7 +231,10 @@ k_fwd_split(const InT* __restrict__ x, const float* __restrict__ Mg,
   for (int r = 0; r < cs; ++r) tot += *cl.map_shared_rank(&s_part, r);
   const float inv = inv_rms(tot, C, eps);
   OutT* ot = out + t * (int64_t)N * C;
-  const float4* sM4 = reinterpret_cast<const float4*>(sM);
+  // M^T staged once more so that one float4 holds M[i..i+3][j]: four output
+  // streams advance with two packed FMAs per column j (same per-stream order
+  // over j as a scalar chain, bit-identical)
+  const float4* sMT4 = reinterpret_cast<const float4*>(sMT);
   for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
     float xc[N], a = 0.f;
 #pragma unroll
@@ -240,18 +243,19 @@ k_fwd_split(const InT* __restrict__ x, const float* __restrict__ Mg,
       a = fmaf(shpre[j], xc[j], a);
     }
     const float yn = (a * inv) * __ldg(w + c);
-#pragma unroll 4
-    for (int i = 0; i < N; ++i) {
-      float m = 0.f;
+#pragma unroll 2
+    for (int i = 0; i < N; i += 4) {
+      float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
 #pragma unroll
-      for (int j = 0; j < N; j += 4) {
-        const float4 r4 = sM4[(i * N + j) / 4];
-        m = fmaf(r4.x, xc[j], m);
-        m = fmaf(r4.y, xc[j + 1], m);
-        m = fmaf(r4.z, xc[j + 2], m);
-        m = fmaf(r4.w, xc[j + 3], m);
+      for (int j = 0; j < N; ++j) {
+        const float4 r4 = sMT4[(j * N + i) / 4];
+        fma2(m0, m1, r4.x, r4.y, xc[j], xc[j]);
+        fma2(m2, m3, r4.z, r4.w, xc[j], xc[j]);
       }
-      ot[(int64_t)i * C + c] = from_f<OutT>(m + shpost[i] * yn);
+      ot[(int64_t)i * C + c] = from_f<OutT>(m0 + shpost[i] * yn);
+      ot[(int64_t)(i + 1) * C + c] = from_f<OutT>(m1 + shpost[i + 1] * yn);
+      ot[(int64_t)(i + 2) * C + c] = from_f<OutT>(m2 + shpost[i + 2] * yn);
+      ot[(int64_t)(i + 3) * C + c] = from_f<OutT>(m3 + shpost[i + 3] * yn);
     }
   }
   cl.sync();  // no CTA leaves while another may still read its partial
