@@ -1378,12 +1378,16 @@ static int try_fwd_vec(const InT* x, const float* M, const float* hpre, const fl
                        const float* w, OutT* out, int64_t T, int C, float eps, cudaStream_t st) {
   const int forced = env_int("MHC_B200_FWD_ITEMS", 0);
   const int groups = (C + VEC - 1) / VEC;
-  // Default: the fewest ITEMS whose block is at most 512 threads.
+  // Default: the fewest ITEMS whose block is at most 512 threads (256 for
+  // 16-bit inputs: measured on B200, n=4, C=4096, 64K tokens, bf16 in/out,
+  // 687 us with 512 threads x 1 group, 660 us with 256 threads x 2 groups;
+  // fp32 is flat between 2 and 4 groups, 1393 / 1389 us).
+  const int cap = sizeof(InT) == 2 ? 256 : 512;
   const int order[4] = {1, 2, 4, 8};
   for (int k = 0; k < 4; ++k) {
     const int items = order[k];
     if (forced && items != forced) continue;
-    if (!forced && round32((groups + items - 1) / items) > 512 && items != 8) continue;
+    if (!forced && round32((groups + items - 1) / items) > cap && items != 8) continue;
     int r = -1;
     switch (items) {
       case 1: r = try_fwd_items<N, InT, OutT, VEC, 1>(x, M, hpre, hpost, w, out, T, C, eps, st); break;
