@@ -275,7 +275,9 @@ __device__ __forceinline__ float inv_rms(float sumsq, int C, float eps) {
 __device__ __forceinline__ float sigmoidf_(float v) { return 1.0f / (1.0f + expf(-v)); }
 
 // Layout of the workspace written by the backward kernels:
-//   [0, 256)            header: int32 number of partial rows G
+//   [0, 256)            header: int32 number of partial rows G, then the row
+//                       step of the parameter partials (1, or the cluster size
+//                       when a cluster's CTAs combined theirs into its first row)
 //   params partials     G x P floats (P = n*n + 2n: dM row-major, dH_pre, dH_post)
 //   column partials     G x C floats (d_rms_weight)
 struct WsLayout {

@@ -457,7 +457,7 @@ k_bwd_fast(const XT* __restrict__ x, const DT* __restrict__ dout, const float* _
 #pragma unroll
   for (int it = 0; it < ITEMS; ++it)
     if (ok[it]) store_vec<float, VEC, false>(ws_c + (size_t)blockIdx.x * C + col[it], aW[it]);
-  if (blockIdx.x == 0 && threadIdx.x == 0) ws_hdr[0] = gridDim.x;
+  if (blockIdx.x == 0 && threadIdx.x == 0) { ws_hdr[0] = gridDim.x; ws_hdr[1] = 1; }
 }
 
 // Full-row backward for 16-bit rows: x, d_out and dx share one 16-bit type T
@@ -678,7 +678,7 @@ k_bwd_rows(const T* __restrict__ x, const T* __restrict__ dout, const float* __r
     ws_p[(size_t)blockIdx.x * P + e] = s;
   }
   store_vec<float, 8, false>(ws_c + (size_t)blockIdx.x * C + col, aW);
-  if (blockIdx.x == 0 && tid == 0) ws_hdr[0] = gridDim.x;
+  if (blockIdx.x == 0 && tid == 0) { ws_hdr[0] = gridDim.x; ws_hdr[1] = 1; }
 }
 
 // Generic backward: any n <= 64, any C.  Pass 1 reduces ss and pd for the
@@ -834,7 +834,7 @@ k_bwd_generic(const XT* __restrict__ x, const DT* __restrict__ dout, const float
         else if (i < n && j == n) pr[n * n + n + i] = acc[q][a][b];  // dHpost_i
       }
   }
-  if (blockIdx.x == 0 && tid == 0) ws_hdr[0] = gridDim.x;
+  if (blockIdx.x == 0 && tid == 0) { ws_hdr[0] = gridDim.x; ws_hdr[1] = 1; }
   cl.sync();  // the last token's partial pairs stay readable until every CTA has them
 }
 
@@ -1134,10 +1134,21 @@ k_bwd_wide(const XT* __restrict__ x, const DT* __restrict__ dout, const float* _
     }
     __syncthreads();
   }
-  float* pr = ws_p + (size_t)blockIdx.x * P;
-  for (int e = tid; e < P; e += kWideBD) pr[e] = sbuf[e];
-  if (blockIdx.x == 0 && tid == 0) ws_hdr[0] = gridDim.x;
-  cl.sync();  // the last token's partial pairs stay readable until every CTA has them
+  // The cluster's CTAs add their parameter partials through distributed
+  // shared memory in rank order; rank 0 writes the sum, so the finalize reads
+  // one parameter row per cluster (header word 1 = cs: rows 0, cs, 2cs, ...).
+  // The d_rms_weight rows stay per CTA (each CTA owns its columns).
+  cl.sync();  // every CTA's sums are complete; the last token's partial pairs are read
+  if (rank == 0) {
+    float* pr = ws_p + (size_t)blockIdx.x * P;
+    for (int e = tid; e < P; e += kWideBD) {
+      float v = 0.f;
+      for (int r = 0; r < cs; ++r) v += cl.map_shared_rank(sbuf, r)[e];
+      pr[e] = v;
+    }
+  }
+  if (blockIdx.x == 0 && tid == 0) { ws_hdr[0] = gridDim.x; ws_hdr[1] = cs; }
+  cl.sync();  // every CTA's shared memory stays alive until rank 0 has read it
 }
 
 // ================================================================ finalize ==
@@ -1167,7 +1178,12 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
            const float* __restrict__ hres_raw, const float* __restrict__ tape, int iters,
            float eps, float* __restrict__ dhpre_raw, float* __restrict__ dhpost_raw,
            float* __restrict__ dhres_raw, int stage_sk) {
-  const int G = *reinterpret_cast<const int*>(ws);
+  const int G = reinterpret_cast<const int*>(ws)[0];
+  // parameter partials sit in rows 0, step, 2 step, ... (step > 1 when the
+  // CTAs of a cluster combined theirs); d_rms_weight partials in all G rows
+  const int step = max(1, reinterpret_cast<const int*>(ws)[1]);
+  const int Gp = (G + step - 1) / step;
+  const size_t pstride = (size_t)step * (size_t)(n * n + 2 * n);
   const int P = n * n + 2 * n;
   const float* wp = reinterpret_cast<const float*>(ws + WsLayout::params_off());
   const float* wc = reinterpret_cast<const float*>(ws + WsLayout::cols_off(G, n));
@@ -1203,7 +1219,7 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
     if (q < S) {
       float s = 0.f;
 #pragma unroll 8
-      for (int g = q; g < G; g += S) s += wp[(size_t)g * P + e];
+      for (int g = q; g < Gp; g += S) s += wp[(size_t)g * pstride + e];
       flat[q * P + e] = s;
     }
     __syncthreads();
@@ -1225,8 +1241,8 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
 #pragma unroll
       for (int k = 0; k < KE; ++k) { ee[k] = base + tid + k * BD; s[k] = 0.f; }
 #pragma unroll 8
-      for (int g = 0; g < G; ++g) {
-        const float* row = wp + (size_t)g * P;
+      for (int g = 0; g < Gp; ++g) {
+        const float* row = wp + (size_t)g * pstride;
 #pragma unroll
         for (int k = 0; k < KE; ++k)
           if (ee[k] < P) s[k] += row[ee[k]];
