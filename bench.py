@@ -26,6 +26,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -85,11 +86,12 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_bench_{os.getpid()}.csv"
+        fd, name = tempfile.mkstemp(prefix="mhc_clocks_", suffix=".csv")
+        os.close(fd)
+        self.path = Path(name)
 
     def start(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",

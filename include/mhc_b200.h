@@ -53,6 +53,10 @@ enum mhc_status {
 /* ---- library info ------------------------------------------------------ */
 MHC_API const char* mhc_last_error(void);
 MHC_API int mhc_version(void);
+/* Hash of the sources and compiler flags this library was built from (no
+ * counterpart in the reference): lets a loader check that the binary it
+ * maps matches the source tree next to it. */
+MHC_API const char* mhc_build_id(void);
 /* Number of SMs of the current device (used to size workspaces). */
 MHC_API int mhc_device_sm_count(int* sm_count);
 /* Self-test of the reciprocal the Sinkhorn kernels use for their row and
@@ -150,11 +154,14 @@ MHC_API int mhc_bwd_finalize(const void* workspace, int n, int C, float* dM,
  * The per-block partial sums live in one file-scope device array of
  * MHC_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps until
  * process exit; the call allocates nothing.  It fails with MHC_ERR_WORKSPACE
- * when mhc_bwd_workspace_bytes(T, n, C) exceeds that size (on a 148-SM B200:
- * n = 4 fits any T up to C = 7,060).  The first call on a device looks up
- * the array's device address (once per device): make it before any stream
- * capture.  All calls share the array, so calls that overlap on the GPU
- * (different streams, or several host threads) race: serialise them. */
+ * when mhc_bwd_workspace_bytes(T, n, C) exceeds that size.  That size is a
+ * 256-byte header, then G * (n*n + 2n) * 4 bytes rounded up to a multiple of
+ * 256, then G * C * 4 bytes, with G = min(4 * SMs, 8 * T) partial rows: on a
+ * 148-SM B200, n = 4 fits any T up to C = 7,060.  The first call on a device
+ * looks up the array's device address (once per device): make it before any
+ * stream capture.  A first call whose lookup failed returns MHC_ERR_CUDA and
+ * may be retried.  All calls share the array, so calls that overlap on the
+ * GPU (different streams, or several host threads) race: serialise them. */
 #define MHC_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
 MHC_API int mhc_bwd_noalloc(const void* x, int x_dtype, const void* d_out, int dout_dtype,
                             const float* M, const float* H_pre_act, const float* H_post_act,

@@ -124,6 +124,11 @@ const char* mhc_last_error(void) { return g_err; }
 
 int mhc_version(void) { return 10000; }  // 1.0.0
 
+#ifndef MHC_BUILD_ID
+#define MHC_BUILD_ID "unknown"
+#endif
+const char* mhc_build_id(void) { return MHC_BUILD_ID; }
+
 int mhc_device_sm_count(int* out) {
   MHC_REQ(out, "mhc_device_sm_count: NULL output");
   *out = sm_count();

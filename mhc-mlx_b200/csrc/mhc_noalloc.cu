@@ -13,7 +13,8 @@
 //  - All calls share the array: calls that overlap on the GPU race.
 //  - The first call on a device resolves the array's device address with
 //    cudaGetSymbolAddress (once per device, with that device current); make
-//    that first call before any stream capture.
+//    that first call before any stream capture.  A first call whose lookup
+//    failed returns MHC_ERR_CUDA and can be retried.
 //  - No cudaMalloc / cudaFree or allocating library routine is called.
 #include <mutex>
 
@@ -25,26 +26,31 @@ namespace mhc {
 static __device__ __align__(256) unsigned char g_noalloc_scratch[MHC_NOALLOC_SCRATCH_BYTES];
 
 static constexpr int kMaxDev = 64;
-static void* g_scratch_addr[kMaxDev];
-static int g_scratch_status[kMaxDev];
-static std::once_flag g_scratch_once[kMaxDev];
+static void* g_scratch_addr[kMaxDev];  // non-null once resolved on that device
+static std::mutex g_scratch_mu[kMaxDev];
 
 // Device address of the array on the current device.  In host code
 // g_noalloc_scratch names a host-side stand-in, never a device address.
+// Only a successful lookup is remembered: a lookup that fails (for example
+// one attempted during stream capture) is retried by the next call, and its
+// error is cleared from the runtime's last-error slot so that it is not
+// reported again by a later, unrelated launch check.
 static int scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_bwd_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDev) return set_error(MHC_ERR_UNSUPPORTED, "mhc_bwd_noalloc: device %d", dev);
-  std::call_once(g_scratch_once[dev], [dev]() {
+  std::lock_guard<std::mutex> lock(g_scratch_mu[dev]);
+  if (!g_scratch_addr[dev]) {
     void* p = nullptr;
     const cudaError_t r = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    g_scratch_status[dev] = (int)r;
-    g_scratch_addr[dev] = (r == cudaSuccess) ? p : nullptr;
-  });
-  if (g_scratch_status[dev] != cudaSuccess || !g_scratch_addr[dev])
-    return set_error(MHC_ERR_CUDA, "mhc_bwd_noalloc: cudaGetSymbolAddress failed: %s",
-                     cudaGetErrorString((cudaError_t)g_scratch_status[dev]));
+    if (r != cudaSuccess || !p) {
+      (void)cudaGetLastError();
+      return set_error(MHC_ERR_CUDA, "mhc_bwd_noalloc: cudaGetSymbolAddress failed: %s "
+                       "(the call can be retried)", cudaGetErrorString(r));
+    }
+    g_scratch_addr[dev] = p;
+  }
   *out = g_scratch_addr[dev];
   return MHC_OK;
 }

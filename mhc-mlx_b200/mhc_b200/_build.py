@@ -6,11 +6,18 @@ The library is written next to this file (``_lib/libmhc_b200.so``) so that it
 travels with the source tree; nothing is installed into site-packages.  The
 CUDA runtime is linked statically, so loading the library needs no GPU and
 no driver (symbols can be inspected on a CPU-only machine).
+
+Staleness is decided by content, not by file times: the build hashes every
+source and header together with the compiler flags, compiles that hash into
+the library (``mhc_build_id()``) and writes it beside the library
+(``libmhc_b200.so.id``).  A library whose id differs from the hash of the
+sources next to it is rebuilt, and the ctypes loader refuses to load one.
 """
 
 from __future__ import annotations
 
 import argparse
+import hashlib
 import os
 import shutil
 import subprocess
@@ -24,6 +31,7 @@ REPO_DIR = PKG_DIR.parent.parent
 INCLUDE_DIR = REPO_DIR / "include"
 LIB_DIR = PKG_DIR / "_lib"
 LIB_PATH = LIB_DIR / "libmhc_b200.so"
+ID_PATH = LIB_DIR / "libmhc_b200.so.id"
 OBJ_DIR = LIB_DIR / "obj"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -56,11 +64,25 @@ def _deps() -> list[Path]:
     ]
 
 
+def source_hash() -> str:
+    """sha256 (first 16 hex digits) of every source and header, by name and
+    content, and of the compiler flags."""
+    h = hashlib.sha256()
+    for p in _deps():
+        h.update(p.name.encode() + b"\0" + p.read_bytes() + b"\0")
+    h.update(" ".join(NVCC_FLAGS).encode())
+    return h.hexdigest()[:16]
+
+
+def built_id() -> str | None:
+    try:
+        return ID_PATH.read_text().strip()
+    except OSError:
+        return None
+
+
 def is_stale() -> bool:
-    if not LIB_PATH.exists():
-        return True
-    t = LIB_PATH.stat().st_mtime
-    return any(p.stat().st_mtime > t for p in _deps())
+    return not LIB_PATH.exists() or built_id() != source_hash()
 
 
 def build(force: bool = False, jobs: int | None = None, verbose: bool = True) -> Path:
@@ -70,10 +92,11 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = True) ->
     nvcc = _nvcc()
     OBJ_DIR.mkdir(parents=True, exist_ok=True)
     inc = [f"-I{INCLUDE_DIR}", f"-I{SRC_DIR}"]
+    bid = source_hash()
 
     def compile_one(src: Path) -> Path:
         obj = OBJ_DIR / (src.stem + ".o")
-        cmd = [nvcc, *NVCC_FLAGS, *inc, "-c", str(src), "-o", str(obj)]
+        cmd = [nvcc, *NVCC_FLAGS, f"-DMHC_BUILD_ID=\"{bid}\"", *inc, "-c", str(src), "-o", str(obj)]
         if verbose:
             print("[mhc_b200 build]", " ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)
@@ -92,6 +115,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = True) ->
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
     os.replace(tmp, LIB_PATH)
+    ID_PATH.write_text(bid + "\n")
     return LIB_PATH
 
 

@@ -26,6 +26,7 @@ _P = c_void_p
 SIGNATURES: dict[str, tuple] = {
     "mhc_last_error": (ctypes.c_char_p, []),
     "mhc_version": (c_int, []),
+    "mhc_build_id": (ctypes.c_char_p, []),
     "mhc_selftest_reciprocal": (c_int, [_P, _P, c_int64, _P]),
     "mhc_device_sm_count": (c_int, [ctypes.POINTER(c_int)]),
     "mhc_sinkhorn_tape_floats": (c_size_t, [c_int, c_int]),
@@ -100,8 +101,28 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
+        _check_build_id(lib, path)
         _lib = lib
     return _lib
+
+
+def _check_build_id(lib: ctypes.CDLL, path: Path) -> None:
+    """Refuse a library built from other sources than the ones beside it
+    (the id compiled into the library is the hash of csrc/ and include/ at
+    build time).  Skipped for an explicit MHC_B200_LIB override and when the
+    sources are not present."""
+    if os.environ.get("MHC_B200_LIB"):
+        return
+    from . import _build
+
+    if not _build.SRC_DIR.is_dir():
+        return
+    have = (lib.mhc_build_id() or b"").decode()
+    want = _build.source_hash()
+    if have != want:
+        raise RuntimeError(
+            f"{path} was built from different sources (build id {have or 'none'}, sources "
+            f"{want}); rebuild it with `python -m mhc_b200._build`.")
 
 
 def exported_symbols() -> list[str]:

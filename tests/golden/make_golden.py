@@ -12,7 +12,9 @@ outputs to ``reference_golden.npz`` next to this file.
 
 Run in a container that has the reference checkout (read-only is fine):
 
-    python tests/golden/make_golden.py [--reference /path/to/mhc-mlx]
+    python tests/golden/make_golden.py --reference /path/to/mhc-mlx
+
+(or set MHC_REFERENCE_DIR instead of passing --reference).
 
 Inputs mirror the reference tests' shapes (tests/test_correctness.py,
 test_stability.py, test_stress.py); MLX's RNG cannot be reproduced, so the
@@ -24,6 +26,7 @@ MLX's ``astype(float32)`` of a half array would see them.
 from __future__ import annotations
 
 import argparse
+import os
 import importlib
 import json
 import sys
@@ -101,7 +104,9 @@ def as_dtype(a: np.ndarray, dtype: str) -> np.ndarray:
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("MHC_REFERENCE_DIR"),
+                    required="MHC_REFERENCE_DIR" not in os.environ,
+                    help="checkout of svdrecbd/mhc-mlx (default: $MHC_REFERENCE_DIR)")
     args = ap.parse_args(argv)
     root = Path(args.reference)
     install_mlx_standin()

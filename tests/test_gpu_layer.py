@@ -200,6 +200,35 @@ def test_layer_gradients_match_oracle_fp32(B, n, C, iters):
         assert_close_to_reference(name, a, b, b32)
 
 
+# the isolated op sweep's exact cells.  x ~ N(0, 1),
+# H_res / H_pre / H_post logits ~ N(0, 0.1), rms_weight = 1, d_out ~ N(0, 1);
+# bf16 runs bf16 in -> bf16 out (return_dtype), fp32 runs fp32 end to end.
+@pytest.mark.parametrize("io", ["f32", "bf16"])
+@pytest.mark.parametrize("C", [512, 2048, 4096])
+@pytest.mark.parametrize("B", [1, 32])
+def test_config2_sweep_cells_match_oracle(io, C, B):
+    n = 4
+    g = torch.Generator().manual_seed(20_000 + 7 * C + B + (1 if io == "bf16" else 0))
+    dt = torch.float32 if io == "f32" else torch.bfloat16
+    x = torch.randn(B, n, C, generator=g).to(dt)
+    params = [0.1 * torch.randn(n, generator=g), 0.1 * torch.randn(n, generator=g),
+              0.1 * torch.randn(n, n, generator=g), torch.ones(C)]
+    d_out = torch.randn(B, n, C, generator=g).to(dt)
+    ref = O.layer_grads(x, *params, d_out, 20, 1e-5, dtype=F64)
+    got = _layer_grads(cu(x, dt), [cu(p) for p in params], cu(d_out, dt), 20, 1e-5,
+                       return_dtype=None if io == "f32" else dt)
+    names = ("out", "dx", "dH_pre", "dH_post", "dH_res", "d_w")
+    if io == "f32":
+        ref32 = O.layer_grads(x, *params, d_out, 20, 1e-5, dtype=torch.float32)
+        for name, a, b, b32 in zip(names, got, ref, ref32):
+            assert_close_to_reference(name, a, b, b32)
+    else:
+        assert got[0].dtype == dt and got[1].dtype == dt
+        for name, a, b in zip(names, got, ref):
+            tol = 2e-2 if name in ("out", "dx") else 1e-5
+            assert rel_err(a, b) < tol, (name, rel_err(a, b))
+
+
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("B,n,C", [(2, 4, 128), (3, 4, 4096), (2, 16, 64), (2, 4, 129)])
 def test_layer_gradients_half_inputs(dt, B, n, C):
