@@ -701,11 +701,12 @@ def run_configs(args):
 
         mk4, per4 = _kernel_us_per_step(fb4, dev)
         step_us = _median_us(fb4, dev, iters=30, warm=3)
-        # algorithmic bytes of the mHC kernels per step (bf16 x / y_inner, fp32 out / d_out):
-        #   prescale fwd x->x_pre 2+2; combine fwd x,y->out 2+2+4; combine bwd x,y,d->dx,dy
-        #   2+2+4+2+2; prescale bwd x,d_xpre->dx 2+2+2  (bytes per element)
+        # algorithmic bytes of the mHC kernels per step (bf16 x / y_inner / dy / d_xpre /
+        # dx, fp32 out / d_out), bytes per element:
+        #   prescale fwd x -> x_pre 2+2; combine fwd x, y -> out 2+2+4;
+        #   backward dy side y, d -> dy 2+4+2; x side x, d, d_xpre -> dx 2+4+2+2
         elems = 8192 * 4096
-        mbytes = elems * ((2 + 2) + (2 + 2 + 4) + (2 + 2 + 4 + 2 + 2) + (2 + 2 + 2))
+        mbytes = elems * ((2 + 2) + (2 + 2 + 4) + (2 + 4 + 2) + (2 + 4 + 2 + 2))
         out.append({"metric": "MHCRewire(QuantizedLinear 4096, n=4) mHC fwd+bwd tokens/s, GEMM "
                               "excluded (BASELINE config 4)",
                     "value": 8192 / (mk4 * 1e-6), "unit": "tokens/s", "higher_is_better": True,

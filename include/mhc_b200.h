@@ -202,6 +202,38 @@ MHC_API int mhc_rewire_combine_bwd(const void* x, int x_dtype, const void* y_inn
                            int n, int C, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* ---- MHCRewire backward end to end -----------------------------------------
+ * The reference differentiates MHCRewire.__call__ (layer.py:469-492) as two
+ * separate pieces: the pre-scale x * H_pre (layer.py:478-480) and the
+ * post-combine (layer.py:312-337, VJP metal.py:2661-2709), each producing a
+ * dx and a dH_pre contribution that MLX then adds.  These two calls bracket
+ * the inner module's backward instead, so dx is written once and dH_pre is
+ * one reduction:
+ *   mhc_rewire_bwd_dy (before the inner backward):
+ *     dy_inner[t,i,c] = H_post_act[i] * d_out[t,i,c], and partial sums of
+ *     R_i = sum d_out_i * y_inner_i into `workspace`;
+ *   mhc_rewire_bwd_dx (after it, with d_xpre = the inner module's input
+ *   gradient, NULL for zero):
+ *     dx[t,j,c] = H_pre_act[j] * (sum_i M[i,j] H_post_act[i] d_out[t,i,c] + d_xpre[t,j,c])
+ *     dM[i,j]   = H_post_act[i] H_pre_act[j] Q[i,j],   Q = sum d_out x^T
+ *     dH_pre_act[j]  = sum_i H_post_act[i] M[i,j] Q[i,j] + sum d_xpre_j x_j
+ *     dH_post_act[i] = R_i + sum_j M[i,j] H_pre_act[j] Q[i,j]
+ *   (fixed summation order; dx may be NULL when only the parameter gradients
+ *   are wanted).  Both calls take the same workspace of
+ *   mhc_rewire_fused_bwd_workspace_bytes(), untouched in between.  d_out and
+ *   d_xpre are fp32 or x's dtype; dy_inner has y_inner's dtype. */
+MHC_API size_t mhc_rewire_fused_bwd_workspace_bytes(int64_t T, int n, int C);
+MHC_API int mhc_rewire_bwd_dy(const void* y_inner, int y_dtype, const void* d_out,
+                              int dout_dtype, const float* H_post_act, void* dy_inner,
+                              int dy_dtype, int64_t T, int n, int C, void* workspace,
+                              size_t workspace_bytes, void* stream);
+MHC_API int mhc_rewire_bwd_dx(const void* x, int x_dtype, const void* d_out, int dout_dtype,
+                              const void* d_xpre, int dxpre_dtype, const float* M,
+                              const float* H_pre_act, const float* H_post_act, void* dx,
+                              int dx_dtype, float* dM, float* dH_pre_act, float* dH_post_act,
+                              int64_t T, int n, int C, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
 /* ---- stream pre-scale (MHCRewire input side) ------------------------------
  * layer.py:478-480: x_pre[t,i,c] = x[t,i,c] * H_pre_act[i].  Backward:
  * dx = H_pre_act[i] * d_xpre, dH_pre_act[i] = sum d_xpre * x (fixed order). */

@@ -339,6 +339,46 @@ int mhc_rewire_combine_bwd(const void* x, int x_dtype, const void* y_inner, int 
   MHC_TRY_END
 }
 
+size_t mhc_rewire_fused_bwd_workspace_bytes(int64_t T, int n, int C) {
+  if (n < 1 || n > 64 || C < 1 || T < 0) return 0;
+  return rewire_fused_ws_bytes(T, n, C);
+}
+
+int mhc_rewire_bwd_dy(const void* y_inner, int y_dtype, const void* d_out, int dout_dtype,
+                      const float* H_post_act, void* dy_inner, int dy_dtype, int64_t T, int n,
+                      int C, void* workspace, size_t workspace_bytes, void* stream) {
+  MHC_TRY_BEGIN
+  MHC_CHK(check_common(__func__, T, n, C));
+  MHC_CHK(check_dtype(__func__, "y_inner", y_dtype));
+  MHC_CHK(check_dtype(__func__, "d_out", dout_dtype));
+  MHC_CHK(check_dtype(__func__, "dy_inner", dy_dtype));
+  MHC_REQ(H_post_act, "%s: NULL parameter pointer", __func__);
+  MHC_REQ(T == 0 || (y_inner && d_out && dy_inner), "%s: NULL tensor pointer", __func__);
+  return launch_rewire_bwd_dy(y_inner, y_dtype, d_out, dout_dtype, H_post_act, dy_inner, dy_dtype,
+                              T, n, C, workspace, workspace_bytes, as_stream(stream));
+  MHC_TRY_END
+}
+
+int mhc_rewire_bwd_dx(const void* x, int x_dtype, const void* d_out, int dout_dtype,
+                      const void* d_xpre, int dxpre_dtype, const float* M, const float* H_pre_act,
+                      const float* H_post_act, void* dx, int dx_dtype, float* dM,
+                      float* dH_pre_act, float* dH_post_act, int64_t T, int n, int C,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  MHC_TRY_BEGIN
+  MHC_CHK(check_common(__func__, T, n, C));
+  MHC_CHK(check_dtype(__func__, "x", x_dtype));
+  MHC_CHK(check_dtype(__func__, "d_out", dout_dtype));
+  MHC_CHK(check_dtype(__func__, "d_xpre", dxpre_dtype));
+  MHC_CHK(check_dtype(__func__, "dx", dx_dtype));
+  MHC_REQ(M && H_pre_act && H_post_act, "%s: NULL parameter pointer", __func__);
+  MHC_REQ(dM && dH_pre_act && dH_post_act, "%s: NULL gradient pointer", __func__);
+  MHC_REQ(T == 0 || (x && d_out), "%s: NULL tensor pointer", __func__);
+  return launch_rewire_bwd_dx(x, x_dtype, d_out, dout_dtype, d_xpre, dxpre_dtype, M, H_pre_act,
+                              H_post_act, dx, dx_dtype, dM, dH_pre_act, dH_post_act, T, n, C,
+                              workspace, workspace_bytes, as_stream(stream));
+  MHC_TRY_END
+}
+
 int mhc_prescale_fwd(const void* x, int x_dtype, const float* H_pre_act, void* x_pre,
                      int out_dtype, int64_t T, int n, int C, void* stream) {
   MHC_TRY_BEGIN

@@ -106,6 +106,14 @@ int launch_rewire_bwd(const void* x, int xdt, const void* y, int ydt, const void
                       const float* M, const float* hpre, const float* hpost, void* dx, int dxdt,
                       void* dy, int dydt, float* dM, float* dhpre, float* dhpost, int64_t T,
                       int n, int C, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t rewire_fused_ws_bytes(int64_t T, int n, int C);
+int launch_rewire_bwd_dy(const void* y, int ydt, const void* d, int ddt, const float* hpost,
+                         void* dy, int dydt, int64_t T, int n, int C, void* ws, size_t ws_bytes,
+                         cudaStream_t st);
+int launch_rewire_bwd_dx(const void* x, int xdt, const void* d, int ddt, const void* p, int pdt,
+                         const float* M, const float* hpre, const float* hpost, void* dx, int dxdt,
+                         float* dM, float* dhpre, float* dhpost, int64_t T, int n, int C, void* ws,
+                         size_t ws_bytes, cudaStream_t st);
 int launch_prescale_fwd(const void* x, int xdt, const float* hpre, void* xo, int odt, int64_t T,
                         int n, int C, cudaStream_t st);
 int launch_prescale_bwd(const void* x, int xdt, const void* d, int ddt, const float* hpre,

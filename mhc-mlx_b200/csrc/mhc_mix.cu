@@ -19,6 +19,17 @@
 //   dM_ij = hpost_i hpre_j Q_ij
 //   dhpre_j = sum_i hpost_i M_ij Q_ij
 //   dhpost_i = R_i + sum_j M_ij hpre_j Q_ij
+//
+// MHCRewire end to end (pre-scale, inner module, post-combine) runs its
+// backward as two passes around the inner module's backward, so that dx is
+// written once and dH_pre comes out of one reduction:
+//   dy side (before the inner backward): dy_i = hpost_i d_i, R_i = sum d_i y_i
+//   x side  (after it, p = d_xpre):      dx_j = hpre_j (sum_i M_ij hpost_i d_i + p_j)
+//                                        Q_ij = sum d_i x_j, S_j = sum p_j x_j
+//   finalize: dM, dhpost as above; dhpre_j = sum_i hpost_i M_ij Q_ij + S_j
+// The two passes write their partial rows into one workspace: the dy side
+// rows [0, G1) (header word 0 = G1), the x side rows [G1, G1 + G2) (word 2 =
+// G2); a row is [Q (n*n) | R (n) | S (n)] with the other side's slots zero.
 #include <cstdlib>
 
 #include "mhc_common.cuh"
@@ -262,7 +273,11 @@ __host__ __device__ inline size_t mix_gen_smem(int n) {
   return ((size_t)n * n + 2 * (size_t)n + 3 * (size_t)n * kMixGenLD) * sizeof(float);
 }
 
-template <typename XT, typename YT, typename DT, typename DXT, typename DYT>
+// TAIL = the x side of the end-to-end MHCRewire backward: `y` is then d_xpre
+// (p, may be NULL), sp holds p_j (not a product), dx_j gains hpre_j p_j, no dy
+// is written, the per-stream sums are S_j = sum p_j x_j (slot n*n + n), and
+// the rows start after the dy side's (header word 0).
+template <typename XT, typename YT, typename DT, typename DXT, typename DYT, bool TAIL = false>
 __global__ void __launch_bounds__(kMixGenBD)
 k_combine_bwd_generic(const XT* __restrict__ x, const YT* __restrict__ y,
                       const DT* __restrict__ dout, const float* __restrict__ Mg,
@@ -275,8 +290,9 @@ k_combine_bwd_generic(const XT* __restrict__ x, const YT* __restrict__ y,
   float* shpost = shpre + n;
   float* sx = shpost + n;            // n x LD
   float* sd = sx + n * kMixGenLD;    // n x LD
-  float* sp = sd + n * kMixGenLD;    // n x LD  (d_i * y_i)
+  float* sp = sd + n * kMixGenLD;    // n x LD  (d_i * y_i, or p_j with TAIL)
   const int tid = threadIdx.x;
+  const int row0 = TAIL ? ws_hdr[0] : 0;
   for (int e = tid; e < n * n; e += kMixGenBD) sM[e] = Mg[e];
   for (int e = tid; e < n; e += kMixGenBD) {
     shpre[e] = hpre_g ? hpre_g[e] : 1.0f;
@@ -305,16 +321,19 @@ k_combine_bwd_generic(const XT* __restrict__ x, const YT* __restrict__ y,
       const float dv = ok ? to_f(dout[base + (int64_t)i * C]) : 0.f;
       sx[i * kMixGenLD + tid] = ok ? to_f(x[base + (int64_t)i * C]) : 0.f;
       sd[i * kMixGenLD + tid] = dv;
-      if (y) sp[i * kMixGenLD + tid] = ok ? dv * to_f(y[base + (int64_t)i * C]) : 0.f;
+      if (TAIL) sp[i * kMixGenLD + tid] = (ok && y) ? to_f(y[base + (int64_t)i * C]) : 0.f;
+      else if (y) sp[i * kMixGenLD + tid] = ok ? dv * to_f(y[base + (int64_t)i * C]) : 0.f;
     }
     if (ok) {
-      for (int j = 0; j < n; ++j) {
-        float o = 0.f;
-        for (int i = 0; i < n; ++i)
-          o = fmaf(sM[i * n + j], shpost[i] * sd[i * kMixGenLD + tid], o);
-        dx[base + (int64_t)j * C] = from_f<DXT>(o * shpre[j]);
-      }
-      if (dy)
+      if (dx)
+        for (int j = 0; j < n; ++j) {
+          float o = 0.f;
+          for (int i = 0; i < n; ++i)
+            o = fmaf(sM[i * n + j], shpost[i] * sd[i * kMixGenLD + tid], o);
+          if (TAIL) o += sp[j * kMixGenLD + tid];
+          dx[base + (int64_t)j * C] = from_f<DXT>(o * shpre[j]);
+        }
+      if (!TAIL && dy)
         for (int i = 0; i < n; ++i)
           dy[base + (int64_t)i * C] = from_f<DYT>(shpost[i] * sd[i * kMixGenLD + tid]);
     }
@@ -338,13 +357,19 @@ k_combine_bwd_generic(const XT* __restrict__ x, const YT* __restrict__ y,
           for (int b = 0; b < kMixRB; ++b) acc[q][a][b] = fmaf(dv[a], xv[b], acc[q][a][b]);
       }
     }
-    if (y && tid < n)
+    if (TAIL && y && tid < n)
+      for (int cc = 0; cc < width; ++cc)
+        accR = fmaf(sp[tid * kMixGenLD + cc], sx[tid * kMixGenLD + cc], accR);
+    else if (!TAIL && y && tid < n)
       for (int cc = 0; cc < width; ++cc) accR += sp[tid * kMixGenLD + cc];
     __syncthreads();
   }
   const int P = n * n + 2 * n;
-  float* pr = ws_p + (size_t)blockIdx.x * P;
-  if (tid < n) { pr[n * n + tid] = accR; pr[n * n + n + tid] = 0.f; }
+  float* pr = ws_p + (size_t)(row0 + blockIdx.x) * P;
+  if (tid < n) {
+    pr[n * n + tid] = TAIL ? 0.f : accR;
+    pr[n * n + n + tid] = TAIL ? accR : 0.f;
+  }
 #pragma unroll
   for (int q = 0; q < kMixMaxBlk; ++q) {
     const int blk = tid + q * kMixGenBD;
@@ -358,7 +383,103 @@ k_combine_bwd_generic(const XT* __restrict__ x, const YT* __restrict__ y,
         if (i < n && j < n) pr[i * n + j] = acc[q][a][b];
       }
   }
-  if (blockIdx.x == 0 && tid == 0) ws_hdr[0] = gridDim.x;
+  if (blockIdx.x == 0 && tid == 0) ws_hdr[TAIL ? 2 : 0] = gridDim.x;
+}
+
+// ------------------------------------------- rewire backward, x side (fast) --
+// n in {1, 2, 4}, 16-byte vectors: thread = (token, VEC columns) with the
+// x rows and the dx accumulators of all n streams in registers, Q and S in
+// registers across the thread's items.  p (d_xpre) may be NULL (zero), dx
+// may be NULL (only the parameter partials are wanted).
+template <int N, typename XT, typename DT, typename PT, int VEC>
+__global__ void __launch_bounds__(kMixBD, 2)
+k_rewire_bwd_x_fast(const XT* __restrict__ x, const DT* __restrict__ dout,
+                    const PT* __restrict__ dp, const float* __restrict__ Mg,
+                    const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
+                    XT* __restrict__ dx, int64_t T, int C, float* __restrict__ ws_p,
+                    int* __restrict__ ws_hdr) {
+  constexpr int P = N * N + 2 * N;
+  __shared__ float sM[N * N];
+  __shared__ float sacc[(kMixBD / 32) * P];
+  const int row0 = ws_hdr[0];
+  for (int e = threadIdx.x; e < N * N; e += blockDim.x) sM[e] = Mg[e];
+  float hpre[N], hpost[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    hpre[i] = __ldg(hpre_g + i);
+    hpost[i] = __ldg(hpost_g + i);
+  }
+  __syncthreads();
+  float aQ[N][N], aS[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    aS[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) aQ[i][j] = 0.f;
+  }
+  const int groups = C / VEC;
+  const int64_t items = T * groups;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < items;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = q / groups;
+    const int col = (int)(q - t * groups) * VEC;
+    const int64_t base = t * (int64_t)N * C + col;
+    float xr[N][VEC], o[N][VEC];
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      load_vec<XT, VEC>(x + base + (int64_t)j * C, xr[j]);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) o[j][v] = 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      float dr[VEC];
+      load_vec<DT, VEC>(dout + base + (int64_t)i * C, dr);
+#pragma unroll
+      for (int j = 0; j < N; ++j)
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) aQ[i][j] = fmaf(dr[v], xr[j][v], aQ[i][j]);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        const float z = hpost[i] * dr[v];
+#pragma unroll
+        for (int j = 0; j < N; ++j) o[j][v] = fmaf(sM[i * N + j], z, o[j][v]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      if (dp) {
+        float pv[VEC];
+        load_vec<PT, VEC>(dp + base + (int64_t)j * C, pv);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          aS[j] = fmaf(pv[v], xr[j][v], aS[j]);
+          o[j][v] += pv[v];
+        }
+      }
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) o[j][v] *= hpre[j];
+      if (dx) store_vec<XT, VEC>(dx + base + (int64_t)j * C, o[j]);
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float v = warp_sum(aQ[i][j]);
+      if (lane == 0) sacc[warp * P + i * N + j] = v;
+    }
+    const float r = warp_sum(aS[i]);
+    if (lane == 0) { sacc[warp * P + N * N + i] = 0.f; sacc[warp * P + N * N + N + i] = r; }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < P; e += blockDim.x) {
+    float s = 0.f;
+    for (int w = 0; w < nw; ++w) s += sacc[w * P + e];
+    ws_p[(size_t)(row0 + blockIdx.x) * P + e] = s;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) ws_hdr[2] = gridDim.x;
 }
 
 // ----------------------------------------------------------- prescale bwd --
@@ -482,6 +603,8 @@ k_residual_bwd(const OT* __restrict__ out, const DT* __restrict__ dout,
 //   mode 1 (rewire):   dM_ij = hpost_i hpre_j Q_ij, dhpre_j = sum_i hpost_i M_ij Q_ij,
 //                      dhpost_i = R_i + sum_j M_ij hpre_j Q_ij
 //   mode 2 (prescale): dhpre = R
+//   mode 3 (rewire end to end): as mode 1 with dhpre_j += S_j; the rows of
+//                      both passes are summed (header words 0 and 2)
 // The partial rows are summed in 32 interleaved slices per entry (slice r
 // takes rows r, r + 32, ...), then the slices in order: a fixed order for a
 // given row count, with 32x fewer dependent loads per thread (a one-CTA
@@ -493,22 +616,24 @@ __global__ void __launch_bounds__(kCFinBD)
 k_combine_finalize(const char* __restrict__ ws, int n, const float* __restrict__ M,
                    const float* __restrict__ hpre, const float* __restrict__ hpost, int mode,
                    float* __restrict__ dM, float* __restrict__ dhpre, float* __restrict__ dhpost) {
-  __shared__ float sQ[kMaxN * kMaxN + kMaxN];
+  __shared__ float sQ[kMaxN * kMaxN + 2 * kMaxN];
   __shared__ float part[kCFinSlices][32];
-  const int G = *reinterpret_cast<const int*>(ws);
+  const int* hdr = reinterpret_cast<const int*>(ws);
+  const int G = mode == 3 ? hdr[0] + hdr[2] : hdr[0];
   const int P = n * n + 2 * n;
+  const int E = mode == 3 ? P : n * n + n;  // entries summed
   const float* wp = reinterpret_cast<const float*>(ws + WsLayout::params_off());
   const int lane = threadIdx.x & 31, r0 = threadIdx.x >> 5;
-  for (int e0 = 0; e0 < n * n + n; e0 += 32) {
+  for (int e0 = 0; e0 < E; e0 += 32) {
     const int e = e0 + lane;
     float s = 0.f;
-    if (e < n * n + n) {
+    if (e < E) {
 #pragma unroll 4
       for (int g = r0; g < G; g += kCFinSlices) s += wp[(size_t)g * P + e];
     }
     part[r0][lane] = s;
     __syncthreads();
-    if (r0 == 0 && e < n * n + n) {
+    if (r0 == 0 && e < E) {
       float t = 0.f;
 #pragma unroll
       for (int q = 0; q < kCFinSlices; ++q) t += part[q][lane];
@@ -529,6 +654,7 @@ k_combine_finalize(const char* __restrict__ ws, int n, const float* __restrict__
     for (int j = threadIdx.x; j < n; j += blockDim.x) {
       float s = 0.f;
       for (int i = 0; i < n; ++i) s = fmaf(hpost[i] * M[i * n + j], sQ[i * n + j], s);
+      if (mode == 3) s += sR[n + j];
       if (dhpre) dhpre[j] = s;
     }
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -814,6 +940,104 @@ int launch_prescale_bwd(const void* x, int xdt, const void* d, int ddt, const fl
   k_combine_finalize<<<1, kCFinBD, 0, st>>>(static_cast<const char*>(ws), n, nullptr, nullptr, nullptr,
                                         2, nullptr, dhpre, nullptr);
   return check_launch("prescale_finalize");
+}
+
+// ---- MHCRewire end to end: dy side and x side ------------------------------------
+size_t rewire_fused_ws_bytes(int64_t T, int n, int C) {
+  (void)T; (void)C;
+  return WsLayout::bytes(2 * mix_rows_cap(), n, 0);
+}
+
+// dy_i = hpost_i d_i and R_i = sum d_i y_i: the pre-scale backward's
+// arithmetic with (y, hpost, dy) in place of (x, hpre, dx); its rows carry R
+// in slot n*n and zeros elsewhere, and it records G1 in header word 0.
+int launch_rewire_bwd_dy(const void* y, int ydt, const void* d, int ddt, const float* hpost,
+                         void* dy, int dydt, int64_t T, int n, int C, void* ws, size_t ws_bytes,
+                         cudaStream_t st) {
+  const size_t need = rewire_fused_ws_bytes(T, n, C);
+  if (!ws || ws_bytes < need)
+    return set_error(MHC_ERR_WORKSPACE, "rewire bwd: workspace %zu < %zu bytes", ws_bytes, need);
+  if (dydt != ydt) return set_error(MHC_ERR_UNSUPPORTED, "rewire bwd: dy dtype must equal y dtype");
+  if (ddt != ydt && ddt != MHC_F32)
+    return set_error(MHC_ERR_UNSUPPORTED, "rewire bwd: d_out dtype must be fp32 or y's dtype");
+  switch (ydt) {
+    case MHC_F32: return prescale_bwd_t<float, float>(y, d, hpost, dy, T, n, C, ws, st);
+    case MHC_BF16:
+      return ddt == MHC_F32 ? prescale_bwd_t<bf16, float>(y, d, hpost, dy, T, n, C, ws, st)
+                            : prescale_bwd_t<bf16, bf16>(y, d, hpost, dy, T, n, C, ws, st);
+    default:
+      return ddt == MHC_F32 ? prescale_bwd_t<f16, float>(y, d, hpost, dy, T, n, C, ws, st)
+                            : prescale_bwd_t<f16, f16>(y, d, hpost, dy, T, n, C, ws, st);
+  }
+}
+
+template <typename XT, typename DT, typename PT>
+static int rewire_x_t(const void* xv, const void* dv, const void* pv, const float* M,
+                      const float* hpre, const float* hpost, void* dxv, int64_t T, int n, int C,
+                      void* ws, cudaStream_t st) {
+  constexpr int VX = VecOf<XT>::value;
+  const XT* x = static_cast<const XT*>(xv);
+  const DT* d = static_cast<const DT*>(dv);
+  const PT* p = static_cast<const PT*>(pv);
+  XT* dx = static_cast<XT*>(dxv);
+  char* b = static_cast<char*>(ws);
+  float* wp = reinterpret_cast<float*>(b + WsLayout::params_off());
+  int* hdr = reinterpret_cast<int*>(b);
+  const int cap = mix_rows_cap();
+  const bool vec = (C % VX == 0) && all_aligned({xv, dv, pv, dxv});
+  if (vec && (n == 1 || n == 2 || n == 4)) {
+    const int G = elem_grid(T * (C / VX), cap);
+#define MHC_RX(NN) \
+  k_rewire_bwd_x_fast<NN, XT, DT, PT, VX><<<G, kMixBD, 0, st>>>(x, d, p, M, hpre, hpost, dx, T, C, wp, hdr)
+    if (n == 1) MHC_RX(1);
+    else if (n == 2) MHC_RX(2);
+    else MHC_RX(4);
+#undef MHC_RX
+    return check_launch("rewire_bwd_x");
+  }
+  const size_t smem = mix_gen_smem(n);
+  auto kern = k_combine_bwd_generic<XT, PT, DT, XT, XT, true>;
+  {
+    cudaError_t e = allow_dyn_smem(kern, smem);
+    if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "rewire_bwd_x: %s", cudaGetErrorString(e));
+  }
+  const int64_t ntile = T * ((C + kMixGenBD - 1) / kMixGenBD);
+  const int G = (int)(ntile < cap ? (ntile < 1 ? 1 : ntile) : cap);
+  kern<<<G, kMixGenBD, smem, st>>>(x, p, d, M, hpre, hpost, dx, nullptr, T, n, C, wp, hdr);
+  return check_launch("rewire_bwd_x(generic)");
+}
+
+template <typename XT>
+static int rewire_x_x(const void* x, int xdt, const void* d, int ddt, const void* p, int pdt,
+                      const float* M, const float* hpre, const float* hpost, void* dx, int64_t T,
+                      int n, int C, void* ws, cudaStream_t st) {
+  const bool d32 = ddt == MHC_F32, p32 = (p == nullptr) || pdt == MHC_F32;
+  if (!d32 && ddt != xdt) return set_error(MHC_ERR_UNSUPPORTED, "rewire bwd: d_out dtype must be fp32 or x's dtype");
+  if (!p32 && pdt != xdt) return set_error(MHC_ERR_UNSUPPORTED, "rewire bwd: d_xpre dtype must be fp32 or x's dtype");
+  if (d32 && p32) return rewire_x_t<XT, float, float>(x, d, p, M, hpre, hpost, dx, T, n, C, ws, st);
+  if (d32) return rewire_x_t<XT, float, XT>(x, d, p, M, hpre, hpost, dx, T, n, C, ws, st);
+  if (p32) return rewire_x_t<XT, XT, float>(x, d, p, M, hpre, hpost, dx, T, n, C, ws, st);
+  return rewire_x_t<XT, XT, XT>(x, d, p, M, hpre, hpost, dx, T, n, C, ws, st);
+}
+
+int launch_rewire_bwd_dx(const void* x, int xdt, const void* d, int ddt, const void* p, int pdt,
+                         const float* M, const float* hpre, const float* hpost, void* dx, int dxdt,
+                         float* dM, float* dhpre, float* dhpost, int64_t T, int n, int C, void* ws,
+                         size_t ws_bytes, cudaStream_t st) {
+  const size_t need = rewire_fused_ws_bytes(T, n, C);
+  if (!ws || ws_bytes < need)
+    return set_error(MHC_ERR_WORKSPACE, "rewire bwd: workspace %zu < %zu bytes", ws_bytes, need);
+  if (dx && dxdt != xdt) return set_error(MHC_ERR_UNSUPPORTED, "rewire bwd: dx dtype must equal x dtype");
+  int r;
+  switch (xdt) {
+    case MHC_F32: r = rewire_x_x<float>(x, xdt, d, ddt, p, pdt, M, hpre, hpost, dx, T, n, C, ws, st); break;
+    case MHC_BF16: r = rewire_x_x<bf16>(x, xdt, d, ddt, p, pdt, M, hpre, hpost, dx, T, n, C, ws, st); break;
+    default: r = rewire_x_x<f16>(x, xdt, d, ddt, p, pdt, M, hpre, hpost, dx, T, n, C, ws, st); break;
+  }
+  if (r != MHC_OK) return r;
+  k_combine_finalize<<<1, kCFinBD, 0, st>>>(static_cast<const char*>(ws), n, M, hpre, hpost, 3,
+                                            dM, dhpre, dhpost);
+  return check_launch("rewire_bwd_finalize");
 }
 
 // ---- residual add + aggregate ----------------------------------------------------

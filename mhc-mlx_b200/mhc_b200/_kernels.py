@@ -269,6 +269,48 @@ def rewire_bwd(x, y, dout, M, hpre, hpost):
     return dx, dy, dM, dpre, dpost
 
 
+def rewire_bwd_dy(y, dout, hpost):
+    """First half of MHCRewire's end-to-end backward (before the inner
+    module's backward): dy = H_post * d_out and the partial sums of
+    R = sum d_out * y, in a workspace that rewire_bwd_dx completes."""
+    dev = C.require_cuda(y, dout, hpost)
+    T, n, Cc = y.shape
+    with _on(dev):
+        yc = _io(y)
+        dc = _c(dout) if dout.dtype in (F32, yc.dtype) else dout.float().contiguous()
+        dy = torch.empty(T, n, Cc, dtype=yc.dtype, device=dev)
+        nb = _ws_bytes("mhc_rewire_fused_bwd_workspace_bytes", dev, T, n, Cc)
+        ws = _ws(nb, dev)
+        _call("mhc_rewire_bwd_dy", yc, C.ptr(yc), C.dtype_code(yc.dtype), C.ptr(dc),
+              C.dtype_code(dc.dtype), C.ptr(_f32(hpost)), C.ptr(dy), C.dtype_code(dy.dtype), T, n,
+              Cc, C.ptr(ws), nb, C.stream_of(yc))
+    return dy, (ws, nb, dc)
+
+
+def rewire_bwd_dx(x, d_xpre, M, hpre, hpost, state, want_dx: bool = True):
+    """Second half (after the inner module's backward gave d_xpre, or None):
+    dx written once, and dM, dH_pre_act (both branches), dH_post_act from one
+    reduction.  `state` is what rewire_bwd_dy returned."""
+    ws, nb, dc = state
+    dev = C.require_cuda(x, d_xpre, M, hpre, hpost)
+    T, n, Cc = x.shape
+    with _on(dev):
+        xc = _io(x)
+        pc = None
+        if d_xpre is not None:
+            pc = _c(d_xpre) if d_xpre.dtype in (F32, xc.dtype) else d_xpre.float().contiguous()
+        dx = torch.empty(T, n, Cc, dtype=xc.dtype, device=dev) if want_dx else None
+        dM = torch.empty(n, n, dtype=F32, device=dev)
+        dpre = torch.empty(n, dtype=F32, device=dev)
+        dpost = torch.empty(n, dtype=F32, device=dev)
+        _call("mhc_rewire_bwd_dx", xc, C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(dc),
+              C.dtype_code(dc.dtype), C.ptr(pc), C.dtype_code(pc.dtype if pc is not None else F32),
+              C.ptr(_f32(M)), C.ptr(_f32(hpre)), C.ptr(_f32(hpost)), C.ptr(dx),
+              C.dtype_code(xc.dtype), C.ptr(dM), C.ptr(dpre), C.ptr(dpost), T, n, Cc, C.ptr(ws), nb,
+              C.stream_of(xc))
+    return dx, dM, dpre, dpost
+
+
 def prescale_fwd(x, hpre, out_dtype=None) -> torch.Tensor:
     dev = C.require_cuda(x, hpre)
     T, n, Cc = x.shape

@@ -79,34 +79,83 @@ class _ParamsFn(torch.autograd.Function):
         return gpre, gpost, gres, None, None
 
 
+class _RewireLink:
+    """Hands d_out (and the partial sums of the dy side) from the
+    post-combine's backward to the pre-scale's backward within one
+    MHCRewire call, so that its backward writes dx once and reduces dH_pre
+    once (see _RewireCombineFn.backward)."""
+
+    __slots__ = ("state",)
+
+    def __init__(self):
+        self.state = None
+
+
 class _PrescaleFn(torch.autograd.Function):
-    """x_pre[t, i, c] = x[t, i, c] * H_pre_act[i]  (reference layer.py:478-480)."""
+    """x_pre[t, i, c] = x[t, i, c] * H_pre_act[i]  (reference layer.py:478-480).
+
+    M and H_post_act are inputs too (unused by the forward): when the
+    post-combine's backward has handed over d_out through `link`, this
+    backward is the x side of MHCRewire's end-to-end backward and returns
+    the gradients of x, M, H_pre_act and H_post_act of the whole layer."""
 
     @staticmethod
-    def forward(ctx, x, hpre):
-        ctx.save_for_backward(x, hpre)
+    def forward(ctx, x, M, hpre, hpost, link=None):
+        ctx.save_for_backward(x, M, hpre, hpost)
+        ctx.link = link
         return K.prescale_fwd(x, hpre)
 
     @staticmethod
     def backward(ctx, d):
-        x, hpre = ctx.saved_tensors
+        x, M, hpre, hpost = ctx.saved_tensors
+        link = ctx.link
+        if link is not None and link.state is not None:
+            state, link.state = link.state, None
+            dx, dM, dpre, dpost = K.rewire_bwd_dx(x, d, M, hpre, hpost, state,
+                                                  want_dx=ctx.needs_input_grad[0])
+            return dx, dM, dpre, dpost, None
         dx, dpre = K.prescale_bwd(x, d, hpre)
-        return dx, dpre
+        return dx, None, dpre, None, None
+
+
+def _engine_will_run(node) -> bool:
+    """Whether the autograd engine runs `node` in the backward pass now in
+    progress (torch's own multi-grad hooks ask the same question)."""
+    if node is None:
+        return False
+    try:
+        return bool(torch._C._will_engine_execute_node(node))
+    except RuntimeError:
+        return False
 
 
 class _RewireCombineFn(torch.autograd.Function):
-    """out = H_post (y_inner + M (H_pre x))  (reference layer.py:302-337)."""
+    """out = H_post (y_inner + M (H_pre x))  (reference layer.py:302-337).
+
+    Inside MHCRewire (link and the pre-scale's autograd node given), the
+    backward is split around the inner module's backward when the engine will
+    also run the pre-scale's backward: here only dy = H_post * d_out and the
+    partial sums of R = sum d_out * y are computed, and the pre-scale's
+    backward then writes dx = H_pre (M^T (H_post d_out) + d_xpre) once and
+    reduces dM, dH_pre (both branches) and dH_post in one finalize.
+    Otherwise (post_combine on its own, or a backward that does not reach the
+    pre-scale) this backward returns every gradient itself."""
 
     @staticmethod
-    def forward(ctx, x, y, M, hpre, hpost, out_dtype=torch.float32):
+    def forward(ctx, x, y, M, hpre, hpost, out_dtype=torch.float32, link=None, node=None):
         ctx.save_for_backward(x, y, M, hpre, hpost)
+        ctx.link, ctx.node = link, node
         return K.rewire_fwd(x, y, M, hpre, hpost, out_dtype)
 
     @staticmethod
     def backward(ctx, dout):
         x, y, M, hpre, hpost = ctx.saved_tensors
+        if ctx.link is not None and _engine_will_run(ctx.node):
+            dy, state = K.rewire_bwd_dy(y, dout, hpost)
+            ctx.link.state = state
+            return None, dy, None, None, None, None, None, None
         dx, dy, dM, dpre, dpost = K.rewire_bwd(x, y, dout, M, hpre, hpost)
-        return dx, dy, dM, dpre, dpost, None
+        return dx, dy, dM, dpre, dpost, None, None, None
 
 
 # --------------------------------------------------------------- modules --
@@ -301,8 +350,9 @@ class MHCRewire(nn.Module):
         self.mhc._require_cuda_path(B, self.n, C)
         hpre, hpost, M = self.mhc.activations()
         x3 = x.reshape(-1, self.n, C)
-        x_pre = _PrescaleFn.apply(x3, hpre).reshape(x.shape)
-        y_inner = self.inner(x_pre)
+        link = _RewireLink()
+        x_pre3 = _PrescaleFn.apply(x3, M, hpre, hpost, link)
+        y_inner = self.inner(x_pre3.reshape(x.shape))
         if tuple(y_inner.shape) != tuple(x.shape):
             raise ValueError(
                 f"inner module output shape {tuple(y_inner.shape)} must equal its input shape "
@@ -310,5 +360,6 @@ class MHCRewire(nn.Module):
         odt = torch.float32
         if self.output_dtype == "input" and x.dtype in _HALF:
             odt = x.dtype
-        out = _RewireCombineFn.apply(x3, y_inner.reshape(-1, self.n, C), M, hpre, hpost, odt)
+        out = _RewireCombineFn.apply(x3, y_inner.reshape(-1, self.n, C), M, hpre, hpost, odt,
+                                     link, x_pre3.grad_fn)
         return out.reshape(x.shape)

@@ -235,6 +235,128 @@ def test_rewire_combine_kernel_matches_oracle(dt):
         assert rel_err(a, b) < (tol_act if k < 2 else 1e-5), k
 
 
+# ------------------------------------------- MHCRewire end-to-end backward --
+def _fused_rewire_ref(x, y, M, hpre, hpost, d, p):
+    """Gradients of <out, d> + <x * hpre, p> for the post-combine
+    out = (y + (M * hpre) x) * hpost: the x-side gradients of MHCRewire when
+    p is the inner module's input gradient (reference layer.py:469-492)."""
+    leaves = [t.double().requires_grad_(True) for t in (x, M, hpre, hpost)]
+    xd, Md, ad, bd = leaves
+    out = (y.double() + torch.einsum("ij,bjc->bic", Md * ad[None, :], xd)) * bd[None, :, None]
+    loss = (out * d.double()).sum()
+    if p is not None:
+        loss = loss + (xd * ad[None, :, None] * p.double()).sum()
+    return torch.autograd.grad(loss, leaves), hpost.double()[None, :, None] * d.double()
+
+
+@pytest.mark.parametrize("B,n,C,dt,with_p", [(5, 4, 1024, torch.float32, True),
+                                             (5, 4, 1024, torch.bfloat16, True),
+                                             (3, 4, 1024, torch.bfloat16, False),
+                                             (7, 2, 64, torch.float32, True),
+                                             (4, 4, 129, torch.float32, True),
+                                             (3, 3, 40, torch.bfloat16, True),
+                                             (2, 16, 256, torch.float32, True),
+                                             (2, 8, 64, torch.float32, False),
+                                             (1, 32, 64, torch.float32, True)])
+def test_rewire_split_backward_kernels_match_oracle(B, n, C, dt, with_p):
+    """mhc_rewire_bwd_dy + mhc_rewire_bwd_dx through the C ABI: dy, dx (both
+    branches, written once) and dM / dH_pre / dH_post from one reduction,
+    against float64 autograd; d_xpre NULL counts as zero."""
+    from mhc_b200 import _kernels as K
+
+    g = torch.Generator().manual_seed(31 * n + C + B)
+    x = torch.randn(B, n, C, generator=g).to(dt)
+    y = torch.randn(B, n, C, generator=g).to(dt)
+    M = O.mixing_matrix_from_logits(torch.randn(n, n, generator=g), 20, 1e-5)
+    hpre, hpost = torch.rand(n, generator=g), 2 * torch.rand(n, generator=g)
+    d = torch.randn(B, n, C, generator=g)
+    pg = torch.randn(B, n, C, generator=g).to(dt) if with_p else None
+    (gx, gM, gpre, gpost), dy_ref = _fused_rewire_ref(x, y, M, hpre, hpost, d, pg)
+    dy, state = K.rewire_bwd_dy(cu(y, dt), cu(d), cu(hpost))
+    dx, dM, dpre, dpost = K.rewire_bwd_dx(cu(x, dt), None if pg is None else cu(pg, dt), cu(M),
+                                          cu(hpre), cu(hpost), state)
+    tol_act = 1e-5 if dt == torch.float32 else 1e-2
+    assert dy.dtype == dt and dx.dtype == dt
+    assert rel_err(dy, dy_ref) < tol_act
+    assert rel_err(dx, gx) < tol_act
+    for name, a, b in (("dM", dM, gM), ("dH_pre", dpre, gpre), ("dH_post", dpost, gpost)):
+        assert rel_err(a, b) < 1e-5, (name, rel_err(a, b))
+
+
+def test_rewire_backward_runs_no_torch_elementwise_kernel():
+    """MHCRewire's backward around a frozen bias-free Linear (BASELINE config 4
+    layout, bf16): the GPU kernels it launches are this library's and the
+    inner GEMM only; dx is written once, so no torch add / copy kernel runs
+    on [T, n, C]."""
+    from torch.profiler import ProfilerActivity, profile
+
+    T, dims, n = 512, 4096, 4
+    lin = nn.Linear(dims, dims, bias=False).to(DEV, torch.bfloat16).requires_grad_(False)
+    model = mhc_b200.MHCRewire(lin, dims=dims, n=n).to(DEV)
+    x = torch.randn(T, dims, device=DEV).to(torch.bfloat16).requires_grad_(True)
+    d = torch.randn(T, dims, device=DEV)
+    for _ in range(2):
+        model(x).backward(d)
+    out = model(x)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        out.backward(d)
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    kernels = [k for k in names if not k.startswith(("Memcpy", "Memset"))]
+    ours = [k for k in kernels if "mhc::" in k]
+    assert any("k_rewire_bwd_x" in k for k in ours), kernels
+    assert not any("k_combine_bwd" in k for k in ours), ours  # the unsplit backward did not run
+    stray = [k for k in kernels if "mhc::" not in k and "elementwise" in k.lower()]
+    assert not stray, stray
+
+
+def test_rewire_backward_without_a_path_to_the_prescale():
+    """When the backward does not reach the pre-scale (an inner module that
+    ignores its input, or gradients asked only for the inner weights), the
+    post-combine's backward returns every gradient itself."""
+    g = torch.Generator().manual_seed(5)
+    dims, n, rows = 64, 4, 3
+    x = torch.randn(rows, dims, generator=g)
+    d = torch.randn(rows, dims, generator=g)
+
+    class Const(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.c = nn.Parameter(torch.randn(dims, generator=g))
+
+        def forward(self, v):
+            return self.c.expand_as(v)
+
+    inner = Const().to(DEV)
+    model = mhc_b200.MHCRewire(inner, dims=dims, n=n).to(DEV)
+    with torch.no_grad():
+        model.mhc.H_pre_raw.copy_(0.5 * torch.randn(n, generator=g))
+        model.mhc.H_res_raw.copy_(torch.randn(n, n, generator=g))
+    xg = cu(x).requires_grad_(True)
+    model(xg).backward(cu(d))
+    leaves = [t.double().requires_grad_(True) for t in
+              (x, model.mhc.H_pre_raw.detach().cpu(), model.mhc.H_post_raw.detach().cpu(),
+               model.mhc.H_res_raw.detach().cpu())]
+    c = inner.c.detach().cpu().double()
+    out_ref = O.rewire_reference(lambda v: c.expand_as(v), leaves[0], n, *leaves[1:], 20, 1e-5,
+                                 dtype=F64)
+    g_ref = torch.autograd.grad(out_ref, leaves, d.double())
+    for a, b in zip((xg.grad, model.mhc.H_pre_raw.grad, model.mhc.H_post_raw.grad,
+                     model.mhc.H_res_raw.grad), g_ref):
+        assert rel_err(a, b) < 1e-5
+    # gradients of the inner weights only: the pre-scale is not on the path
+    lin = nn.Linear(dims, dims).to(DEV)
+    model2 = mhc_b200.MHCRewire(lin, dims=dims, n=n).to(DEV)
+    out = model2(cu(x).requires_grad_(True))
+    (gw,) = torch.autograd.grad(out, [lin.weight], cu(d))
+    pre = torch.sigmoid(model2.mhc.H_pre_raw.detach())
+    post = 2 * torch.sigmoid(model2.mhc.H_post_raw.detach())
+    dy = (cu(d).view(rows, n, -1) * post[None, :, None]).view(rows, dims)
+    xp = (cu(x).view(rows, n, -1) * pre[None, :, None]).view(rows, dims)
+    assert rel_err(gw, dy.T @ xp) < 1e-5
+
+
 # --------------------------------------------------------- residual agg --
 @pytest.mark.parametrize("B,n,C,dt", [(2, 4, 128, torch.float32), (3, 4, 129, torch.float32),
                                       (2, 16, 64, torch.bfloat16), (2, 5, 32, torch.float16)])
