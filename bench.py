@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-latency", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the compact BASELINE config 1-5 records of the default run")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--workload", choices=["layer", "sweep", "sinkhorn", "rewire", "llama", "all"],
                     default="layer",
@@ -132,6 +134,24 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------- workload --
+def workload_name(T, n, C, io):
+    """The headline workload, named identically by both arms."""
+    return (f"MHCLayer fwd+bwd (+grad all-reduce when N>1, SGD) T={T} tokens/GPU, n={n}, C={C}, "
+            f"{io} I/O, fp32 math, 20 Sinkhorn iters")
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
 def algo_bytes(T, n, C, s_x, s_out, s_dout, s_dx):
     """Algorithmic HBM bytes per launch (one read of every input, one write of
     every output; the O(C) parameter traffic added per call)."""
@@ -154,9 +174,13 @@ def make_layer(n, C, dev):
 
 
 def make_step(layer, x, d, rdt, world):
+    from mhc_b200 import _kernels
     from mhc_b200 import dist as mdist
 
     params = list(layer.parameters())
+    # one flat gradient buffer: the backward's finalize writes the parameter
+    # gradients into it and the step's all-reduce is one NCCL call on it
+    bucket = mdist.GradBucket(layer) if world > 1 else None
 
     def step():
         for p in params:
@@ -165,7 +189,8 @@ def make_step(layer, x, d, rdt, world):
         out = layer(x, return_dtype=rdt)
         out.backward(d)
         if world > 1:
-            mdist.allreduce_grads(params)
+            with _kernels._timed("nccl_allreduce_grads", x):
+                bucket.allreduce()
         with torch.no_grad():
             torch._foreach_add_(params, [p.grad for p in params], alpha=-1e-3)
         return out
@@ -231,6 +256,7 @@ def e2e_measure(layer, T, n, C, iodt, rdt, dev, steps, world, chunks=8):
     xd = [torch.empty(Tc, n, C, dtype=iodt, device=dev) for _ in range(2)]
     dd = [torch.empty(Tc, n, C, dtype=odt, device=dev) for _ in range(2)]
     params = list(layer.parameters())
+    bucket = mdist.GradBucket(layer) if world > 1 else None
     comp = torch.cuda.current_stream(dev)
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev_in = [torch.cuda.Event() for _ in range(2)]
@@ -261,7 +287,7 @@ def e2e_measure(layer, T, n, C, iodt, rdt, dev, steps, world, chunks=8):
             out.record_stream(s_out)
             dx.record_stream(s_out)
         if world > 1:
-            mdist.allreduce_grads(params)
+            bucket.allreduce()
         with torch.no_grad():
             torch._foreach_add_(params, [p.grad for p in params], alpha=-1e-3)
         comp.wait_stream(s_out)
@@ -305,7 +331,11 @@ def e2e_measure(layer, T, n, C, iodt, rdt, dev, steps, world, chunks=8):
     return {"value": world * T / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms,
             "h2d_bytes_per_step": per_dir, "d2h_bytes_per_step": per_dir,
             "link": {"bound": "pcie", "achieved_gbs_per_direction": achieved,
-                     "measured_bidirectional_gbs_per_direction": link, "frac": achieved / link},
+                     "measured_bidirectional_gbs_per_direction": link, "frac": achieved / link,
+                     "aggregate_gbs_per_direction_all_ranks": world * achieved,
+                     "note": "per-rank figures; at N>1 every rank streams its host tensors at "
+                             "once through the same host memory and PCIe switches, and the "
+                             "link ceiling is measured per rank at the same time"},
             "path": f"MHCLayer forward+backward on pinned host tensors, {chunks} token chunks, "
                     "H2D/compute/D2H overlapped on 3 streams"}
 
@@ -319,7 +349,10 @@ def cpu_oracle_step(T, n, C, iters, dtype=torch.float32, seed=0):
     params = [0.1 * torch.randn(n, generator=g), 0.1 * torch.randn(n, generator=g),
               0.1 * torch.randn(n, n, generator=g), torch.ones(C)]
     t0 = time.perf_counter()
-    O.layer_grads(x, *params, d, iters, 1e-5, dtype=dtype)
+    grads = O.layer_grads(x, *params, d, iters, 1e-5, dtype=dtype)[2:]
+    with torch.no_grad():  # the step's SGD update of the four mHC parameters
+        for p_, g_ in zip(params, grads):
+            p_.add_(g_.to(p_.dtype), alpha=-1e-3)
     return time.perf_counter() - t0
 
 
@@ -334,6 +367,7 @@ def cpu_baseline(n, C, seconds, iters=20):
     times = [cpu_oracle_step(T, n, C, iters, seed=k) for k in range(3)]
     med = statistics.median(times)
     return {"value": T / med, "unit": UNIT, "cores": cores, "kind": "port",
+            "cpu_model": cpu_model(),
             "sample": f"{T} of the 65536 tokens per step, fwd+bwd fp32 (oracle restatement of "
                       f"mhc_mlx/reference.py + torch autograd), median of 3, {torch.get_num_threads()} threads"}
 
@@ -445,8 +479,7 @@ def run_b200(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"MHCLayer fwd+bwd (+grad all-reduce, SGD) T={T} tokens/GPU, n={n}, "
-                               f"C={C}, {args.io_dtype} I/O, fp32 math, 20 Sinkhorn iters",
+        "config": {"workload": workload_name(T, n, C, args.io_dtype),
                    "tokens_per_gpu": T, "n": n, "C": C, "io_dtype": args.io_dtype,
                    "sinkhorn_iters": 20, "parallelism": f"dp{world}",
                    "l2": "inputs larger than L2 (T*n*C elements per tensor); no flush"},
@@ -468,14 +501,39 @@ def run_b200(args):
                                     "bwd_achieved_gbs": b2 / (bu * 1e-6) / 1e9 if bu else None,
                                     "step_achieved_gbs": (f2 + b2) / (ms2 * 1e-3) / 1e9,
                                     "kernels": ks2}
+    if world > 1:
+        # which rank limits the step: per-rank kernel times (min / max over
+        # ranks) and the all-reduce's CUDA-event time per step
+        keys = ("mhc_params_fwd", "mhc_fwd", "mhc_bwd", "mhc_bwd_finalize", "nccl_allreduce_grads")
+        mine = torch.tensor([kstats.get(k, {}).get("avg_us", 0.0) for k in keys] + [ms],
+                            device=dev, dtype=torch.float64)
+        allr = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+        allr = torch.stack(allr).cpu()
+        per_rank = {k: {"min_us": float(allr[:, i].min()), "max_us": float(allr[:, i].max()),
+                        "argmax_rank": int(allr[:, i].argmax())} for i, k in enumerate(keys)}
+        per_rank["step_ms"] = {"min": float(allr[:, -1].min()), "max": float(allr[:, -1].max())}
+        kern_max = float((allr[:, 1] + allr[:, 2] + allr[:, 0] + allr[:, 3]).max()) / 1e3
+        res["per_rank"] = per_rank
+        res["attribution"] = {
+            "step_ms_max_rank": ms,
+            "mhc_kernels_ms_slowest_rank": kern_max,
+            "allreduce_ms_max_rank": per_rank["nccl_allreduce_grads"]["max_us"] / 1e3,
+            "rest_ms": ms - kern_max - per_rank["nccl_allreduce_grads"]["max_us"] / 1e3,
+            "note": "rest = SGD update, launch gaps and the wait for the slowest rank"}
     if not args.no_e2e:
         iodt = torch.float32 if args.io_dtype == "f32" else torch.bfloat16
         rdt = None if args.io_dtype == "f32" else torch.bfloat16
         res["e2e"] = e2e_measure(layer, T, n, C, iodt, rdt, dev, args.e2e_steps, world)
+    del layer
+    torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not args.no_latency:
         res["latency_b1"] = latency_b1(make_layer(n, C, dev), n, C, dev)
     if rank == 0 and world == 1 and not args.no_cpu:
         res["cpu_baseline"] = cpu_baseline(n, C, args.cpu_seconds)
+    if not args.no_configs:
+        torch.cuda.empty_cache()
+        res.update(secondary_configs(dev, rank, world, peak, peak_kind))
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -502,19 +560,22 @@ def run_reference(args):
     times = [cpu_oracle_step(Ts, n, C, 20, seed=100 + k) for k in range(args.steps)]
     sec = sum(times)
     value = Ts * args.steps / sec
-    sample = (f"{Ts} tokens per step of the {args.tokens}-token workload, fwd+bwd fp32 "
-              f"(oracle restatement of mhc_mlx/reference.py, torch autograd), {cores} threads")
+    sample = (f"{Ts} tokens per step of the {args.tokens}-token workload (fwd+bwd fp32 + SGD, "
+              f"oracle restatement of mhc_mlx/reference.py with torch autograd), {cores} threads; "
+              "value = sampled tokens / time")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sec / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": f"MHCLayer fwd+bwd T={args.tokens} tokens/GPU, n={n}, C={C}, "
-                               f"{args.io_dtype} I/O, fp32 math, 20 Sinkhorn iters",
+        "config": {"workload": workload_name(args.tokens, n, C, args.io_dtype),
                    "tokens_per_gpu": args.tokens, "n": n, "C": C, "io_dtype": args.io_dtype,
-                   "parallelism": "host cores"},
+                   "sinkhorn_iters": 20, "parallelism": "host cores (rank 0)"},
+        "sampling": {"tokens_timed_per_step": Ts, "tokens_per_step_in_workload": args.tokens,
+                     "why": "the CPU oracle takes about 7 s for the full 65,536-token step; a "
+                            "bounded sample keeps --steps K --warmup W within a few minutes"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": sample},
+                         "cpu_model": cpu_model(), "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -568,165 +629,165 @@ def _kernel_us_per_step(step, dev, steps=20):
     return sum(per.values()), per
 
 
-def run_configs(args):
+def config1_quickstart(dev):
+    """README quick-start, MHCRewire(Linear(2048, 2048),
+    n=32), one fp32 row, loss = sum(y), grads of all parameters."""
     import mhc_b200
-    from mhc_b200 import metal
+    from torch import nn
 
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    peak, peak_kind = load_peaks()
-    out = []
-    w = args.workload
-    if w in ("sweep", "all"):
-        # config 2: MHCLayer x[B, 4, C], B in {1, 32}, C in {512, 2048, 4096}, fp32 / bf16
-        rows = []
-        for io in ("f32", "bf16"):
-            dt = torch.float32 if io == "f32" else torch.bfloat16
-            for C in (512, 2048, 4096):
-                for B in (1, 32):
-                    layer = make_layer(4, C, dev)
-                    x = torch.randn(B, 4, C, device=dev).to(dt).requires_grad_(True)
-                    rdt = None if io == "f32" else dt
-                    d = torch.randn(B, 4, C, device=dev).to(rdt or torch.float32)
+    torch.manual_seed(0)
+    model = mhc_b200.MHCRewire(nn.Linear(2048, 2048), dims=2048, n=32).to(dev)
+    x = torch.randn(1, 2048, device=dev, requires_grad=True)
 
-                    def fb():
-                        x.grad = None
-                        for p_ in layer.parameters():
-                            p_.grad = None
-                        layer(x, return_dtype=rdt).backward(d)
+    def fb1():
+        x.grad = None
+        for p_ in model.parameters():
+            p_.grad = None
+        model(x).sum().backward()
 
-                    def fo():
-                        with torch.no_grad():
-                            layer(x, return_dtype=rdt)
+    mk, per1 = _kernel_us_per_step(fb1, dev)
+    return {"metric": "MHCRewire quick-start fwd+bwd latency (BASELINE config 1)",
+            "unit": "us", "higher_is_better": False,
+            "eager_us": _median_us(fb1, dev), "graph_us": _graph_us(fb1, dev),
+            "mhc_kernels_event_us": mk, "mhc_kernels": per1,
+            "config": {"workload": "MHCRewire(nn.Linear(2048, 2048), dims=2048, n=32), x (1, 2048) "
+                                   "fp32, loss = sum(y), grads of all params",
+                       "note": "graph_us = replay of one captured fwd+bwd incl. the 2048x2048 "
+                               "GEMMs; per-kernel event times include host gaps in eager mode"}}
 
-                    rows.append({"io": io, "B": B, "C": C, "fwd_us": _median_us(fo, dev),
-                                 "fwd_bwd_us": _median_us(fb, dev),
-                                 "fwd_bwd_graph_us": _graph_us(fb, dev)})
-        out.append({"metric": "MHCLayer per-call latency, BASELINE config 2 sweep (n=4)",
-                    "unit": "us", "higher_is_better": False, "rows": rows,
-                    "config": {"workload": "config 2 op sweep", "n": 4,
-                               "note": "median of 200 calls, CUDA events; graph = replay of one "
-                                       "captured fwd+bwd"}})
-        # the shapes the reference publishes MHCLayer forward timings for
-        # (BENCHMARKS.csv: n=32, fp32, B=1 latency and B=32 per-call time),
-        # with its Apple M4 Pro numbers beside ours as context only
-        published = {(1, 256): 514.33, (1, 512): 430.67, (1, 1024): 437.08, (1, 2048): 520.04,
-                     (1, 4096): 406.88, (32, 512): 117.73, (32, 2048): 1529.09,
-                     (32, 4096): 2078.89}
-        rows = []
-        for (B, C), ref_us in list(published.items()) + [((256, 4096), None)]:
-            layer = make_layer(32, C, dev)
-            x = torch.randn(B, 32, C, device=dev)
-            xg = x.clone().requires_grad_(True)
-            d = torch.randn(B, 32, C, device=dev)
 
-            def fo():
-                with torch.no_grad():
-                    layer(x)
+def config2_sweep(dev, iters=200):
+    """MHCLayer x[B, 4, C], B in {1, 32}, C in {512, 2048,
+    4096}, fp32 / bf16 (bf16 in -> bf16 out), fwd and fwd+bwd per call."""
+    rows = []
+    for io in ("f32", "bf16"):
+        dt = torch.float32 if io == "f32" else torch.bfloat16
+        for C in (512, 2048, 4096):
+            for B in (1, 32):
+                layer = make_layer(4, C, dev)
+                x = torch.randn(B, 4, C, device=dev).to(dt).requires_grad_(True)
+                rdt = None if io == "f32" else dt
+                d = torch.randn(B, 4, C, device=dev).to(rdt or torch.float32)
 
-            def fb():
-                xg.grad = None
-                for p_ in layer.parameters():
-                    p_.grad = None
-                layer(xg).backward(d)
+                def fb():
+                    x.grad = None
+                    for p_ in layer.parameters():
+                        p_.grad = None
+                    layer(x, return_dtype=rdt).backward(d)
 
-            _, per32 = _kernel_us_per_step(fb, dev)
-            rows.append({"B": B, "C": C, "fwd_us": _median_us(fo, dev),
-                         "fwd_graph_us": _graph_us(fo, dev),
-                         "fwd_bwd_graph_us": _graph_us(fb, dev),
-                         "fwd_bwd_kernels_us": {k: round(v, 1) for k, v in per32.items()},
-                         "reference_m4pro_fwd_us": ref_us})
-        out.append({"metric": "MHCLayer per-call time at the reference's published shapes "
-                              "(n=32, fp32; forward, and forward+backward)",
-                    "unit": "us", "higher_is_better": False, "rows": rows,
-                    "config": {"workload": "BENCHMARKS.csv MHCLayer rows (+ B=256, C=4096)",
-                               "n": 32,
-                               "note": "reference_m4pro_fwd_us: the reference's published Apple "
-                                       "M4 Pro Metal forward timings, other hardware, context "
-                                       "only (it publishes no backward timing)"}})
-    if w in ("sinkhorn", "all"):
-        # config 3: 65,536 independent 4x4 logits, 20 iterations, fwd + bwd
-        from mhc_b200 import _kernels as K
+                def fo():
+                    with torch.no_grad():
+                        layer(x, return_dtype=rdt)
 
-        H = torch.randn(65536, 4, 4, device=dev)
-        dM = torch.randn(65536, 4, 4, device=dev)
-        def sk_step():
-            K.sinkhorn_batched_fwd(H, 20, 1e-5)
-            K.sinkhorn_batched_bwd(H, dM, 20, 1e-5)
+                rows.append({"io": io, "B": B, "C": C, "fwd_us": _median_us(fo, dev, iters),
+                             "fwd_bwd_us": _median_us(fb, dev, iters),
+                             "fwd_bwd_graph_us": _graph_us(fb, dev, iters)})
+    return rows
 
-        tot, per = _kernel_us_per_step(sk_step, dev, steps=50)
-        fw, bw = per["mhc_sinkhorn_batched_fwd"], per["mhc_sinkhorn_batched_bwd"]
-        out.append({"metric": "batched Sinkhorn fwd+bwd matrices/s (65,536 x 4x4, 20 iters)",
-                    "value": 65536 / (tot * 1e-6), "unit": "matrices/s", "higher_is_better": True,
-                    "fwd_us": fw, "bwd_us": bw,
-                    "fwd_gbs": 65536 * 128 / (fw * 1e-6) / 1e9,
-                    "bwd_gbs": 65536 * 192 / (bw * 1e-6) / 1e9,
-                    "config": {"workload": "BASELINE config 3", "note": "8 MB working set: "
-                               "L2-resident, latency/compute-bound (backward replays 20 "
-                               "iterations and reverses them)"}})
-    if w in ("rewire", "all"):
-        from torch import nn
 
-        # config 1: README quick-start, MHCRewire(Linear(2048, 2048), n=32), one row, fp32
-        torch.manual_seed(0)
-        model = mhc_b200.MHCRewire(nn.Linear(2048, 2048), dims=2048, n=32).to(dev)
-        x = torch.randn(1, 2048, device=dev, requires_grad=True)
+def config2_n32_rows(dev):
+    """The shapes the reference publishes MHCLayer forward timings for
+    (BENCHMARKS.csv: n=32, fp32, B=1 latency and B=32 per-call time), with its
+    Apple M4 Pro numbers beside ours as context only."""
+    published = {(1, 256): 514.33, (1, 512): 430.67, (1, 1024): 437.08, (1, 2048): 520.04,
+                 (1, 4096): 406.88, (32, 512): 117.73, (32, 2048): 1529.09,
+                 (32, 4096): 2078.89}
+    rows = []
+    for (B, C), ref_us in list(published.items()) + [((256, 4096), None)]:
+        layer = make_layer(32, C, dev)
+        x = torch.randn(B, 32, C, device=dev)
+        xg = x.clone().requires_grad_(True)
+        d = torch.randn(B, 32, C, device=dev)
 
-        def fb1():
-            x.grad = None
-            for p_ in model.parameters():
+        def fo():
+            with torch.no_grad():
+                layer(x)
+
+        def fb():
+            xg.grad = None
+            for p_ in layer.parameters():
                 p_.grad = None
-            model(x).sum().backward()
+            layer(xg).backward(d)
 
-        mk, per1 = _kernel_us_per_step(fb1, dev)
-        out.append({"metric": "MHCRewire quick-start fwd+bwd latency (BASELINE config 1)",
-                    "unit": "us", "higher_is_better": False,
-                    "eager_us": _median_us(fb1, dev), "graph_us": _graph_us(fb1, dev),
-                    "mhc_kernels_us": mk, "mhc_kernels": per1,
-                    "config": {"workload": "MHCRewire(nn.Linear(2048, 2048), dims=2048, n=32), "
-                                           "x (1, 2048) fp32, loss = sum(y), grads of all params"}})
-        # config 4: MHCRewire around a 4-bit QuantizedLinear 4096 -> 4096, n=4, 8192 bf16 tokens
-        g = torch.Generator().manual_seed(4)
-        ql = mhc_b200.QuantizedLinear.random(4096, 4096, group_size=64, bits=4,
-                                             dtype=torch.bfloat16, generator=g).to(dev)
-        model4 = mhc_b200.MHCRewire(ql, dims=4096, n=4).to(dev)
-        x4 = torch.randn(8192, 4096, device=dev).to(torch.bfloat16).requires_grad_(True)
-        d4 = torch.randn(8192, 4096, device=dev)
-
-        def fb4():
-            x4.grad = None
-            for p_ in model4.parameters():
-                p_.grad = None
-            model4(x4).backward(d4)
-
-        mk4, per4 = _kernel_us_per_step(fb4, dev)
-        step_us = _median_us(fb4, dev, iters=30, warm=3)
-        # algorithmic bytes of the mHC kernels per step (bf16 x / y_inner / dy / d_xpre /
-        # dx, fp32 out / d_out), bytes per element:
-        #   prescale fwd x -> x_pre 2+2; combine fwd x, y -> out 2+2+4;
-        #   backward dy side y, d -> dy 2+4+2; x side x, d, d_xpre -> dx 2+4+2+2
-        elems = 8192 * 4096
-        mbytes = elems * ((2 + 2) + (2 + 2 + 4) + (2 + 4 + 2) + (2 + 4 + 2 + 2))
-        out.append({"metric": "MHCRewire(QuantizedLinear 4096, n=4) mHC fwd+bwd tokens/s, GEMM "
-                              "excluded (BASELINE config 4)",
-                    "value": 8192 / (mk4 * 1e-6), "unit": "tokens/s", "higher_is_better": True,
-                    "mhc_kernels_us": mk4, "mhc_kernels": per4,
-                    "mhc_achieved_gbs": mbytes / (mk4 * 1e-6) / 1e9, "peak": peak,
-                    "whole_step_us_incl_gemm": step_us,
-                    "config": {"workload": "8192 bf16 tokens, 4-bit affine QuantizedLinear "
-                                           "(group 64), random codes, fp16-range scales",
-                               "peak_source": f"{peak_kind} hbm_gbs"}})
-    for r in out:
-        print(json.dumps(r), flush=True)
+        _, per32 = _kernel_us_per_step(fb, dev)
+        rows.append({"B": B, "C": C, "fwd_us": _median_us(fo, dev),
+                     "fwd_graph_us": _graph_us(fo, dev),
+                     "fwd_bwd_graph_us": _graph_us(fb, dev),
+                     "fwd_bwd_kernels_us": {k: round(v, 1) for k, v in per32.items()},
+                     "reference_m4pro_fwd_us": ref_us})
+    return rows
 
 
-def run_llama(args):
+def config3_sinkhorn(dev):
+    """65,536 independent 4x4 logits, 20 iterations, fwd + bwd."""
+    from mhc_b200 import _kernels as K
+
+    H = torch.randn(65536, 4, 4, device=dev)
+    dM = torch.randn(65536, 4, 4, device=dev)
+
+    def sk_step():
+        K.sinkhorn_batched_fwd(H, 20, 1e-5)
+        K.sinkhorn_batched_bwd(H, dM, 20, 1e-5)
+
+    tot, per = _kernel_us_per_step(sk_step, dev, steps=50)
+    fw, bw = per["mhc_sinkhorn_batched_fwd"], per["mhc_sinkhorn_batched_bwd"]
+    return {"metric": "batched Sinkhorn fwd+bwd matrices/s (65,536 x 4x4, 20 iters)",
+            "value": 65536 / (tot * 1e-6), "unit": "matrices/s", "higher_is_better": True,
+            "fwd_us": fw, "bwd_us": bw,
+            "fwd_gbs": 65536 * 128 / (fw * 1e-6) / 1e9,
+            "bwd_gbs": 65536 * 192 / (bw * 1e-6) / 1e9,
+            "config": {"workload": "BASELINE config 3", "note": "8 MB working set: "
+                       "L2-resident, latency/compute-bound (backward replays 20 "
+                       "iterations and reverses them)"}}
+
+
+def config4_rewire(dev, peak, peak_kind):
+    """MHCRewire n=4 around a 4-bit QuantizedLinear 4096 ->
+    4096, 8192 bf16 tokens; mHC kernels timed, the GEMM excluded."""
+    import mhc_b200
+
+    g = torch.Generator().manual_seed(4)
+    ql = mhc_b200.QuantizedLinear.random(4096, 4096, group_size=64, bits=4,
+                                         dtype=torch.bfloat16, generator=g).to(dev)
+    model4 = mhc_b200.MHCRewire(ql, dims=4096, n=4).to(dev)
+    x4 = torch.randn(8192, 4096, device=dev).to(torch.bfloat16).requires_grad_(True)
+    d4 = torch.randn(8192, 4096, device=dev)
+
+    def fb4():
+        x4.grad = None
+        for p_ in model4.parameters():
+            p_.grad = None
+        model4(x4).backward(d4)
+
+    mk4, per4 = _kernel_us_per_step(fb4, dev)
+    step_us = _median_us(fb4, dev, iters=30, warm=3)
+    # algorithmic bytes of the mHC kernels per step (bf16 x / y_inner / dy / d_xpre /
+    # dx, fp32 out / d_out), bytes per element:
+    #   prescale fwd x -> x_pre 2+2; combine fwd x, y -> out 2+2+4;
+    #   backward dy side y, d -> dy 2+4+2; x side x, d, d_xpre -> dx 2+4+2+2
+    elems = 8192 * 4096
+    mbytes = elems * ((2 + 2) + (2 + 2 + 4) + (2 + 4 + 2) + (2 + 4 + 2 + 2))
+    return {"metric": "MHCRewire(QuantizedLinear 4096, n=4) mHC fwd+bwd tokens/s, GEMM "
+                      "excluded (BASELINE config 4)",
+            "value": 8192 / (mk4 * 1e-6), "unit": "tokens/s", "higher_is_better": True,
+            "mhc_kernels_us": mk4, "mhc_kernels": per4,
+            "mhc_algorithmic_bytes": mbytes,
+            "mhc_achieved_gbs": mbytes / (mk4 * 1e-6) / 1e9, "peak": peak,
+            "frac": mbytes / (mk4 * 1e-6) / 1e9 / peak,
+            "whole_step_us_incl_gemm": step_us,
+            "config": {"workload": "8192 bf16 tokens, 4-bit affine QuantizedLinear "
+                                   "(group 64), random codes, fp16-range scales",
+                       "peak_source": f"{peak_kind} hbm_gbs",
+                       "note": "mhc_kernels_us = sum of CUDA-event durations around each "
+                               "mHC C-ABI call (the two Sinkhorn parameter kernels included)"}}
+
+
+def llama_measure(dev, rank, world, steps, warmup):
     """Llama-style mock (32 layers, hidden 4096, SwiGLU
     11008, vocab 32000, bf16 random init), every square projection wrapped
     with MHCRewire n=4; batch 8 x seq 4096 random token ids, sequences
-    sharded over ranks (strong scaling), mHC fine-tuning step."""
-    import datetime
-
+    sharded over ranks (strong scaling), mHC fine-tuning step.  Needs the
+    process group initialised when world > 1."""
     import torch.distributed as dist
 
     sys.path.insert(0, str(ROOT / "mhc-mlx_b200" / "examples"))
@@ -734,19 +795,13 @@ def run_llama(args):
     from mhc_b200 import _kernels
     from mhc_b200.dist import shard_tokens
 
-    rank, local, world = env_rank()
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
     B, S, V = 8, 4096, 32000
     model = llama_mock.build(device=dev)
     g = torch.Generator(device=dev).manual_seed(5)
     tokens = torch.randint(0, V, (B, S), device=dev, generator=g)
     targets = torch.randint(0, V, (B, S), device=dev, generator=g)
     tok, tgt = shard_tokens(tokens, rank, world), shard_tokens(targets, rank, world)
-    steps = max(1, min(args.steps, 5))
-    for _ in range(max(1, min(args.warmup, 2))):
+    for _ in range(warmup):
         llama_mock.train_step(model, tok, tgt, B * S)
     torch.cuda.synchronize(dev)
     if world > 1:
@@ -769,11 +824,9 @@ def run_llama(args):
         lt = loss.clone()
         dist.all_reduce(lt)
         loss = lt
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps({
-            "metric": "Llama-mock mHC fine-tuning step tokens/s (BASELINE config 5)",
+    del model
+    torch.cuda.empty_cache()
+    return {"metric": "Llama-mock mHC fine-tuning step tokens/s (BASELINE config 5)",
             "value": B * S / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
             "data": "synthetic", "loss": float(loss),
@@ -782,7 +835,87 @@ def run_llama(args):
                                    "4096, vocab 32000, bf16; 128 MHCRewire(n=4, C=1024) around "
                                    "wq/wk/wv/wo; batch 8 x seq 4096; wrapped weights frozen",
                        "parallelism": f"sequences sharded over {world} rank(s), one NCCL "
-                                      "all-reduce of the mHC gradients per step"}}), flush=True)
+                                      "all-reduce of the mHC gradients per step"}}
+
+
+def run_configs(args):
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak, peak_kind = load_peaks()
+    out = []
+    w = args.workload
+    if w in ("sweep", "all"):
+        out.append({"metric": "MHCLayer per-call latency, BASELINE config 2 sweep (n=4)",
+                    "unit": "us", "higher_is_better": False, "rows": config2_sweep(dev),
+                    "config": {"workload": "config 2 op sweep", "n": 4,
+                               "note": "median of 200 calls, CUDA events; graph = replay of one "
+                                       "captured fwd+bwd"}})
+        out.append({"metric": "MHCLayer per-call time at the reference's published shapes "
+                              "(n=32, fp32; forward, and forward+backward)",
+                    "unit": "us", "higher_is_better": False, "rows": config2_n32_rows(dev),
+                    "config": {"workload": "BENCHMARKS.csv MHCLayer rows (+ B=256, C=4096)",
+                               "n": 32,
+                               "note": "reference_m4pro_fwd_us: the reference's published Apple "
+                                       "M4 Pro Metal forward timings, other hardware, context "
+                                       "only (it publishes no backward timing)"}})
+    if w in ("sinkhorn", "all"):
+        out.append(config3_sinkhorn(dev))
+    if w in ("rewire", "all"):
+        out.append(config1_quickstart(dev))
+        out.append(config4_rewire(dev, peak, peak_kind))
+    for r in out:
+        print(json.dumps(r), flush=True)
+
+
+def run_llama(args):
+    import datetime
+
+    import torch.distributed as dist
+
+    rank, local, world = env_rank()
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    res = llama_measure(dev, rank, world, max(1, min(args.steps, 5)),
+                        max(1, min(args.warmup, 2)))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+def secondary_configs(dev, rank, world, peak, peak_kind, llama_steps=3):
+    """Compact records of BASELINE configs 1-5 for the default run's JSON
+    line.  Configs 1-4 are single-GPU latency / kernel measurements and run
+    on a 1-GPU job; config 5 (the Llama mock, sequences sharded) runs on
+    every rank of the job."""
+    out = {}
+    if world == 1:
+        c1 = config1_quickstart(dev)
+        out["secondary_config1_quickstart"] = {
+            "graph_us": c1["graph_us"], "eager_us": c1["eager_us"],
+            "workload": c1["config"]["workload"]}
+        rows = config2_sweep(dev, iters=100)
+        out["secondary_config2_sweep"] = {
+            "unit": "us", "rows": [{k: (round(v, 2) if isinstance(v, float) else v)
+                                    for k, v in r.items()} for r in rows],
+            "note": "median per call (CUDA events, 100 calls); fwd_bwd_graph = replay of one "
+                    "captured fwd+bwd"}
+        c3 = config3_sinkhorn(dev)
+        out["secondary_config3_sinkhorn"] = {k: c3[k] for k in
+                                             ("value", "unit", "fwd_us", "bwd_us")}
+        c4 = config4_rewire(dev, peak, peak_kind)
+        out["secondary_config4_rewire_q4"] = {
+            k: c4[k] for k in ("value", "unit", "mhc_kernels_us", "mhc_achieved_gbs", "frac",
+                               "whole_step_us_incl_gemm", "mhc_kernels")}
+        torch.cuda.empty_cache()
+    c5 = llama_measure(dev, rank, world, llama_steps, 1)
+    out["secondary_config5_llama"] = {k: c5[k] for k in
+                                      ("value", "unit", "n_gpus", "ms_per_step",
+                                       "mhc_kernels_ms_per_step_max_rank", "scaling", "loss")}
+    return out
 
 
 def main():

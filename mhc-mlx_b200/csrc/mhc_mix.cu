@@ -605,38 +605,41 @@ k_residual_bwd(const OT* __restrict__ out, const DT* __restrict__ dout,
 //   mode 2 (prescale): dhpre = R
 //   mode 3 (rewire end to end): as mode 1 with dhpre_j += S_j; the rows of
 //                      both passes are summed (header words 0 and 2)
-// The partial rows are summed in 32 interleaved slices per entry (slice r
-// takes rows r, r + 32, ...), then the slices in order: a fixed order for a
-// given row count, with 32x fewer dependent loads per thread (a one-CTA
-// kernel is a latency chain).
+// Thread t sums entry e = t % EW of a block of EW consecutive entries over the
+// interleaved row slice t / EW (slice r takes rows r, r + S, ...; S = 1024 /
+// EW slices), then the slices are added in order: a fixed order for a given
+// row count.  EW is the entry count rounded up to a warp, at most 1024, so a
+// few entries (n = 4: 24) get 32 slices of the rows (a one-CTA kernel is a
+// latency chain: fewer dependent loads per thread) and many entries (n = 32:
+// 1088) take two passes instead of one pass per 32 entries.
 constexpr int kCFinBD = 1024;
-constexpr int kCFinSlices = kCFinBD / 32;
 
 __global__ void __launch_bounds__(kCFinBD)
 k_combine_finalize(const char* __restrict__ ws, int n, const float* __restrict__ M,
                    const float* __restrict__ hpre, const float* __restrict__ hpost, int mode,
                    float* __restrict__ dM, float* __restrict__ dhpre, float* __restrict__ dhpost) {
   __shared__ float sQ[kMaxN * kMaxN + 2 * kMaxN];
-  __shared__ float part[kCFinSlices][32];
+  __shared__ float part[kCFinBD];
   const int* hdr = reinterpret_cast<const int*>(ws);
   const int G = mode == 3 ? hdr[0] + hdr[2] : hdr[0];
   const int P = n * n + 2 * n;
   const int E = mode == 3 ? P : n * n + n;  // entries summed
   const float* wp = reinterpret_cast<const float*>(ws + WsLayout::params_off());
-  const int lane = threadIdx.x & 31, r0 = threadIdx.x >> 5;
-  for (int e0 = 0; e0 < E; e0 += 32) {
-    const int e = e0 + lane;
+  const int EW = min((E + 31) / 32 * 32, kCFinBD);
+  const int S = kCFinBD / EW;
+  const int el = threadIdx.x % EW, r0 = threadIdx.x / EW;
+  for (int e0 = 0; e0 < E; e0 += EW) {
+    const int e = e0 + el;
     float s = 0.f;
-    if (e < E) {
+    if (e < E && r0 < S) {
 #pragma unroll 4
-      for (int g = r0; g < G; g += kCFinSlices) s += wp[(size_t)g * P + e];
+      for (int g = r0; g < G; g += S) s += wp[(size_t)g * P + e];
     }
-    part[r0][lane] = s;
+    part[threadIdx.x] = s;
     __syncthreads();
     if (r0 == 0 && e < E) {
       float t = 0.f;
-#pragma unroll
-      for (int q = 0; q < kCFinSlices; ++q) t += part[q][lane];
+      for (int q = 0; q < S; ++q) t += part[q * EW + el];
       sQ[e] = t;
     }
     __syncthreads();

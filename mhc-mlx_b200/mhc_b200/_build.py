@@ -94,14 +94,29 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = True) ->
     inc = [f"-I{INCLUDE_DIR}", f"-I{SRC_DIR}"]
     bid = source_hash()
 
+    headers = [p for p in _deps() if p.suffix != ".cu"]
+
     def compile_one(src: Path) -> Path:
         obj = OBJ_DIR / (src.stem + ".o")
+        # an object is reused when its source, every header and the flags are
+        # byte-identical to the ones it was compiled from (the build id is
+        # only compiled into mhc_capi.cu, which is rebuilt whenever it changes)
+        h = hashlib.sha256()
+        for q in [src, *headers]:
+            h.update(q.name.encode() + b"\0" + q.read_bytes() + b"\0")
+        h.update(" ".join(NVCC_FLAGS).encode())
+        if src.name == "mhc_capi.cu":
+            h.update(bid.encode())
+        stamp = obj.with_suffix(".o.id")
+        if obj.exists() and stamp.exists() and stamp.read_text().strip() == h.hexdigest():
+            return obj
         cmd = [nvcc, *NVCC_FLAGS, f"-DMHC_BUILD_ID=\"{bid}\"", *inc, "-c", str(src), "-o", str(obj)]
         if verbose:
             print("[mhc_b200 build]", " ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed on {src.name}:\n{r.stdout}\n{r.stderr}")
+        stamp.write_text(h.hexdigest() + "\n")
         return obj
 
     jobs = jobs or min(8, os.cpu_count() or 4)

@@ -167,11 +167,12 @@ def layer_fwd(x, M, hpre, hpost, w, eps: float, out_dtype: torch.dtype) -> torch
     return out
 
 
-def layer_bwd(x, dout, M, hpre, hpost, w, eps: float, raw=None):
+def layer_bwd(x, dout, M, hpre, hpost, w, eps: float, raw=None, out=None):
     """dx plus either (dM, dH_pre_act, dH_post_act, d_w) or, with
     raw = (H_pre_raw, H_post_raw, H_res_raw, tape, iters), the raw-parameter
     gradients (dH_pre_raw, dH_post_raw, dH_res_raw, d_w) from the same
-    finalize launch."""
+    finalize launch.  With raw, `out` may give the four fp32 destination
+    tensors (e.g. views of a flat gradient bucket) that the finalize writes."""
     dev = C.require_cuda(x, dout, M, hpre, hpost, w)
     T, n, Cc = x.shape
     with _on(dev):
@@ -194,9 +195,12 @@ def layer_bwd(x, dout, M, hpre, hpost, w, eps: float, raw=None):
                    C.ptr(dw), None, None, None, None, 0, float(eps), None, None, None, st)
             return dx, dM, dpre, dpost, dw
         pre_raw, post_raw, res_raw, tape, iters = raw
-        gpre = torch.empty(n, dtype=F32, device=dev)
-        gpost = torch.empty(n, dtype=F32, device=dev)
-        gres = torch.empty(n, n, dtype=F32, device=dev)
+        if out is not None:
+            gpre, gpost, gres, dw = out
+        else:
+            gpre = torch.empty(n, dtype=F32, device=dev)
+            gpost = torch.empty(n, dtype=F32, device=dev)
+            gres = torch.empty(n, n, dtype=F32, device=dev)
         args = (C.ptr(ws), n, Cc, None, None, None, C.ptr(dw), C.ptr(_f32(pre_raw)),
                 C.ptr(_f32(post_raw)), C.ptr(_f32(res_raw)), C.ptr(tape), int(iters), float(eps),
                 C.ptr(gpre), C.ptr(gpost), C.ptr(gres), st)

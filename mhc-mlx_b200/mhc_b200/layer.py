@@ -36,23 +36,34 @@ class _LayerFn(torch.autograd.Function):
     """x, raw parameters, rms_weight -> out (fused parameter chain)."""
 
     @staticmethod
-    def forward(ctx, x, H_pre_raw, H_post_raw, H_res_raw, rms_weight, iters, eps, out_dtype):
+    def forward(ctx, x, H_pre_raw, H_post_raw, H_res_raw, rms_weight, iters, eps, out_dtype,
+                bound=None):
         hpre, hpost, M, tape = K.params_fwd(H_pre_raw, H_post_raw, H_res_raw, iters, eps,
                                             want_tape=True)
         out = K.layer_fwd(x, M, hpre, hpost, rms_weight, eps, out_dtype)
         empty = M.new_empty(0)
         ctx.save_for_backward(x, H_pre_raw, H_post_raw, H_res_raw, rms_weight, hpre, hpost, M,
                               tape if tape is not None else empty)
-        ctx.iters, ctx.eps = iters, eps
+        ctx.iters, ctx.eps, ctx.bound = iters, eps, bound
         return out
 
     @staticmethod
     def backward(ctx, dout):
         x, pre, post, res, w, hpre, hpost, M, tape = ctx.saved_tensors
-        dx, gpre, gpost, gres, dw = K.layer_bwd(
-            x, dout, M, hpre, hpost, w, ctx.eps,
-            raw=(pre, post, res, tape if tape.numel() else None, ctx.iters))
-        return dx, gpre, gpost, gres, dw, None, None, None
+        raw = (pre, post, res, tape if tape.numel() else None, ctx.iters)
+        bound = ctx.bound
+        # a gradient bucket (mhc_b200.dist.GradBucket) bound to this layer:
+        # when none of the four parameters holds a gradient yet, the finalize
+        # writes straight into the bucket's views, which become their .grad
+        # (nothing to accumulate into, no copy); otherwise autograd
+        # accumulates the returned gradients as usual
+        if bound is not None and all(p.grad is None for p in bound.params):
+            dx, *_ = K.layer_bwd(x, dout, M, hpre, hpost, w, ctx.eps, raw=raw, out=bound.views)
+            for p, v in zip(bound.params, bound.views):
+                p.grad = v
+            return dx, None, None, None, None, None, None, None, None
+        dx, gpre, gpost, gres, dw = K.layer_bwd(x, dout, M, hpre, hpost, w, ctx.eps, raw=raw)
+        return dx, gpre, gpost, gres, dw, None, None, None, None
 
 
 class _ParamsFn(torch.autograd.Function):
@@ -312,7 +323,8 @@ class MHCLayer(nn.Module):
         if return_dtype is not None and return_dtype == x_expanded.dtype and return_dtype in _HALF:
             out_dtype = return_dtype
         out = _LayerFn.apply(x_expanded, self.H_pre_raw, self.H_post_raw, self.H_res_raw,
-                             self.rms_weight, self.sinkhorn_iters, self.eps, out_dtype)
+                             self.rms_weight, self.sinkhorn_iters, self.eps, out_dtype,
+                             getattr(self, "_grad_binding", None))
         if return_dtype is not None and out.dtype != return_dtype:
             out = out.to(return_dtype)
         return out

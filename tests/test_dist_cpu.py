@@ -92,6 +92,58 @@ def test_sharded_allreduce_matches_full_batch():
             assert torch.allclose(a.double(), b, rtol=1e-5, atol=1e-6)
 
 
+def _worker_bucket(rank, world, port, q):
+    try:
+        _setup(rank, world, port)
+        from mhc_b200 import MHCLayer
+        from mhc_b200.dist import GradBucket, allreduce_grads, mhc_parameters
+
+        torch.manual_seed(rank)
+        model = torch.nn.Sequential(MHCLayer(n=4, C=32), MHCLayer(n=2, C=8))
+        ps = mhc_parameters(model)
+        grads = [torch.randn(p.shape) * (k + 1) for k, p in enumerate(ps)]
+        # reference: the gather/scatter all-reduce
+        for p, g in zip(ps, grads):
+            p.grad = g.clone()
+        allreduce_grads(ps)
+        want = [p.grad.clone() for p in ps]
+        # bucket: gradients arriving as plain tensors, one parameter without a
+        # gradient (zeros), one already holding its bucket view
+        bucket = GradBucket(model)
+        for p, g in zip(ps, grads):
+            p.grad = g.clone()
+        ps[3].grad = None
+        bucket.views[5].copy_(grads[5])
+        ps[5].grad = bucket.views[5]
+        bucket.allreduce()
+        want[3] = torch.zeros_like(want[3])
+        got = [p.grad.clone() for p in ps]
+        views_ok = all(p.grad.data_ptr() == v.data_ptr() for p, v in zip(ps, bucket.views))
+        q.put((rank, views_ok, got, want))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, False, repr(e), None))
+
+
+def test_grad_bucket_allreduce_matches_gather_scatter():
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker_bucket, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, views_ok, got, want in res:
+        assert views_ok, got
+        # parameter 3 has no gradient on either rank in the bucket run: zeros
+        for k, (a, b) in enumerate(zip(got, want)):
+            assert torch.allclose(a, b), k
+
+
 def _worker_dead_peer(rank, world, port, q):
     _setup(rank, world, port, timeout_s=10)
     from mhc_b200.dist import allreduce_grads

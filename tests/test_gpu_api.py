@@ -198,3 +198,42 @@ def test_workspace_too_small_is_reported():
         C.call("mhc_bwd", C.ptr(x), 0, C.ptr(x), 0, C.ptr(torch.eye(4, device=DEV)), C.ptr(h),
                C.ptr(h), C.ptr(torch.ones(64, device=DEV)), C.ptr(torch.empty_like(x)), 0, 8, 4,
                64, 1e-5, C.ptr(ws), 16, C.stream_of(x))
+
+
+def test_grad_bucket_backward_writes_into_the_bucket():
+    """With a GradBucket bound, the layer backward's finalize writes the four
+    parameter gradients into the bucket's views (they become .grad, same
+    values as an unbound layer's), a second backward without zeroing
+    accumulates, and allreduce() on one process leaves them unchanged."""
+    from mhc_b200.dist import GradBucket
+
+    g = torch.Generator().manual_seed(3)
+    n, C, T = 4, 256, 33
+    params = [0.5 * torch.randn(n, generator=g), 0.5 * torch.randn(n, generator=g),
+              torch.randn(n, n, generator=g), 1 + 0.1 * torch.randn(C, generator=g)]
+    x = torch.randn(T, n, C, generator=g).to(DEV)
+    d = torch.randn(T, n, C, generator=g).to(DEV)
+
+    def make():
+        layer = mhc_b200.MHCLayer(n=n, C=C).to(DEV)
+        with torch.no_grad():
+            for p, v in zip(layer.parameters(), params):
+                p.copy_(v)
+        return layer
+
+    plain, bound = make(), make()
+    bucket = GradBucket(bound)
+    plain(x).backward(d)
+    bound(x).backward(d)
+    for p, q, v in zip(plain.parameters(), bound.parameters(), bucket.views):
+        assert q.grad.data_ptr() == v.data_ptr()
+        assert torch.equal(p.grad, q.grad)
+    bound(x).backward(d)  # accumulates into the views
+    for p, q in zip(plain.parameters(), bound.parameters()):
+        assert torch.allclose(q.grad, 2 * p.grad, rtol=1e-6, atol=1e-6)
+    for q in bound.parameters():
+        q.grad = None
+    bound(x).backward(d)
+    bucket.allreduce()
+    for p, q in zip(plain.parameters(), bound.parameters()):
+        assert torch.equal(p.grad, q.grad)

@@ -298,6 +298,9 @@ def test_rewire_backward_runs_no_torch_elementwise_kernel():
     for _ in range(2):
         model(x).backward(d)
     out = model(x)
+    x.grad = None  # no gradient accumulation into an existing .grad in the profiled backward
+    for p_ in model.parameters():
+        p_.grad = None
     torch.cuda.synchronize()
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         out.backward(d)
