@@ -141,6 +141,60 @@ __device__ __forceinline__ void cp_async_wait_group() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(K) : "memory");
 }
 
+// ------------------------------------------------- mbarrier + bulk copies --
+// 1-D bulk copies (cp.async.bulk: the TMA unit without a tensor map) from
+// this GPU's own global memory into the CTA's shared memory, completing on an
+// mbarrier through its transaction count.  Plain loads: no cluster multicast.
+// Both addresses and the size must be multiples of 16 bytes.
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+// Makes the mbarrier initialisation visible to the async proxy.
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// Orders this thread's earlier generic-proxy shared-memory accesses before
+// its later async-proxy (bulk copy) writes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase with parity `parity` to complete: false after
+// `limit` tries (each try may suspend the thread for a short hardware-chosen
+// time), so a copy that never lands cannot hang the kernel.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity,
+                                          unsigned limit = 1u << 22) {
+  for (unsigned k = 0; k < limit; ++k)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
 // ------------------------------------------------ warp-level tensor cores --
 // ldmatrix.x4: lanes 8q..8q+7 give the row addresses (16 bytes each) of 8x8
 // b16 matrix q; r[q] receives this lane's pair of that matrix: row lane/4,
@@ -220,6 +274,29 @@ __device__ __forceinline__ float2 block_sum2(float a, float b, float* red) {
   const int nw = blockDim.x >> 5;
   float sa = 0.f, sb = 0.f;
   for (int w = 0; w < nw; ++w) { sa += red[w]; sb += red[32 + w]; }
+  return make_float2(sa, sb);
+}
+
+// block_sum2 for a block of NW <= 32 warps with fewer instructions: after
+// the barrier each lane reads one warp partial of each sum (zero above NW)
+// and a 32-lane butterfly adds them.  Every lane of every warp ends with the
+// same bits (each butterfly step adds the same two values on both lanes of a
+// pair).  `red` holds 64 floats.
+template <int NW>
+__device__ __forceinline__ float2 block_sum2_bfly(float a, float b, float* red) {
+  static_assert(NW >= 1 && NW <= 32, "at most 32 warps");
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  a = warp_sum(a);
+  b = warp_sum(b);
+  if (lane == 0) { red[warp] = a; red[32 + warp] = b; }
+  __syncthreads();
+  float sa = lane < NW ? red[lane] : 0.f;
+  float sb = lane < NW ? red[32 + lane] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sa += __shfl_xor_sync(0xffffffffu, sa, o);
+    sb += __shfl_xor_sync(0xffffffffu, sb, o);
+  }
   return make_float2(sa, sb);
 }
 

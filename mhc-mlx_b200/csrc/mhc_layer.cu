@@ -463,13 +463,21 @@ k_bwd_fast(const XT* __restrict__ x, const DT* __restrict__ dout, const float* _
 // Full-row backward for 16-bit rows: x, d_out and dx share one 16-bit type T
 // and C = 8 * BD, so thread t owns columns 8t..8t+7 of every stream with no
 // tail.  Same math and partial-row output as k_bwd_fast; the differences:
-//   - NBUF = 2 double-buffers the staging slots: token t + G's x and d_out
-//     rows are requested (cp.async, 16 bytes per thread and row) before token
-//     t is processed.  NBUF = 1 refills the single buffer once the first pass
-//     has read it, as k_bwd_fast does;
+//   - staging: BULK = false copies the next token's x and d_out rows with
+//     per-thread 16-byte cp.async (NBUF = 2 double-buffers the slots: token
+//     t + G is requested before token t is processed; NBUF = 1 refills the
+//     single buffer once the first pass has read it, as k_bwd_fast does).
+//     BULK = true has one thread issue a 1-D bulk copy (cp.async.bulk, the TMA
+//     unit) per stream row into NBUF >= 2 buffers, each completing on its own
+//     mbarrier; a buffer is refilled with token t + NBUF * G right after the
+//     block reduction of token t, when every thread has read it.  The waits
+//     are bounded: a copy that never lands makes the CTA write NaN into its
+//     dx rows and partial rows (so the gradients come out NaN, visibly) and
+//     return;
 //   - y and dyn of the first pass stay in registers for the second; w is
 //     staged once in shared memory and M is kept transposed there, so the
 //     per-token parameter reads are shared-memory vector loads;
+//   - the two per-token block sums take one barrier and a warp butterfly;
 //   - MMA (n = 4): dM = sum d x^T runs on the tensor cores from the staged
 //     rows.  Per warp and 64-column group, ldmatrix gives A = d_out rows
 //     (stream i, 16-column block b) and B = x columns (stream j, block b'),
@@ -481,7 +489,7 @@ k_bwd_fast(const XT* __restrict__ x, const DT* __restrict__ dout, const float* _
 // Dynamic shared layout: w as [2][BD] float4 (thread t's columns 8t..8t+3
 // and 8t+4..8t+7, conflict-free), then [NBUF][x rows N | d_out rows N][SB
 // chunks of 16 bytes].
-template <int N, typename T, int BD, bool MMA, int NBUF>
+template <int N, typename T, int BD, bool MMA, int NBUF, bool BULK = false>
 __global__ void __launch_bounds__(BD, 512 / BD)
 k_bwd_rows(const T* __restrict__ x, const T* __restrict__ dout, const float* __restrict__ Mg,
            const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
@@ -489,18 +497,30 @@ k_bwd_rows(const T* __restrict__ x, const T* __restrict__ dout, const float* __r
            float* __restrict__ ws_p, float* __restrict__ ws_c, int* __restrict__ ws_hdr) {
   static_assert(sizeof(T) == 2, "16-bit rows");
   static_assert(!MMA || N == 4, "the tensor-core dM layout is for n = 4");
-  static_assert(NBUF == 1 || NBUF == 2, "one or two staging buffers");
+  static_assert(BULK ? (NBUF == 2 || NBUF == 3) : (NBUF == 1 || NBUF == 2), "staging buffers");
   constexpr int C = 8 * BD, P = N * N + 2 * N, NW = BD / 32;
   constexpr int SB = BD + (MMA ? 1 : 0);  // chunks per staged stream row
   constexpr int BUF = 2 * N * SB;         // chunks per buffer
   constexpr int64_t RS = (int64_t)N * C;  // elements per token
+  constexpr unsigned kRowBytes = BD * 16, kTokBytes = 2 * N * kRowBytes;
   extern __shared__ uint4 s_dyn[];
   float4* s_w = reinterpret_cast<float4*>(s_dyn);
   uint4* s_stage = s_dyn + 2 * BD;
   __shared__ __align__(16) float sMT[N * N];  // sMT[j * N + i] = M[i][j]
   __shared__ float red[2][64];
   __shared__ float sacc[NW * P];
+  __shared__ __align__(8) uint64_t s_full[BULK ? NBUF : 1];
+  __shared__ int s_abort;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t G = gridDim.x;
+  if constexpr (BULK) {
+    if (tid == 0) {
+#pragma unroll
+      for (int b = 0; b < NBUF; ++b) mbar_init(&s_full[b], 1);
+      s_abort = 0;
+      mbar_init_fence();
+    }
+  }
   for (int e = tid; e < N * N; e += BD) sMT[(e % N) * N + e / N] = Mg[e];
   s_w[tid] = __ldg(reinterpret_cast<const float4*>(w) + 2 * tid);
   s_w[BD + tid] = __ldg(reinterpret_cast<const float4*>(w) + 2 * tid + 1);
@@ -526,6 +546,7 @@ k_bwd_rows(const T* __restrict__ x, const T* __restrict__ dout, const float* __r
 #pragma unroll
   for (int v = 0; v < 8; ++v) aW[v] = 0.f;
 
+  // per-thread cp.async staging of token tp into buffer buf
   auto prefetch = [&](int64_t tp, int buf) {
     uint4* s = s_stage + buf * BUF + tid;
     const T* xs = x + tp * RS + col;
@@ -536,12 +557,34 @@ k_bwd_rows(const T* __restrict__ x, const T* __restrict__ dout, const float* __r
       cp_async16(s + (N + i) * SB, ds + (int64_t)i * C);
     }
   };
-  const int64_t G = gridDim.x;
-  if ((int64_t)blockIdx.x < T_) prefetch(blockIdx.x, 0);
-  cp_async_commit();
+  // one thread: bulk copies of token tp's 2N rows into buffer buf
+  auto issue = [&](int64_t tp, int buf) {
+    uint4* s = s_stage + buf * BUF;
+    mbar_arrive_expect_tx(&s_full[buf], kTokBytes);
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      bulk_g2s(s + i * SB, x + tp * RS + (int64_t)i * C, kRowBytes, &s_full[buf]);
+      bulk_g2s(s + (N + i) * SB, dout + tp * RS + (int64_t)i * C, kRowBytes, &s_full[buf]);
+    }
+  };
+  if constexpr (BULK) {
+    if (tid == 0)
+#pragma unroll
+      for (int k = 0; k < NBUF; ++k)
+        if ((int64_t)blockIdx.x + k * G < T_) issue(blockIdx.x + k * G, k);
+  } else {
+    if ((int64_t)blockIdx.x < T_) prefetch(blockIdx.x, 0);
+    cp_async_commit();
+  }
   int par = 0, buf = 0;
-  for (int64_t t = blockIdx.x; t < T_; t += G) {
-    if constexpr (NBUF == 2) {
+  unsigned use = 0;  // BULK: tokens consumed so far (buffer use = use / NBUF)
+  bool aborted = false;
+  int64_t t = blockIdx.x;
+  for (; t < T_; t += G) {
+    if constexpr (BULK) {
+      buf = (int)(use % NBUF);
+      if (!mbar_wait(&s_full[buf], (use / NBUF) & 1u)) s_abort = 1;
+    } else if constexpr (NBUF == 2) {
       // the other buffer was last read before the previous token's barrier
       if (t + G < T_) prefetch(t + G, buf ^ 1);
       cp_async_commit();
@@ -572,12 +615,14 @@ k_bwd_rows(const T* __restrict__ x, const T* __restrict__ dout, const float* __r
       unpack16<T, 8>(sb[i * SB + tid], xr[i]);
       unpack16<T, 8>(sb[(N + i) * SB + tid], dr[i]);
     }
-    if constexpr (NBUF == 1) {
-      if constexpr (MMA) __syncwarp();  // the warp's ldmatrix reads precede the refill
-      if (t + G < T_) prefetch(t + G, 0);
-      cp_async_commit();
-    } else {
-      buf ^= 1;
+    if constexpr (!BULK) {
+      if constexpr (NBUF == 1) {
+        if constexpr (MMA) __syncwarp();  // the warp's ldmatrix reads precede the refill
+        if (t + G < T_) prefetch(t + G, 0);
+        cp_async_commit();
+      } else {
+        buf ^= 1;
+      }
     }
     float yk[8], dk[8], ss = 0.f, pd = 0.f;
     {
@@ -597,8 +642,18 @@ k_bwd_rows(const T* __restrict__ x, const T* __restrict__ dout, const float* __r
         pd = fmaf(dyn * wv[v], y, pd);
       }
     }
-    const float2 red2 = block_sum2(ss, pd, red[par]);
+    const float2 red2 = block_sum2_bfly<NW>(ss, pd, red[par]);
     par ^= 1;
+    if constexpr (BULK) {
+      // after the barrier: every thread has read buffer `buf` (the MMA's
+      // ldmatrix and the unpack precede it), and s_abort is the same for all
+      if (s_abort) { aborted = true; break; }
+      if (tid == 0 && t + NBUF * G < T_) {
+        fence_proxy_async_smem();
+        issue(t + NBUF * G, buf);
+      }
+      ++use;
+    }
     const float inv = inv_rms(red2.x, C, eps);
     const float k2 = (red2.y * (inv * inv * inv)) * (1.0f / (float)C);
 
@@ -640,7 +695,30 @@ k_bwd_rows(const T* __restrict__ x, const T* __restrict__ dout, const float* __r
       store_vec<T, 8>(dxt + (int64_t)j * C, o);
     }
   }
-  cp_async_wait_all();  // only empty groups can remain; nothing is left in flight at exit
+  if constexpr (BULK) {
+    if (aborted) {
+      // a bulk copy did not land in time: wait (bounded) for the copies this
+      // CTA still has in flight, then mark everything it owns as invalid
+      if (tid == 0) {
+        for (unsigned k = use; k < use + NBUF; ++k)
+          if ((int64_t)blockIdx.x + (int64_t)k * G < T_)
+            (void)mbar_wait(&s_full[k % NBUF], (k / NBUF) & 1u);
+      }
+      const float nan = __int_as_float(0x7fc00000);
+      float o[8];
+#pragma unroll
+      for (int v = 0; v < 8; ++v) { o[v] = nan; aW[v] = nan; }
+      for (; t < T_; t += G)
+#pragma unroll
+        for (int j = 0; j < N; ++j) store_vec<T, 8>(dx + t * RS + col + (int64_t)j * C, o);
+#pragma unroll
+      for (int i = 0; i < N; ++i) { aPre[i] = nan; aPost[i] = nan; }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) { accA[e] = nan; accB[e] = nan; }
+    }
+  } else {
+    cp_async_wait_all();  // only empty groups can remain; nothing is left in flight at exit
+  }
 
   // ---- per-CTA partials: fixed-order warp reductions + ordered warp sum ----
   if constexpr (MMA) {
@@ -1558,6 +1636,14 @@ static int launch_bwd_rows(const T* x, const T* d, const float* M, const float* 
   if constexpr (kMma) {
     if (env_int("MHC_B200_MMA", 1)) {
       const size_t rows = (size_t)2 * N * (BD + 1) * row;
+      // bulk-copy staging, three buffers by default (MHC_B200_BULK = 0
+      // selects the per-thread cp.async staging, 2 or 3 the number of
+      // bulk-copy buffers).  B200, n = 4, C = 4096, T = 65536 bf16:
+      // cp.async 1132-1288 us, 2 buffers 1017 us, 3 buffers 990 us.
+      const int bulk = env_int("MHC_B200_BULK", 3);
+      if (bulk == 3 && wb + 3 * rows + 4096 <= (size_t)max_smem_optin())
+        return go(k_bwd_rows<N, T, BD, true, 3, true>, wb + 3 * rows);
+      if (bulk >= 2) return go(k_bwd_rows<N, T, BD, true, 2, true>, wb + 2 * rows);
       if (two) return go(k_bwd_rows<N, T, BD, true, 2>, wb + 2 * rows);
       return go(k_bwd_rows<N, T, BD, true, 1>, wb + rows);
     }
