@@ -265,6 +265,32 @@ MHC_API int mhc_residual_add_agg_bwd(const void* out, int out_dtype, const void*
                                      int C, void* workspace, size_t workspace_bytes,
                                      void* stream);
 
+/* ---- quantized linear layer (the module MHCRewire wraps) -------------------
+ * The 4-bit affine group-wise QuantizedLinear that the reference wraps
+ * (tests/test_quantized.py:15 QuantizedLinear.from_linear(..., group_size=64,
+ * bits=4), examples/patch_llama_mock.py:90, patching.py:74-80), with the
+ * weight dequantised tile by tile inside a tensor-core GEMM (the [out, in]
+ * weight is never written to memory):
+ *   W[n, k] = scales[n, k/64] * q[n, k] + biases[n, k/64],  q in [0, 15]
+ * w_packed is [N][K/8] 32-bit words, code k%8 of row n in bits [4(k%8), 4(k%8)+4)
+ * of word k/8; scales / biases are [N][K/64] in scales_dtype (MHC_BF16 or
+ * MHC_F16).  The dequantisation rounds q * scale and then + bias to that
+ * dtype, then the value to the activations' dtype.
+ *   mhc_qlinear_fwd:    y[M, N]  = x[M, K] W^T (+ bias[N], x's dtype, may be NULL)
+ *   mhc_qlinear_bwd_dx: dx[M, K] = dy[M, N] W
+ * x / dy / y / dx are row-contiguous bf16 or fp16 (one dtype per call);
+ * fp32 accumulation.  Covered: bits = 4, group_size = 64, N and K multiples
+ * of 128, 16-byte aligned x / dy, w_packed and outputs (MHC_ERR_UNSUPPORTED
+ * or MHC_ERR_INVALID otherwise). */
+MHC_API int mhc_qlinear_fwd(const void* x, int x_dtype, const uint32_t* w_packed,
+                            const void* scales, const void* biases, int scales_dtype,
+                            const void* bias, void* y, int64_t M, int N, int K,
+                            int group_size, int bits, void* stream);
+MHC_API int mhc_qlinear_bwd_dx(const void* dy, int dy_dtype, const uint32_t* w_packed,
+                               const void* scales, const void* biases, int scales_dtype,
+                               void* dx, int64_t M, int N, int K, int group_size, int bits,
+                               void* stream);
+
 #ifdef __cplusplus
 }
 #endif

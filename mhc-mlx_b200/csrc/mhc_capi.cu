@@ -406,6 +406,24 @@ int mhc_prescale_bwd(const void* x, int x_dtype, const void* d_xpre, int d_dtype
   MHC_TRY_END
 }
 
+int mhc_qlinear_fwd(const void* x, int x_dtype, const uint32_t* w_packed, const void* scales,
+                    const void* biases, int scales_dtype, const void* bias, void* y, int64_t M,
+                    int N, int K, int group_size, int bits, void* stream) {
+  MHC_TRY_BEGIN
+  return launch_qlinear_fwd(x, x_dtype, w_packed, scales, biases, scales_dtype, bias, y, M, N, K,
+                            group_size, bits, as_stream(stream));
+  MHC_TRY_END
+}
+
+int mhc_qlinear_bwd_dx(const void* dy, int dy_dtype, const uint32_t* w_packed,
+                       const void* scales, const void* biases, int scales_dtype, void* dx,
+                       int64_t M, int N, int K, int group_size, int bits, void* stream) {
+  MHC_TRY_BEGIN
+  return launch_qlinear_bwd_dx(dy, dy_dtype, w_packed, scales, biases, scales_dtype, dx, M, N, K,
+                               group_size, bits, as_stream(stream));
+  MHC_TRY_END
+}
+
 int mhc_residual_add_agg(const void* x, int x_dtype, const void* res, int res_dtype,
                          const float* H_pre, void* out, int out_dtype, float* y_agg, int64_t T,
                          int n, int C, void* stream) {

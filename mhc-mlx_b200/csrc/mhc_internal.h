@@ -127,4 +127,12 @@ int launch_residual_add_agg_bwd(const void* out, int odt, const void* dout, int 
                                 float* dhpre, int64_t T, int n, int C, void* ws, size_t ws_bytes,
                                 cudaStream_t st);
 
+// ---- quantized linear (mhc_qmm.cu) ------------------------------------------
+int launch_qlinear_fwd(const void* x, int xdt, const uint32_t* wq, const void* scales,
+                       const void* biases, int sdt, const void* bias, void* y, int64_t M, int N,
+                       int K, int group_size, int bits, cudaStream_t st);
+int launch_qlinear_bwd_dx(const void* dy, int dydt, const uint32_t* wq, const void* scales,
+                          const void* biases, int sdt, void* dx, int64_t M, int N, int K,
+                          int group_size, int bits, cudaStream_t st);
+
 }  // namespace mhc

@@ -60,6 +60,10 @@ SIGNATURES: dict[str, tuple] = {
     "mhc_prescale_fwd": (c_int, [_P, c_int, _P, _P, c_int, c_int64, c_int, c_int, _P]),
     "mhc_prescale_bwd": (c_int, [_P, c_int, _P, c_int, _P, _P, c_int, _P, c_int64, c_int, c_int, _P,
                                  c_size_t, _P]),
+    "mhc_qlinear_fwd": (c_int, [_P, c_int, _P, _P, _P, c_int, _P, _P, c_int64, c_int, c_int, c_int,
+                                c_int, _P]),
+    "mhc_qlinear_bwd_dx": (c_int, [_P, c_int, _P, _P, _P, c_int, _P, c_int64, c_int, c_int, c_int,
+                                   c_int, _P]),
     "mhc_residual_add_agg": (c_int, [_P, c_int, _P, c_int, _P, _P, c_int, _P, c_int64, c_int, c_int,
                                      _P]),
     "mhc_residual_add_agg_bwd": (c_int, [_P, c_int, _P, c_int, _P, _P, _P, c_int, _P, c_int64,

@@ -373,3 +373,34 @@ def residual_add_agg_bwd(out, d_out, d_y, hpre, dx_dtype):
               C.dtype_code(oc.dtype), C.ptr(yc), C.ptr(_f32(hpre)), C.ptr(dx),
               C.dtype_code(dx_dtype), C.ptr(dpre), T, n, Cc, C.ptr(ws), nb, C.stream_of(oc))
     return dx, dpre
+
+
+# ------------------------------------------------------- quantized linear --
+def qlinear_fwd(x2, w_packed, scales, biases, bias, group_size: int, bits: int):
+    """y[M, N] = x2[M, K] W^T (+ bias) with the 4-bit weight dequantised inside
+    the GEMM (mhc_qlinear_fwd)."""
+    dev = C.require_cuda(x2, w_packed, scales, biases)
+    M, Kd = x2.shape
+    N = w_packed.shape[0]
+    with _on(dev):
+        xc = _c(x2)
+        b = None if bias is None else _c(bias.to(xc.dtype))
+        y = torch.empty(M, N, dtype=xc.dtype, device=dev)
+        _call("mhc_qlinear_fwd", xc, C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(_c(w_packed)),
+              C.ptr(_c(scales)), C.ptr(_c(biases)), C.dtype_code(scales.dtype), C.ptr(b),
+              C.ptr(y), M, N, Kd, int(group_size), int(bits), C.stream_of(xc))
+    return y
+
+
+def qlinear_bwd_dx(dy2, w_packed, scales, biases, in_dims: int, group_size: int, bits: int):
+    """dx[M, K] = dy2[M, N] W with the weight dequantised inside the GEMM
+    (mhc_qlinear_bwd_dx)."""
+    dev = C.require_cuda(dy2, w_packed, scales, biases)
+    M, N = dy2.shape
+    with _on(dev):
+        dc = _c(dy2)
+        dx = torch.empty(M, in_dims, dtype=dc.dtype, device=dev)
+        _call("mhc_qlinear_bwd_dx", dc, C.ptr(dc), C.dtype_code(dc.dtype), C.ptr(_c(w_packed)),
+              C.ptr(_c(scales)), C.ptr(_c(biases)), C.dtype_code(scales.dtype), C.ptr(dx), M, N,
+              in_dims, int(group_size), int(bits), C.stream_of(dc))
+    return dx

@@ -9,8 +9,13 @@ scale = (max - min) / (2^bits - 1), bias = min.  Codes are packed
 little-endian into uint32 words (32 // bits codes per word); scales and
 biases are stored in the weight's float dtype.
 
-The forward dequantises the weight and runs one plain GEMM (torch.matmul):
-the wrapped layer is outside the mHC hot path.  Its weights are buffers, so
+On CUDA with bf16 / fp16 activations, 4-bit codes and groups of 64 (the
+configuration the reference uses), forward and input-gradient are one
+tensor-core GEMM each with the weight dequantised tile by tile inside the
+kernel (mhc_qlinear_fwd / mhc_qlinear_bwd_dx): the [out, in] weight is never
+materialised.  Other configurations (2 / 8 bits, other group sizes, fp32 or
+CPU activations) dequantise with torch ops and run torch.matmul; the wrapped
+layer is outside the mHC hot path either way.  Its weights are buffers, so
 the layer is frozen by construction; ``freeze()`` exists for API parity.
 """
 
@@ -18,6 +23,33 @@ from __future__ import annotations
 
 import torch
 from torch import nn
+
+from . import _kernels as K
+
+
+class _QLinearFn(torch.autograd.Function):
+    """y = x W^T (+ bias) with W dequantised inside the GEMM; the backward
+    gives the input gradient only (codes, scales and biases are frozen)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, scales, biases, bias, group_size, bits):
+        shape = x.shape
+        y = K.qlinear_fwd(x.reshape(-1, shape[-1]), weight, scales, biases, bias, group_size,
+                          bits)
+        ctx.save_for_backward(weight, scales, biases)
+        ctx.meta = (shape, x.dtype, group_size, bits)
+        return y.reshape(*shape[:-1], y.shape[-1])
+
+    @staticmethod
+    def backward(ctx, dy):
+        weight, scales, biases = ctx.saved_tensors
+        shape, dtype, group_size, bits = ctx.meta
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dy2 = dy.reshape(-1, dy.shape[-1]).to(dtype)
+            dx = K.qlinear_bwd_dx(dy2, weight, scales, biases, shape[-1], group_size, bits)
+            dx = dx.reshape(shape)
+        return dx, None, None, None, None, None, None
 
 
 class QuantizedLinear(nn.Module):
@@ -109,7 +141,16 @@ class QuantizedLinear(nn.Module):
         """No trainable parameters: codes, scales and biases are buffers."""
         return self
 
+    def _in_kernel(self, x: torch.Tensor) -> bool:
+        return (x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and self.bits == 4
+                and self.group_size == 64 and self.input_dims % 128 == 0
+                and self.output_dims % 128 == 0
+                and self.scales.dtype in (torch.bfloat16, torch.float16))
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self._in_kernel(x):
+            return _QLinearFn.apply(x, self.weight, self.scales, self.biases, self.bias,
+                                    self.group_size, self.bits)
         w = self.dequantize(dtype=x.dtype)
         y = torch.matmul(x, w.t())
         if self.bias is not None:

@@ -208,6 +208,72 @@ def test_rewire_quantized_inner_bf16():
     assert len([p for p in model.parameters() if p.requires_grad]) == 4
 
 
+# --------------------------------------------- quantized linear (in-kernel) --
+def _random_qlinear(in_d, out_d, sdt, seed, bias=False):
+    g = torch.Generator().manual_seed(seed)
+    ql = mhc_b200.QuantizedLinear.random(in_d, out_d, group_size=64, bits=4, dtype=sdt,
+                                         generator=g)
+    if bias:
+        ql.bias = (0.1 * torch.randn(out_d, generator=g)).to(sdt)
+    return ql.to(DEV)
+
+
+@pytest.mark.parametrize("M,N,Kd,xdt,sdt", [
+    (8192, 4096, 4096, torch.bfloat16, torch.float16),   # BASELINE config 4, full rows
+    (300, 4096, 4096, torch.bfloat16, torch.bfloat16),   # ragged rows, bf16 scales
+    (1, 384, 1024, torch.float16, torch.float16),        # one row, 128-wide tiles
+    (129, 1024, 2048, torch.bfloat16, torch.float16)])
+def test_qlinear_kernels_match_dequantized_gemm(M, N, Kd, xdt, sdt):
+    """mhc_qlinear_fwd / mhc_qlinear_bwd_dx (weight dequantised inside the
+    tensor-core GEMM) against dequantize() + a float64 matmul; the outputs
+    are rounded once to x's dtype (2e-2 is the bf16 tolerance of the other
+    tests; the observed error is one rounding)."""
+    from mhc_b200 import _kernels as K
+
+    ql = _random_qlinear(Kd, N, sdt, M + N + Kd)
+    g = torch.Generator().manual_seed(M)
+    x = torch.randn(M, Kd, generator=g).to(xdt).to(DEV)
+    dy = torch.randn(M, N, generator=g).to(xdt).to(DEV)
+    W = ql.dequantize(xdt).double()
+    y = K.qlinear_fwd(x, ql.weight, ql.scales, ql.biases, None, 64, 4)
+    dx = K.qlinear_bwd_dx(dy, ql.weight, ql.scales, ql.biases, Kd, 64, 4)
+    assert y.dtype == xdt and dx.dtype == xdt
+    y_ref = x.double() @ W.T
+    dx_ref = dy.double() @ W
+    tol = 1e-2 if xdt == torch.bfloat16 else 2e-3
+    assert rel_err(y, y_ref) < tol, rel_err(y, y_ref)
+    assert rel_err(dx, dx_ref) < tol, rel_err(dx, dx_ref)
+    # and against torch's own GEMM on the materialised weight
+    Wt = ql.dequantize(xdt)
+    assert rel_err(y, (x @ Wt.T).double()) < tol
+    assert rel_err(dx, (dy @ Wt).double()) < tol
+
+
+def test_qlinear_module_allocates_no_weight_and_matches_torch_path():
+    """QuantizedLinear.forward on CUDA bf16 runs the in-kernel dequantisation:
+    no [out, in] weight is allocated (peak memory grows by far less than one
+    bf16 copy of it), output and input gradient match the torch
+    dequantise-and-matmul path, including a bias."""
+    out_d, in_d, M = 4096, 4096, 64
+    ql = _random_qlinear(in_d, out_d, torch.float16, 7, bias=True)
+    x = torch.randn(M, in_d, device=DEV).to(torch.bfloat16).requires_grad_(True)
+    assert ql._in_kernel(x)
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    base = torch.cuda.memory_allocated()
+    y = ql(x)
+    y.backward(torch.ones_like(y))
+    torch.cuda.synchronize()
+    grown = torch.cuda.max_memory_allocated() - base
+    assert grown < out_d * in_d * 2 // 4, grown  # a bf16 weight copy would be 32 MiB
+    W = ql.dequantize(torch.bfloat16)
+    xr = x.detach().clone().requires_grad_(True)
+    yr = xr @ W.T + ql.bias.to(torch.bfloat16)
+    yr.backward(torch.ones_like(yr))
+    assert rel_err(y, yr) < 1e-2
+    assert rel_err(x.grad, xr.grad) < 1e-2
+
+
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
 def test_rewire_combine_kernel_matches_oracle(dt):
     g = torch.Generator().manual_seed(21)
