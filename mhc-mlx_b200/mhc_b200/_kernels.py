@@ -379,7 +379,7 @@ def residual_add_agg_bwd(out, d_out, d_y, hpre, dx_dtype):
 def qlinear_fwd(x2, w_packed, scales, biases, bias, group_size: int, bits: int):
     """y[M, N] = x2[M, K] W^T (+ bias) with the 4-bit weight dequantised inside
     the GEMM (mhc_qlinear_fwd)."""
-    dev = C.require_cuda(x2, w_packed, scales, biases)
+    dev = C.require_cuda(x2, w_packed, scales, biases, bias)
     M, Kd = x2.shape
     N = w_packed.shape[0]
     with _on(dev):

@@ -213,9 +213,10 @@ def _random_qlinear(in_d, out_d, sdt, seed, bias=False):
     g = torch.Generator().manual_seed(seed)
     ql = mhc_b200.QuantizedLinear.random(in_d, out_d, group_size=64, bits=4, dtype=sdt,
                                          generator=g)
-    if bias:
-        ql.bias = (0.1 * torch.randn(out_d, generator=g)).to(sdt)
-    return ql.to(DEV)
+    ql = ql.to(DEV)
+    if bias:  # random() makes no bias buffer: attach one on the device
+        ql.bias = (0.1 * torch.randn(out_d, generator=g)).to(DEV, sdt)
+    return ql
 
 
 @pytest.mark.parametrize("M,N,Kd,xdt,sdt", [

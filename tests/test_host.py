@@ -242,3 +242,31 @@ def test_llama_mock_patch_structure():
     trainable = [n for n, p in model.named_parameters() if p.requires_grad]
     assert trainable and all(".mhc." in n for n in trainable)
     assert not isinstance(model.layers[0].feed_forward.w1, MHCRewire)
+
+
+def test_qlinear_validation_without_gpu():
+    """The in-kernel-dequantisation GEMM checks its arguments before any CUDA
+    call: unsupported bit widths / group sizes / shapes are reported, not run."""
+    with pytest.raises(_capi.MHCError, match="bits=4, group_size=64"):
+        _capi.call("mhc_qlinear_fwd", None, _capi.MHC_BF16, None, None, None, _capi.MHC_F16, None,
+                   None, 8, 256, 256, 64, 8, None)
+    with pytest.raises(_capi.MHCError, match="multiples of 128"):
+        _capi.call("mhc_qlinear_bwd_dx", None, _capi.MHC_BF16, None, None, None, _capi.MHC_F16,
+                   None, 8, 256, 192, 64, 4, None)
+    with pytest.raises(_capi.MHCError, match="bf16 or fp16"):
+        _capi.call("mhc_qlinear_fwd", None, _capi.MHC_F32, None, None, None, _capi.MHC_F16, None,
+                   None, 8, 256, 256, 64, 4, None)
+    # M = 0 is a no-op
+    _capi.call("mhc_qlinear_fwd", None, _capi.MHC_BF16, None, None, None, _capi.MHC_F16, None,
+               None, 0, 256, 256, 64, 4, None)
+
+
+def test_qlinear_kernel_selection():
+    """CUDA bf16/fp16 activations with 4-bit codes in groups of 64 take the
+    in-kernel path; other configurations dequantise with torch."""
+    q = QuantizedLinear(256, 256, bits=4, group_size=64)
+    x16 = torch.zeros(2, 256, dtype=torch.bfloat16)
+    assert not q._in_kernel(x16)  # CPU tensor
+    assert not QuantizedLinear(256, 256, bits=8, group_size=64)._in_kernel(x16)
+    y = q(x16)  # torch path on the CPU
+    assert y.shape == (2, 256)
