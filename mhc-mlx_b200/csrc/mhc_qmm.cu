@@ -9,17 +9,17 @@
 //   forward:   y[m, n] = sum_k x[m, k] W[n, k]  (+ bias[n])
 //   backward:  dx[m, k] = sum_n dy[m, n] W[n, k]
 // q is packed eight to a 32-bit word, code j of a word in bits [4j, 4j + 4)
-// (word w of row n holds k = 8w .. 8w + 7).  The dequantisation rounds like
-// the reference's dequantize-then-matmul in the scales' dtype: q * scale is
-// rounded to that dtype, then + bias is rounded, then the value is rounded to
-// the activations' dtype (bf16 or fp16) for the product.
+// (word w of row n holds k = 8w .. 8w + 7).  Each weight is q * scale + bias
+// computed with one fused multiply-add in the scales' dtype (one rounding),
+// then rounded to the activations' dtype (bf16 or fp16) for the product;
+// products are accumulated in fp32.
 //
 // One CTA computes a 128 x BN output tile (BN = 256 or 128) with
 // tcgen05.mma (kind::f16, fp32 accumulators in tensor memory), looping over
 // the reduction in slices of 64:
 //   warp 0      one thread issues TMA loads of the activation slice (128 x 64,
 //               128-byte swizzled) and of the slice's packed words into a
-//               three-stage ring;
+//               three- or four-stage ring;
 //   warp 1      allocates the accumulator columns in tensor memory; one
 //               thread issues four 128 x BN x 16 MMAs per slice and commits
 //               them to the slice's "empty" barrier;
@@ -41,7 +41,7 @@
 namespace mhc {
 namespace {
 
-constexpr int kBM = 128, kBK = 64, kStages = 3, kGroup = 64;
+constexpr int kBM = 128, kBK = 64, kGroup = 64;
 constexpr int kThreads = 320, kDqThreads = 256;
 constexpr unsigned kWaitLimit = 1u << 22;
 
@@ -152,7 +152,9 @@ __device__ __forceinline__ P of_bits(uint32_t u) {
   return *reinterpret_cast<P*>(&u);
 }
 
-// Eight codes of one word -> eight XT values (one 16-byte chunk, in k order).
+// Eight codes of one word -> eight XT values (one 16-byte chunk, in k order):
+// q * scale + bias as one fused multiply-add in the scales' dtype (one
+// rounding), then converted to the operand dtype when it differs.
 template <typename XT, typename ST>
 __device__ __forceinline__ uint4 dequant8(uint32_t w, typename Pair<ST>::P s2,
                                           typename Pair<ST>::P b2) {
@@ -166,8 +168,7 @@ __device__ __forceinline__ uint4 dequant8(uint32_t w, typename Pair<ST>::P s2,
     uint32_t m;
     asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(m) : "r"(t), "r"(0x000F000Fu), "r"(Pair<ST>::kMagic));
     PS v = __hsub2(of_bits<PS>(m), Pair<ST>::offset());  // exact codes
-    v = __hmul2(v, s2);                                    // rounded like q * scale
-    v = __hadd2(v, b2);                                    // rounded like + bias
+    v = __hfma2(v, s2, b2);
     if constexpr (std::is_same<XT, ST>::value) {
       o[p] = bits_of(v);
     } else {
@@ -183,6 +184,8 @@ struct Layout {
   static constexpr int kB = BN * kBK * 2;                      // BN x 64 16-bit values
   static constexpr int kW = BWD ? (kBK * BN / 2) : (BN * 32);  // packed words of the slice
   static constexpr int kStage = kA + kB + kW;
+  // four stages where they fit next to the static shared memory, else three
+  static constexpr int kStages = (4 * kStage + 1024 <= 226 * 1024) ? 4 : 3;
   static constexpr int kBytes = kStages * kStage + 1024;       // + alignment slack
 };
 
@@ -193,6 +196,7 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
           const XT* __restrict__ bias, XT* __restrict__ out, int M, int N, int K) {
   using L = Layout<BN, BWD>;
   using PS = typename Pair<ST>::P;
+  constexpr int kStages = L::kStages;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t a_full[kStages], b_full[kStages], empty[kStages], acc_full;
   __shared__ uint32_t s_tmem;
@@ -306,43 +310,64 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
       j0 = (dq / BN) * WPT;
     }
     const int wofs = BWD ? r * (BN / 2) + (dq & 3) * WPT * 4 : r * 32 + j0 * 4;
-    for (int it = 0; it < KT; ++it) {
-      const int s = it % kStages;
-      const unsigned ph = (unsigned)(it / kStages) & 1u;
-      // this slice's scale / bias (requested before the wait)
+    // scale / bias of slice it: requested kPre slices ahead into a register
+    // ring (the inner loop is unrolled, so the ring index is a constant)
+    constexpr int kPre = 4;
+    auto sb_index = [&](int it) -> size_t {
       const int row = BWD ? it * kBK + r : n0 + r;   // weight row n
       const int grp = BWD ? n0 / kGroup + blk : it;  // its group of 64 columns
-      const ST sv = scales[(size_t)row * G + grp];
-      const ST bv = biases[(size_t)row * G + grp];
-      if (!wait_or_abort(&a_full[s], ph, abort_flag)) { s_abort = 1; break; }
-      uint32_t wd[WPT];
+      return (size_t)row * G + grp;
+    };
+    ST sv[kPre], bv[kPre];
 #pragma unroll
-      for (int q = 0; q < WPT; q += 4) {
-        const uint4 w = *reinterpret_cast<const uint4*>(sW(s) + wofs + 4 * q);
-        wd[q] = w.x; wd[q + 1] = w.y; wd[q + 2] = w.z; wd[q + 3] = w.w;
-      }
-      const PS s2 = Pair<ST>::dup(sv), b2 = Pair<ST>::dup(bv);
-      uint8_t* bt = sB(s);
+    for (int u = 0; u < kPre; ++u) {
+      const size_t i = sb_index(u < KT ? u : 0);
+      sv[u] = scales[i];
+      bv[u] = biases[i];
+    }
+    bool stop = false;
+    for (int it0 = 0; it0 < KT && !stop; it0 += kPre) {
 #pragma unroll
-      for (int q = 0; q < WPT; ++q) {
-        const uint4 v = dequant8<XT, ST>(wd[q], s2, b2);
-        const int j = j0 + q;  // 16-byte chunk within the row's 128 bytes
-        uint32_t off;
-        if constexpr (BWD) {
-          // [k-group][64-column block][8 rows][128 bytes], chunks swizzled by row
-          off = (uint32_t)((r >> 3) * (BN / 64) * 1024 + blk * 1024 + (r & 7) * 128 +
-                           ((j ^ (r & 7)) << 4));
-        } else {
-          // [8-row group][8 rows][128 bytes], chunks swizzled by row
-          off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4));
+      for (int u = 0; u < kPre; ++u) {
+        const int it = it0 + u;
+        if (it >= KT) break;
+        const int s = it % kStages;
+        const unsigned ph = (unsigned)(it / kStages) & 1u;
+        const PS s2 = Pair<ST>::dup(sv[u]), b2 = Pair<ST>::dup(bv[u]);
+        if (it + kPre < KT) {
+          const size_t i = sb_index(it + kPre);
+          sv[u] = scales[i];
+          bv[u] = biases[i];
         }
-        *reinterpret_cast<uint4*>(bt + off) = v;
+        if (!wait_or_abort(&a_full[s], ph, abort_flag)) { s_abort = 1; stop = true; break; }
+        uint32_t wd[WPT];
+#pragma unroll
+        for (int q = 0; q < WPT; q += 4) {
+          const uint4 w = *reinterpret_cast<const uint4*>(sW(s) + wofs + 4 * q);
+          wd[q] = w.x; wd[q + 1] = w.y; wd[q + 2] = w.z; wd[q + 3] = w.w;
+        }
+        uint8_t* bt = sB(s);
+#pragma unroll
+        for (int q = 0; q < WPT; ++q) {
+          const uint4 v = dequant8<XT, ST>(wd[q], s2, b2);
+          const int j = j0 + q;  // 16-byte chunk within the row's 128 bytes
+          uint32_t off;
+          if constexpr (BWD) {
+            // [k-group][64-column block][8 rows][128 bytes], chunks swizzled by row
+            off = (uint32_t)((r >> 3) * (BN / 64) * 1024 + blk * 1024 + (r & 7) * 128 +
+                             ((j ^ (r & 7)) << 4));
+          } else {
+            // [8-row group][8 rows][128 bytes], chunks swizzled by row
+            off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4));
+          }
+          *reinterpret_cast<uint4*>(bt + off) = v;
+        }
+        fence_proxy_async_smem();  // the MMA reads these through the async proxy
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(
+                                        smem_u32(&b_full[s]))
+                                    : "memory");
       }
-      fence_proxy_async_smem();  // the MMA reads these through the async proxy
-      __syncwarp();
-      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(
-                                      smem_u32(&b_full[s]))
-                                  : "memory");
     }
     // ---------------------------------------------------------- epilogue --
     const bool ok = wait_or_abort(&acc_full, 0u, abort_flag) && !*abort_flag;
