@@ -19,13 +19,14 @@
 // the reduction in slices of 64:
 //   warp 0      one thread issues TMA loads of the activation slice (128 x 64,
 //               128-byte swizzled) and of the slice's packed words into a
-//               three- or four-stage ring;
+//               five- or six-stage ring;
 //   warp 1      allocates the accumulator columns in tensor memory; one
 //               thread issues four 128 x BN x 16 MMAs per slice and commits
 //               them to the slice's "empty" barrier;
 //   warps 2-9   dequantise the slice's words into the B operand's 128-byte
-//               swizzled layout in shared memory (K-major for the forward,
-//               MN-major for the backward), then read the accumulators back
+//               swizzled layout in a three- or four-stage ring in shared
+//               memory (K-major for the forward, MN-major for the backward),
+//               then read the accumulators back
 //               (tcgen05.ld) and write the output tile.
 // Every wait is bounded: a barrier that never completes makes the CTA write
 // NaN into its output tile and return (after waiting, again bounded, for its
@@ -178,15 +179,21 @@ __device__ __forceinline__ uint4 dequant8(uint32_t w, typename Pair<ST>::P s2,
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// Two rings in shared memory: SA stages of (activation slice, packed words
+// of the slice), filled by TMA and released when the slice's MMAs complete,
+// and SB stages of the dequantised B slice, filled by the dequantising warps
+// and released the same way.  The activation ring is the deeper one, so the
+// TMA runs several slices ahead of the tensor cores.
 template <int BN, bool BWD>
 struct Layout {
   static constexpr int kA = kBM * kBK * 2;                     // 16 KB
   static constexpr int kB = BN * kBK * 2;                      // BN x 64 16-bit values
   static constexpr int kW = BWD ? (kBK * BN / 2) : (BN * 32);  // packed words of the slice
-  static constexpr int kStage = kA + kB + kW;
-  // four stages where they fit next to the static shared memory, else three
-  static constexpr int kStages = (4 * kStage + 1024 <= 226 * 1024) ? 4 : 3;
-  static constexpr int kBytes = kStages * kStage + 1024;       // + alignment slack
+  static constexpr int kAW = kA + kW;
+  static constexpr int kSA = BN == 256 ? 5 : 6;
+  static constexpr int kSB = BN == 256 ? 3 : 4;
+  static constexpr int kBytes = kSA * kAW + kSB * kB + 1024;   // + alignment slack
+  static_assert(kBytes <= 226 * 1024, "shared memory");
 };
 
 template <int BN, bool BWD, typename XT, typename ST>
@@ -196,16 +203,16 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
           const XT* __restrict__ bias, XT* __restrict__ out, int M, int N, int K) {
   using L = Layout<BN, BWD>;
   using PS = typename Pair<ST>::P;
-  constexpr int kStages = L::kStages;
+  constexpr int SA = L::kSA, SB = L::kSB;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t a_full[kStages], b_full[kStages], empty[kStages], acc_full;
+  __shared__ __align__(8) uint64_t a_full[SA], a_empty[SA], b_full[SB], b_empty[SB], acc_full;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  auto sA = [&](int s) { return smem + s * L::kStage; };
-  auto sB = [&](int s) { return smem + s * L::kStage + L::kA; };
-  auto sW = [&](int s) { return smem + s * L::kStage + L::kA + L::kB; };
+  auto sA = [&](int s) { return smem + s * L::kAW; };
+  auto sW = [&](int s) { return smem + s * L::kAW + L::kA; };
+  auto sB = [&](int s) { return smem + SA * L::kAW + s * L::kB; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // forward: output tile (m0, n0), reduction over K; backward: output tile
@@ -217,10 +224,13 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
   volatile int* abort_flag = &s_abort;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < SA; ++s) {
       mbar_init(&a_full[s], 1);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int s = 0; s < SB; ++s) {
       mbar_init(&b_full[s], kDqThreads / 32);
-      mbar_init(&empty[s], 1);
+      mbar_init(&b_empty[s], 1);
     }
     mbar_init(&acc_full, 1);
     s_abort = 0;
@@ -243,10 +253,10 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
     if (lane == 0) {
       int issued = 0;
       for (int it = 0; it < KT; ++it) {
-        const int s = it % kStages;
-        const unsigned ph = (unsigned)(it / kStages) & 1u;
-        if (!wait_or_abort(&empty[s], ph ^ 1u, abort_flag)) { s_abort = 1; break; }
-        mbar_arrive_expect_tx(&a_full[s], (unsigned)(L::kA + L::kW));
+        const int s = it % SA;
+        const unsigned ph = (unsigned)(it / SA) & 1u;
+        if (!wait_or_abort(&a_empty[s], ph ^ 1u, abort_flag)) { s_abort = 1; break; }
+        mbar_arrive_expect_tx(&a_full[s], (unsigned)L::kAW);
         tma_2d(sA(s), &tmap_a, it * kBK, m0, &a_full[s]);
         if constexpr (BWD) tma_2d(sW(s), &tmap_w, n0 / 8, it * kBK, &a_full[s]);
         else tma_2d(sW(s), &tmap_w, it * (kBK / 8), n0, &a_full[s]);
@@ -254,8 +264,8 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
       }
       if (*abort_flag) {
         // copies still in flight land before the CTA's shared memory goes away
-        for (int it = issued - kStages < 0 ? 0 : issued - kStages; it < issued; ++it)
-          (void)mbar_wait(&a_full[it % kStages], (unsigned)(it / kStages) & 1u);
+        for (int it = issued - SA < 0 ? 0 : issued - SA; it < issued; ++it)
+          (void)mbar_wait(&a_full[it % SA], (unsigned)(it / SA) & 1u);
       }
     }
   } else if (warp == 1) {
@@ -264,15 +274,14 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
       constexpr uint32_t ab = std::is_same<XT, bf16>::value ? 1u : 0u;
       constexpr uint32_t idesc = f16_idesc(ab, BWD ? 1u : 0u, kBM, BN);
       for (int it = 0; it < KT; ++it) {
-        const int s = it % kStages;
-        const unsigned ph = (unsigned)(it / kStages) & 1u;
-        if (!wait_or_abort(&a_full[s], ph, abort_flag) ||
-            !wait_or_abort(&b_full[s], ph, abort_flag)) {
+        const int sa = it % SA, sb = it % SB;
+        if (!wait_or_abort(&a_full[sa], (unsigned)(it / SA) & 1u, abort_flag) ||
+            !wait_or_abort(&b_full[sb], (unsigned)(it / SB) & 1u, abort_flag)) {
           s_abort = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(s));
+        const uint32_t a0 = smem_u32(sA(sa)), b0 = smem_u32(sB(sb));
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {
           // A: 128 rows x 128 bytes, 8-row groups 1 KB apart; +32 bytes per 16 k
@@ -287,7 +296,8 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
           }
           umma_f16(tmem, ad, bd, idesc, (it | kk) != 0 ? 1u : 0u);
         }
-        umma_commit(&empty[s]);
+        umma_commit(&a_empty[sa]);  // both slots free once these MMAs complete
+        umma_commit(&b_empty[sb]);
       }
       umma_commit(&acc_full);  // also after an abort: marks the issued MMAs' completion
     }
@@ -331,22 +341,26 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
       for (int u = 0; u < kPre; ++u) {
         const int it = it0 + u;
         if (it >= KT) break;
-        const int s = it % kStages;
-        const unsigned ph = (unsigned)(it / kStages) & 1u;
+        const int sa = it % SA, sb = it % SB;
         const PS s2 = Pair<ST>::dup(sv[u]), b2 = Pair<ST>::dup(bv[u]);
         if (it + kPre < KT) {
           const size_t i = sb_index(it + kPre);
           sv[u] = scales[i];
           bv[u] = biases[i];
         }
-        if (!wait_or_abort(&a_full[s], ph, abort_flag)) { s_abort = 1; stop = true; break; }
+        if (!wait_or_abort(&a_full[sa], (unsigned)(it / SA) & 1u, abort_flag) ||
+            !wait_or_abort(&b_empty[sb], ((unsigned)(it / SB) & 1u) ^ 1u, abort_flag)) {
+          s_abort = 1;
+          stop = true;
+          break;
+        }
         uint32_t wd[WPT];
 #pragma unroll
         for (int q = 0; q < WPT; q += 4) {
-          const uint4 w = *reinterpret_cast<const uint4*>(sW(s) + wofs + 4 * q);
+          const uint4 w = *reinterpret_cast<const uint4*>(sW(sa) + wofs + 4 * q);
           wd[q] = w.x; wd[q + 1] = w.y; wd[q + 2] = w.z; wd[q + 3] = w.w;
         }
-        uint8_t* bt = sB(s);
+        uint8_t* bt = sB(sb);
 #pragma unroll
         for (int q = 0; q < WPT; ++q) {
           const uint4 v = dequant8<XT, ST>(wd[q], s2, b2);
@@ -365,7 +379,7 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
         fence_proxy_async_smem();  // the MMA reads these through the async proxy
         __syncwarp();
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(
-                                        smem_u32(&b_full[s]))
+                                        smem_u32(&b_full[sb]))
                                     : "memory");
       }
     }
