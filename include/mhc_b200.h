@@ -274,8 +274,9 @@ MHC_API int mhc_residual_add_agg_bwd(const void* out, int out_dtype, const void*
  *   W[n, k] = scales[n, k/64] * q[n, k] + biases[n, k/64],  q in [0, 15]
  * w_packed is [N][K/8] 32-bit words, code k%8 of row n in bits [4(k%8), 4(k%8)+4)
  * of word k/8; scales / biases are [N][K/64] in scales_dtype (MHC_BF16 or
- * MHC_F16).  The dequantisation rounds q * scale and then + bias to that
- * dtype, then the value to the activations' dtype.
+ * MHC_F16).  Each weight is q * scale + bias, one fused multiply-add in the
+ * activations' dtype (the tensor-core operand type; scale and bias are
+ * rounded to it first when stored in the other 16-bit type).
  *   mhc_qlinear_fwd:    y[M, N]  = x[M, K] W^T (+ bias[N], x's dtype, may be NULL)
  *   mhc_qlinear_bwd_dx: dx[M, K] = dy[M, N] W
  * x / dy / y / dx are row-contiguous bf16 or fp16 (one dtype per call);

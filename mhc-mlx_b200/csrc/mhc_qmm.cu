@@ -10,8 +10,9 @@
 //   backward:  dx[m, k] = sum_n dy[m, n] W[n, k]
 // q is packed eight to a 32-bit word, code j of a word in bits [4j, 4j + 4)
 // (word w of row n holds k = 8w .. 8w + 7).  Each weight is q * scale + bias
-// computed with one fused multiply-add in the scales' dtype (one rounding),
-// then rounded to the activations' dtype (bf16 or fp16) for the product;
+// computed with one fused multiply-add in the activations' dtype (bf16 or
+// fp16, the tensor-core operand type; one rounding), the scale and bias
+// rounded to that dtype first when they are stored in the other 16-bit type;
 // products are accumulated in fp32.
 //
 // One CTA computes a 128 x BN output tile (BN = 256 or 128) with
@@ -154,12 +155,13 @@ __device__ __forceinline__ P of_bits(uint32_t u) {
 }
 
 // Eight codes of one word -> eight XT values (one 16-byte chunk, in k order):
-// q * scale + bias as one fused multiply-add in the scales' dtype (one
-// rounding), then converted to the operand dtype when it differs.
-template <typename XT, typename ST>
-__device__ __forceinline__ uint4 dequant8(uint32_t w, typename Pair<ST>::P s2,
-                                          typename Pair<ST>::P b2) {
-  using PS = typename Pair<ST>::P;
+// q * scale + bias as one fused multiply-add in XT (one rounding).  The scale
+// and bias arrive already in XT (converted once per slice), so no value is
+// converted per weight: the conversion unit is the narrowest pipe of the SM.
+template <typename XT>
+__device__ __forceinline__ uint4 dequant8(uint32_t w, typename Pair<XT>::P s2,
+                                          typename Pair<XT>::P b2) {
+  using PX = typename Pair<XT>::P;
   const uint32_t w4 = w >> 4;
   uint32_t o[4];
 #pragma unroll
@@ -167,14 +169,9 @@ __device__ __forceinline__ uint4 dequant8(uint32_t w, typename Pair<ST>::P s2,
     // byte p of w holds codes 2p (low nibble) and 2p + 1 (high nibble)
     const uint32_t t = __byte_perm(w, w4, 0x4400u + 0x1111u * (uint32_t)p);
     uint32_t m;
-    asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(m) : "r"(t), "r"(0x000F000Fu), "r"(Pair<ST>::kMagic));
-    PS v = __hsub2(of_bits<PS>(m), Pair<ST>::offset());  // exact codes
-    v = __hfma2(v, s2, b2);
-    if constexpr (std::is_same<XT, ST>::value) {
-      o[p] = bits_of(v);
-    } else {
-      o[p] = bits_of(Pair<XT>::from_f2(Pair<ST>::to_f2(v)));
-    }
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(m) : "r"(t), "r"(0x000F000Fu), "r"(Pair<XT>::kMagic));
+    const PX v = __hsub2(of_bits<PX>(m), Pair<XT>::offset());  // exact codes
+    o[p] = bits_of(__hfma2(v, s2, b2));
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
@@ -202,7 +199,7 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
           const ST* __restrict__ scales, const ST* __restrict__ biases,
           const XT* __restrict__ bias, XT* __restrict__ out, int M, int N, int K) {
   using L = Layout<BN, BWD>;
-  using PS = typename Pair<ST>::P;
+  using PX = typename Pair<XT>::P;
   constexpr int SA = L::kSA, SB = L::kSB;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t a_full[SA], a_empty[SA], b_full[SB], b_empty[SB], acc_full;
@@ -342,7 +339,9 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
         const int it = it0 + u;
         if (it >= KT) break;
         const int sa = it % SA, sb = it % SB;
-        const PS s2 = Pair<ST>::dup(sv[u]), b2 = Pair<ST>::dup(bv[u]);
+        // scale / bias in the operand dtype (exact when ST is XT)
+        const PX s2 = Pair<XT>::dup(from_f<XT>(to_f(sv[u])));
+        const PX b2 = Pair<XT>::dup(from_f<XT>(to_f(bv[u])));
         if (it + kPre < KT) {
           const size_t i = sb_index(it + kPre);
           sv[u] = scales[i];
@@ -363,7 +362,7 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
         uint8_t* bt = sB(sb);
 #pragma unroll
         for (int q = 0; q < WPT; ++q) {
-          const uint4 v = dequant8<XT, ST>(wd[q], s2, b2);
+          const uint4 v = dequant8<XT>(wd[q], s2, b2);
           const int j = j0 + q;  // 16-byte chunk within the row's 128 bytes
           uint32_t off;
           if constexpr (BWD) {
