@@ -24,7 +24,7 @@
 //   warp 1      allocates the accumulator columns in tensor memory; one
 //               thread issues four 128 x BN x 16 MMAs per slice and commits
 //               them to the slice's "empty" barrier;
-//   warps 2-9   dequantise the slice's words into the B operand's 128-byte
+//   warps 2-17  dequantise the slice's words into the B operand's 128-byte
 //               swizzled layout in a three- or four-stage ring in shared
 //               memory (K-major for the forward, MN-major for the backward),
 //               then read the accumulators back
@@ -44,7 +44,7 @@ namespace mhc {
 namespace {
 
 constexpr int kBM = 128, kBK = 64, kGroup = 64;
-constexpr int kThreads = 320, kDqThreads = 256;
+constexpr int kThreads = 576, kDqThreads = 512;
 constexpr unsigned kWaitLimit = 1u << 22;
 
 // Shared-memory descriptor of a 128-byte-swizzled operand tile (tcgen05
@@ -301,22 +301,23 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
   } else {
     // -------------------------------------------------------- dequantise --
     // A slice holds 8 * BN packed words (forward: BN weight rows x 8 words;
-    // backward: 64 weight rows x BN / 8 words); each of the 256 threads
-    // dequantises WPT = BN / 32 consecutive words of one row.
-    constexpr int WPT = BN / 32;
-    const int dq = threadIdx.x - 64;  // 0..255
+    // backward: 64 weight rows x BN / 8 words); each of the 512 threads
+    // dequantises WPT = BN / 64 consecutive words of one row (four warps per
+    // scheduler hide the latency of the shared-memory round trips).
+    constexpr int WPT = BN / 64;
+    const int dq = threadIdx.x - 64;  // 0..511
     const int G = K / kGroup;         // groups per weight row
     int r, blk, j0;                   // B-tile row, 64-column block (backward), first chunk
     if constexpr (BWD) {
-      r = dq >> 2;                    // reduction row 0..63
-      blk = ((dq & 3) * WPT) >> 3;
-      j0 = ((dq & 3) * WPT) & 7;
+      r = dq >> 3;                    // reduction row 0..63
+      blk = ((dq & 7) * WPT) >> 3;
+      j0 = ((dq & 7) * WPT) & 7;
     } else {
       r = dq % BN;                    // output feature row of the tile
       blk = 0;
       j0 = (dq / BN) * WPT;
     }
-    const int wofs = BWD ? r * (BN / 2) + (dq & 3) * WPT * 4 : r * 32 + j0 * 4;
+    const int wofs = BWD ? r * (BN / 2) + (dq & 7) * WPT * 4 : r * 32 + j0 * 4;
     // scale / bias of slice it: requested kPre slices ahead into a register
     // ring (the inner loop is unrolled, so the ring index is a constant)
     constexpr int kPre = 4;
@@ -354,10 +355,12 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
           break;
         }
         uint32_t wd[WPT];
-#pragma unroll
-        for (int q = 0; q < WPT; q += 4) {
-          const uint4 w = *reinterpret_cast<const uint4*>(sW(sa) + wofs + 4 * q);
-          wd[q] = w.x; wd[q + 1] = w.y; wd[q + 2] = w.z; wd[q + 3] = w.w;
+        if constexpr (WPT == 4) {
+          const uint4 w = *reinterpret_cast<const uint4*>(sW(sa) + wofs);
+          wd[0] = w.x; wd[1] = w.y; wd[2] = w.z; wd[3] = w.w;
+        } else {
+          const uint2 w = *reinterpret_cast<const uint2*>(sW(sa) + wofs);
+          wd[0] = w.x; wd[1] = w.y;
         }
         uint8_t* bt = sB(sb);
 #pragma unroll
@@ -386,9 +389,9 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
     const bool ok = wait_or_abort(&acc_full, 0u, abort_flag) && !*abort_flag;
     tc_fence_after();
     const int sp = warp & 3;                 // TMEM lanes 32 sp .. 32 sp + 31
-    const int half = (warp - 2) >> 2;        // columns [half BN/2, (half + 1) BN/2)
+    const int qtr = (warp - 2) >> 2;         // columns [qtr BN/4, (qtr + 1) BN/4)
     const int m = m0 + sp * 32 + lane;
-    for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
+    for (int c0 = qtr * (BN / 4); c0 < (qtr + 1) * (BN / 4); c0 += 32) {
       uint32_t r[32];
       tmem_ld32(tmem + ((uint32_t)(sp * 32) << 16) + (uint32_t)c0, r);
       if (m < M) {
