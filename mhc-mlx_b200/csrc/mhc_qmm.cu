@@ -24,7 +24,7 @@
 //   warp 1      allocates the accumulator columns in tensor memory; one
 //               thread issues four 128 x BN x 16 MMAs per slice and commits
 //               them to the slice's "empty" barrier;
-//   warps 2-17  dequantise the slice's words into the B operand's 128-byte
+//   warps 2-9   dequantise the slice's words into the B operand's 128-byte
 //               swizzled layout in a three- or four-stage ring in shared
 //               memory (K-major for the forward, MN-major for the backward),
 //               then read the accumulators back
@@ -35,6 +35,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "mhc_common.cuh"
@@ -44,7 +45,7 @@ namespace mhc {
 namespace {
 
 constexpr int kBM = 128, kBK = 64, kGroup = 64;
-constexpr int kThreads = 576, kDqThreads = 512;
+constexpr int kThreads = 320, kDqThreads = 256;
 constexpr unsigned kWaitLimit = 1u << 22;
 
 // Shared-memory descriptor of a 128-byte-swizzled operand tile (tcgen05
@@ -301,23 +302,22 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
   } else {
     // -------------------------------------------------------- dequantise --
     // A slice holds 8 * BN packed words (forward: BN weight rows x 8 words;
-    // backward: 64 weight rows x BN / 8 words); each of the 512 threads
-    // dequantises WPT = BN / 64 consecutive words of one row (four warps per
-    // scheduler hide the latency of the shared-memory round trips).
-    constexpr int WPT = BN / 64;
-    const int dq = threadIdx.x - 64;  // 0..511
+    // backward: 64 weight rows x BN / 8 words); each of the 256 threads
+    // dequantises WPT = BN / 32 consecutive words of one row.
+    constexpr int WPT = BN / 32;
+    const int dq = threadIdx.x - 64;  // 0..255
     const int G = K / kGroup;         // groups per weight row
     int r, blk, j0;                   // B-tile row, 64-column block (backward), first chunk
     if constexpr (BWD) {
-      r = dq >> 3;                    // reduction row 0..63
-      blk = ((dq & 7) * WPT) >> 3;
-      j0 = ((dq & 7) * WPT) & 7;
+      r = dq >> 2;                    // reduction row 0..63
+      blk = ((dq & 3) * WPT) >> 3;
+      j0 = ((dq & 3) * WPT) & 7;
     } else {
       r = dq % BN;                    // output feature row of the tile
       blk = 0;
       j0 = (dq / BN) * WPT;
     }
-    const int wofs = BWD ? r * (BN / 2) + (dq & 7) * WPT * 4 : r * 32 + j0 * 4;
+    const int wofs = BWD ? r * (BN / 2) + (dq & 3) * WPT * 4 : r * 32 + j0 * 4;
     // scale / bias of slice it: requested kPre slices ahead into a register
     // ring (the inner loop is unrolled, so the ring index is a constant)
     constexpr int kPre = 4;
@@ -355,12 +355,10 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
           break;
         }
         uint32_t wd[WPT];
-        if constexpr (WPT == 4) {
-          const uint4 w = *reinterpret_cast<const uint4*>(sW(sa) + wofs);
-          wd[0] = w.x; wd[1] = w.y; wd[2] = w.z; wd[3] = w.w;
-        } else {
-          const uint2 w = *reinterpret_cast<const uint2*>(sW(sa) + wofs);
-          wd[0] = w.x; wd[1] = w.y;
+#pragma unroll
+        for (int q = 0; q < WPT; q += 4) {
+          const uint4 w = *reinterpret_cast<const uint4*>(sW(sa) + wofs + 4 * q);
+          wd[q] = w.x; wd[q + 1] = w.y; wd[q + 2] = w.z; wd[q + 3] = w.w;
         }
         uint8_t* bt = sB(sb);
 #pragma unroll
@@ -389,9 +387,9 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
     const bool ok = wait_or_abort(&acc_full, 0u, abort_flag) && !*abort_flag;
     tc_fence_after();
     const int sp = warp & 3;                 // TMEM lanes 32 sp .. 32 sp + 31
-    const int qtr = (warp - 2) >> 2;         // columns [qtr BN/4, (qtr + 1) BN/4)
+    const int half = (warp - 2) >> 2;        // columns [half BN/2, (half + 1) BN/2)
     const int m = m0 + sp * 32 + lane;
-    for (int c0 = qtr * (BN / 4); c0 < (qtr + 1) * (BN / 4); c0 += 32) {
+    for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
       uint32_t r[32];
       tmem_ld32(tmem + ((uint32_t)(sp * 32) << 16) + (uint32_t)c0, r);
       if (m < M) {
@@ -425,6 +423,218 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
                  "r"((uint32_t)BN)
+                 : "memory");
+  }
+}
+
+// ------------------------------------------- forward, weights in TMEM --
+// Forward y = x W^T computed transposed, y^T[n, m] = sum_k W[n, k] x[m, k]:
+// the dequantised weights are the A operand and live in tensor memory (the
+// dequantising threads write them with tcgen05.st straight from registers,
+// no shared-memory round trip), the activations are the B operand (TMA,
+// 128-byte swizzled, K-major).  A CTA computes 128 features x 256 tokens.
+//   warp 0      TMA: activation slice (256 x 64) and the slice's packed words
+//               (two 128 x 4-word boxes) into a five-stage ring;
+//   warp 1      TMEM allocation; one thread issues the MMAs;
+//   warps 2-9   dequantise: warp w owns TMEM lanes 32 (w % 4) .. + 31 (its
+//               features) and half of the slice's 64 columns; afterwards
+//               they read y^T back and write y (32 consecutive features per
+//               warp store: 64 contiguous bytes).
+// TMEM columns: [0, 256) accumulators, [256, 384) four A stages of 32.
+constexpr int kTmTok = 256, kTmFeat = 128, kTmSX = 5, kTmSA = 4;
+
+struct TmLayout {
+  static constexpr int kX = kTmTok * kBK * 2;         // 32 KB activation slice
+  static constexpr int kW = kTmFeat * 8 * 4;          // 4 KB of packed words
+  static constexpr int kStage = kX + kW;
+  static constexpr int kBytes = kTmSX * kStage + 1024;
+  static_assert(kBytes <= 226 * 1024, "shared memory");
+};
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};\n" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <typename XT, typename ST>
+__global__ void __launch_bounds__(kThreads, 1)
+k_qlinear_fwd_tm(const __grid_constant__ CUtensorMap tmap_x,
+                 const __grid_constant__ CUtensorMap tmap_w, const ST* __restrict__ scales,
+                 const ST* __restrict__ biases, const XT* __restrict__ bias,
+                 XT* __restrict__ out, int M, int N, int K) {
+  using L = TmLayout;
+  using PX = typename Pair<XT>::P;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t x_full[kTmSX], x_empty[kTmSX], a_full[kTmSA], a_empty[kTmSA],
+      acc_full;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  auto sX = [&](int s) { return smem + s * L::kStage; };
+  auto sW = [&](int s, int h) { return smem + s * L::kStage + L::kX + h * (L::kW / 2); };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int f0 = blockIdx.x * kTmFeat, m0 = blockIdx.y * kTmTok;  // features, tokens
+  const int KT = K / kBK;
+  volatile int* abort_flag = &s_abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTmSX; ++s) { mbar_init(&x_full[s], 1); mbar_init(&x_empty[s], 1); }
+    for (int s = 0; s < kTmSA; ++s) {
+      mbar_init(&a_full[s], kDqThreads / 32);
+      mbar_init(&a_empty[s], 1);
+    }
+    mbar_init(&acc_full, 1);
+    s_abort = 0;
+    mbar_init_fence();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                     smem_u32(&s_tmem)),
+                 "r"(512u)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;             // accumulators: columns [0, 256)
+  const uint32_t tmem_a = tmem + kTmTok;    // A stages: 32 columns each
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int it = 0; it < KT; ++it) {
+        const int s = it % kTmSX;
+        if (!wait_or_abort(&x_empty[s], ((unsigned)(it / kTmSX) & 1u) ^ 1u, abort_flag)) {
+          s_abort = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&x_full[s], (unsigned)L::kStage);
+        tma_2d(sX(s), &tmap_x, it * kBK, m0, &x_full[s]);
+        tma_2d(sW(s, 0), &tmap_w, it * 8, f0, &x_full[s]);
+        tma_2d(sW(s, 1), &tmap_w, it * 8 + 4, f0, &x_full[s]);
+        issued = it + 1;
+      }
+      if (*abort_flag)
+        for (int it = issued - kTmSX < 0 ? 0 : issued - kTmSX; it < issued; ++it)
+          (void)mbar_wait(&x_full[it % kTmSX], (unsigned)(it / kTmSX) & 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ab = std::is_same<XT, bf16>::value ? 1u : 0u;
+      constexpr uint32_t idesc = f16_idesc(ab, 0u, kTmFeat, kTmTok);
+      for (int it = 0; it < KT; ++it) {
+        const int sx = it % kTmSX, sa = it % kTmSA;
+        if (!wait_or_abort(&x_full[sx], (unsigned)(it / kTmSX) & 1u, abort_flag) ||
+            !wait_or_abort(&a_full[sa], (unsigned)(it / kTmSA) & 1u, abort_flag)) {
+          s_abort = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t x0 = smem_u32(sX(sx));
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          umma_f16_ts(tmem, tmem_a + sa * 32 + kk * 8, sw128_desc(x0 + kk * 32, 16, 1024), idesc,
+                      (it | kk) != 0 ? 1u : 0u);
+        umma_commit(&x_empty[sx]);
+        umma_commit(&a_empty[sa]);
+      }
+      umma_commit(&acc_full);
+    }
+  } else {
+    // ---- dequantise: feature row f (TMEM lane), 32 of the slice's 64 columns
+    const int sp = warp & 3, half = (warp - 2) >> 2;
+    const int f = sp * 32 + lane;
+    const int G = K / kGroup;
+    const uint32_t lane_base = (uint32_t)(sp * 32) << 16;
+    constexpr int kPre = 4;
+    ST sv[kPre], bv[kPre];
+#pragma unroll
+    for (int u = 0; u < kPre; ++u) {
+      const size_t i = (size_t)(f0 + f) * G + (u < KT ? u : 0);
+      sv[u] = scales[i];
+      bv[u] = biases[i];
+    }
+    bool stop = false;
+    for (int it0 = 0; it0 < KT && !stop; it0 += kPre) {
+#pragma unroll
+      for (int u = 0; u < kPre; ++u) {
+        const int it = it0 + u;
+        if (it >= KT) break;
+        const int sx = it % kTmSX, sa = it % kTmSA;
+        const PX s2 = Pair<XT>::dup(from_f<XT>(to_f(sv[u])));
+        const PX b2 = Pair<XT>::dup(from_f<XT>(to_f(bv[u])));
+        if (it + kPre < KT) {
+          const size_t i = (size_t)(f0 + f) * G + it + kPre;
+          sv[u] = scales[i];
+          bv[u] = biases[i];
+        }
+        if (!wait_or_abort(&x_full[sx], (unsigned)(it / kTmSX) & 1u, abort_flag) ||
+            !wait_or_abort(&a_empty[sa], ((unsigned)(it / kTmSA) & 1u) ^ 1u, abort_flag)) {
+          s_abort = 1;
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+        // 4 words = 32 values of row f: [128 rows][4 words] per half, 16 B per row
+        const uint4 w = *reinterpret_cast<const uint4*>(sW(sx, half) + f * 16);
+        const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+        uint32_t v[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 o = dequant8<XT>(wd[q], s2, b2);
+          v[4 * q] = o.x; v[4 * q + 1] = o.y; v[4 * q + 2] = o.z; v[4 * q + 3] = o.w;
+        }
+        tmem_st16(tmem_a + lane_base + (uint32_t)(sa * 32 + half * 16), v);
+        asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(
+                                        smem_u32(&a_full[sa]))
+                                    : "memory");
+      }
+    }
+    // ---- epilogue: y[m, f0 + f] for the warp's 128 tokens
+    const bool ok = wait_or_abort(&acc_full, 0u, abort_flag) && !*abort_flag;
+    tc_fence_after();
+    const float bf = bias ? to_f(bias[f0 + f]) : 0.f;
+    for (int c0 = half * (kTmTok / 2); c0 < (half + 1) * (kTmTok / 2); c0 += 32) {
+      uint32_t r[32];
+      tmem_ld32(tmem + lane_base + (uint32_t)c0, r);
+#pragma unroll
+      for (int t = 0; t < 32; ++t) {
+        const int m = m0 + c0 + t;
+        if (m < M) {
+          float y = ok ? __uint_as_float(r[t]) : __int_as_float(0x7fc00000);
+          XT yv = from_f<XT>(y);
+          if (bias) yv = from_f<XT>(to_f(yv) + bf);
+          out[(size_t)m * N + f0 + f] = yv;
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
+                 "r"(512u)
                  : "memory");
   }
 }
@@ -492,9 +702,38 @@ int run_qlinear(const void* a, const uint32_t* wq, const void* scales, const voi
   return check_launch(BWD ? "qlinear_bwd_dx" : "qlinear_fwd");
 }
 
+template <typename XT, typename ST>
+int run_qlinear_fwd_tm(const void* x, const uint32_t* wq, const void* scales, const void* biases,
+                       const void* bias, void* out, int64_t M, int N, int K, cudaStream_t st) {
+  CUtensorMap mx, mw;
+  const CUtensorMapDataType xdt =
+      std::is_same<XT, bf16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  int r = make_map(&mx, xdt, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kBK, kTmTok,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+  if (r != MHC_OK) return r;
+  r = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, wq, (uint64_t)K / 8, (uint64_t)N,
+               (uint64_t)K / 2, 4, kTmFeat, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (r != MHC_OK) return r;
+  auto kern = k_qlinear_fwd_tm<XT, ST>;
+  const size_t smem = TmLayout::kBytes;
+  const cudaError_t e = allow_dyn_smem(kern, smem);
+  if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "qlinear: %s", cudaGetErrorString(e));
+  const dim3 grid(N / kTmFeat, (unsigned)((M + kTmTok - 1) / kTmTok));
+  kern<<<grid, kThreads, smem, st>>>(mx, mw, static_cast<const ST*>(scales),
+                                     static_cast<const ST*>(biases), static_cast<const XT*>(bias),
+                                     static_cast<XT*>(out), (int)M, N, K);
+  return check_launch("qlinear_fwd");
+}
+
 template <bool BWD, typename XT, typename ST>
 int dispatch_bn(const void* a, const uint32_t* wq, const void* scales, const void* biases,
                 const void* bias, void* out, int64_t M, int N, int K, cudaStream_t st) {
+  if constexpr (!BWD) {
+    // MHC_B200_QMM_SMEM_B=1 selects the shared-memory-B forward (A/B measurement)
+    const char* e = std::getenv("MHC_B200_QMM_SMEM_B");
+    if (!e || std::atoi(e) == 0)
+      return run_qlinear_fwd_tm<XT, ST>(a, wq, scales, biases, bias, out, M, N, K, st);
+  }
   const int out_cols = BWD ? K : N;
   if (out_cols % 256 == 0)
     return run_qlinear<256, BWD, XT, ST>(a, wq, scales, biases, bias, out, M, N, K, st);
