@@ -759,6 +759,231 @@ k_bwd_rows(const T* __restrict__ x, const T* __restrict__ dout, const float* __r
   if (blockIdx.x == 0 && tid == 0) { ws_hdr[0] = gridDim.x; ws_hdr[1] = 1; }
 }
 
+// Full-row backward for fp32 rows (x, d_out, dx fp32, C = 8 * BD): the
+// k_bwd_rows design with the rows staged by bulk copies, in half tokens.  An
+// fp32 token is 2N rows of C floats (128 KB at n = 4, C = 4096), too large for
+// a ring of whole tokens, so the ring holds NS = 3 half tokens (columns
+// [0, C/2) or [C/2, C) of all 2N rows, 64 KB each): thread t owns columns
+// 4t .. 4t + 3 of each half, so its shared-memory reads are consecutive
+// 16-byte chunks across the warp.  After token t's block reduction both of
+// its halves are free and the next two halves of this CTA's sequence are
+// requested into them.  dM runs on the fp32 pipe (fp32 products are not exact
+// on the tensor cores).  Waits are bounded as in k_bwd_rows: a copy that never
+// lands makes the CTA write NaN into its dx rows and partial rows.
+template <int N, int BD>
+__global__ void __launch_bounds__(BD, 1)
+k_bwd_rows32(const float* __restrict__ x, const float* __restrict__ dout,
+             const float* __restrict__ Mg, const float* __restrict__ hpre_g,
+             const float* __restrict__ hpost_g, const float* __restrict__ w,
+             float* __restrict__ dx, int64_t T_, float eps, float* __restrict__ ws_p,
+             float* __restrict__ ws_c, int* __restrict__ ws_hdr) {
+  constexpr int C = 8 * BD, H = C / 2, P = N * N + 2 * N, NW = BD / 32, NS = 3;
+  constexpr int64_t RS = (int64_t)N * C;   // elements per token
+  constexpr int SLOT = 2 * N * H;          // floats per half-token slot
+  constexpr unsigned kRowBytes = H * 4, kHalfBytes = 2 * N * kRowBytes;
+  extern __shared__ float4 s_dyn4[];
+  float4* s_w = s_dyn4;                                         // [2][BD]
+  float* s_stage = reinterpret_cast<float*>(s_dyn4 + 2 * BD);   // [NS][2N][H]
+  __shared__ __align__(16) float sMT[N * N];  // sMT[j * N + i] = M[i][j]
+  __shared__ float red[2][64];
+  __shared__ float sacc[NW * P];
+  __shared__ __align__(8) uint64_t s_full[NS];
+  __shared__ int s_abort;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t G = gridDim.x;
+  if (tid == 0) {
+#pragma unroll
+    for (int b = 0; b < NS; ++b) mbar_init(&s_full[b], 1);
+    s_abort = 0;
+    mbar_init_fence();
+  }
+  for (int e = tid; e < N * N; e += BD) sMT[(e % N) * N + e / N] = Mg[e];
+  s_w[tid] = __ldg(reinterpret_cast<const float4*>(w) + tid);
+  s_w[BD + tid] = __ldg(reinterpret_cast<const float4*>(w + H) + tid);
+  float hpre[N], hpost[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) { hpre[i] = __ldg(hpre_g + i); hpost[i] = __ldg(hpost_g + i); }
+  __syncthreads();
+  auto load_w = [&](float (&wv)[8]) {
+    const float4 a = s_w[tid], b = s_w[BD + tid];
+    wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
+    wv[4] = b.x; wv[5] = b.y; wv[6] = b.z; wv[7] = b.w;
+  };
+
+  // this CTA's tokens blockIdx.x, blockIdx.x + G, ...; half k of the
+  // sequence is token k / 2, columns [(k % 2) H, (k % 2 + 1) H)
+  const int64_t ntok = (int64_t)blockIdx.x < T_ ? (T_ - 1 - blockIdx.x) / G + 1 : 0;
+  const unsigned nhalf = (unsigned)(2 * ntok);
+  auto issue = [&](unsigned k) {  // one thread
+    const int64_t tok = blockIdx.x + (int64_t)(k >> 1) * G;
+    const int h = (int)(k & 1u);
+    const int slot = (int)(k % NS);
+    float* sd = s_stage + slot * SLOT;
+    mbar_arrive_expect_tx(&s_full[slot], kHalfBytes);
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      bulk_g2s(sd + i * H, x + tok * RS + (int64_t)i * C + h * H, kRowBytes, &s_full[slot]);
+      bulk_g2s(sd + (N + i) * H, dout + tok * RS + (int64_t)i * C + h * H, kRowBytes,
+               &s_full[slot]);
+    }
+  };
+  unsigned issued = 0;  // meaningful in thread 0
+  if (tid == 0)
+    for (; issued < NS && issued < nhalf; ++issued) issue(issued);
+
+  float aM[N][N], aPre[N], aPost[N], aW[8];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    aPre[i] = 0.f; aPost[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) aM[i][j] = 0.f;
+  }
+#pragma unroll
+  for (int v = 0; v < 8; ++v) aW[v] = 0.f;
+
+  int par = 0;
+  unsigned use = 0;  // halves consumed
+  bool aborted = false;
+  int64_t t = blockIdx.x;
+  for (; t < T_; t += G) {
+    float xr[N][8], dr[N][8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int slot = (int)(use % NS);
+      if (!mbar_wait(&s_full[slot], (use / NS) & 1u)) s_abort = 1;
+      const float* sb = s_stage + slot * SLOT + 4 * tid;
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const float4 a = *reinterpret_cast<const float4*>(sb + i * H);
+        const float4 b = *reinterpret_cast<const float4*>(sb + (N + i) * H);
+        xr[i][4 * h] = a.x; xr[i][4 * h + 1] = a.y; xr[i][4 * h + 2] = a.z; xr[i][4 * h + 3] = a.w;
+        dr[i][4 * h] = b.x; dr[i][4 * h + 1] = b.y; dr[i][4 * h + 2] = b.z; dr[i][4 * h + 3] = b.w;
+      }
+      ++use;
+    }
+    // y and dyn are recomputed in the second pass (fp32 has issue slots to
+    // spare; keeping them would spill at 128 registers)
+    float ss = 0.f, pd = 0.f;
+    {
+      float wv[8];
+      load_w(wv);
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        float y = 0.f, dyn = 0.f;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          y = fmaf(hpre[i], xr[i][v], y);
+          dyn = fmaf(hpost[i], dr[i][v], dyn);
+        }
+        ss = fmaf(y, y, ss);
+        pd = fmaf(dyn * wv[v], y, pd);
+      }
+    }
+    const float2 red2 = block_sum2_bfly<NW>(ss, pd, red[par]);
+    par ^= 1;
+    // after the barrier every thread has read both halves, and s_abort is
+    // the same for all
+    if (s_abort) { aborted = true; break; }
+    if (tid == 0) {
+      fence_proxy_async_smem();
+      for (int k = 0; k < 2 && issued < nhalf; ++k, ++issued) issue(issued);
+    }
+    const float inv = inv_rms(red2.x, C, eps);
+    const float k2 = (red2.y * (inv * inv * inv)) * (1.0f / (float)C);
+
+    float dya[8];
+    {
+      float wv[8];
+      load_w(wv);
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        float yv = 0.f, dv = 0.f;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          yv = fmaf(hpre[i], xr[i][v], yv);
+          dv = fmaf(hpost[i], dr[i][v], dv);
+        }
+        const float yi = yv * inv;
+        const float yn = yi * wv[v];
+        aW[v] = fmaf(dv, yi, aW[v]);
+        const float g = (dv * wv[v]) * inv - k2 * yv;
+        dya[v] = g;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          aPost[i] = fmaf(dr[i][v], yn, aPost[i]);
+          aPre[i] = fmaf(g, xr[i][v], aPre[i]);
+#pragma unroll
+          for (int j = 0; j < N; ++j) aM[i][j] = fmaf(dr[i][v], xr[j][v], aM[i][j]);
+        }
+      }
+    }
+    float* dxt = dx + t * RS + 4 * tid;
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      float mc[N];
+#pragma unroll
+      for (int i = 0; i < N; ++i) mc[i] = sMT[j * N + i];
+      float o[8];
+#pragma unroll
+      for (int v = 0; v < 8; ++v) o[v] = hpre[j] * dya[v];
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+#pragma unroll
+        for (int v = 0; v < 8; ++v) o[v] = fmaf(mc[i], dr[i][v], o[v]);
+      __stcs(reinterpret_cast<float4*>(dxt + (int64_t)j * C), make_float4(o[0], o[1], o[2], o[3]));
+      __stcs(reinterpret_cast<float4*>(dxt + (int64_t)j * C + H),
+             make_float4(o[4], o[5], o[6], o[7]));
+    }
+  }
+  if (aborted) {
+    // a bulk copy did not land in time: wait (bounded) for this CTA's other
+    // copies in flight, then mark everything it owns as invalid
+    if (tid == 0)
+      for (unsigned k = use; k < issued; ++k) (void)mbar_wait(&s_full[k % NS], (k / NS) & 1u);
+    const float nan = __int_as_float(0x7fc00000);
+    const float4 n4 = make_float4(nan, nan, nan, nan);
+    for (; t < T_; t += G)
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float* dxt = dx + t * RS + (int64_t)j * C + 4 * tid;
+        reinterpret_cast<float4*>(dxt)[0] = n4;
+        reinterpret_cast<float4*>(dxt + H)[0] = n4;
+      }
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      aPre[i] = nan; aPost[i] = nan;
+#pragma unroll
+      for (int j = 0; j < N; ++j) aM[i][j] = nan;
+    }
+#pragma unroll
+    for (int v = 0; v < 8; ++v) aW[v] = nan;
+  }
+
+  // ---- per-CTA partials: fixed-order warp reductions + ordered warp sum ----
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float v = warp_sum(aM[i][j]);
+      if (lane == 0) sacc[warp * P + i * N + j] = v;
+    }
+    const float a = warp_sum(aPre[i]);
+    const float b = warp_sum(aPost[i]);
+    if (lane == 0) { sacc[warp * P + N * N + i] = a; sacc[warp * P + N * N + N + i] = b; }
+  }
+  __syncthreads();
+  for (int e = tid; e < P; e += BD) {
+    float sum = 0.f;
+#pragma unroll 4
+    for (int q = 0; q < NW; ++q) sum += sacc[q * P + e];
+    ws_p[(size_t)blockIdx.x * P + e] = sum;
+  }
+  float* wc = ws_c + (size_t)blockIdx.x * C + 4 * tid;
+  reinterpret_cast<float4*>(wc)[0] = make_float4(aW[0], aW[1], aW[2], aW[3]);
+  reinterpret_cast<float4*>(wc + H)[0] = make_float4(aW[4], aW[5], aW[6], aW[7]);
+  if (blockIdx.x == 0 && tid == 0) { ws_hdr[0] = gridDim.x; ws_hdr[1] = 1; }
+}
+
 // Generic backward: any n <= 64, any C.  Pass 1 reduces ss and pd for the
 // row; pass 2 walks the row in tiles of blockDim columns: each thread stages
 // its column of x and d_out in shared memory (plus two extra rows: y inv w
@@ -1653,6 +1878,38 @@ static int launch_bwd_rows(const T* x, const T* d, const float* M, const float* 
   return go(k_bwd_rows<N, T, BD, false, 1>, wb + rows);
 }
 
+// fp32 full-row backward with bulk-copy half-token staging (k_bwd_rows32) for
+// n = 4, C = 8 * BD, BD in {128, 256, 512}.  Returns -1 when not applicable.
+template <int BD>
+static int launch_bwd_rows32(const float* x, const float* d, const float* M, const float* hpre,
+                             const float* hpost, const float* w, float* dx, int64_t T_,
+                             float eps, void* ws, cudaStream_t st) {
+  constexpr int C = 8 * BD;
+  const size_t dyn = (size_t)BD * 32 + (size_t)3 * 2 * 4 * (C / 2) * sizeof(float);
+  if (dyn + 4096 > (size_t)max_smem_optin()) return -1;
+  auto kern = k_bwd_rows32<4, BD>;
+  cudaError_t e = allow_dyn_smem(kern, dyn);
+  if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "mhc_bwd: %s", cudaGetErrorString(e));
+  const int G = persistent_grid(kern, BD, dyn, T_, max_partial_rows(T_));
+  BwdPtrs p = ws_ptrs(ws, G, 4);
+  kern<<<G, BD, dyn, st>>>(x, d, M, hpre, hpost, w, dx, T_, eps, p.p, p.c, p.hdr);
+  return check_launch("mhc_bwd");
+}
+
+static int bwd_rows32(const float* x, const float* d, const float* M, const float* hpre,
+                      const float* hpost, const float* w, float* dx, int64_t T_, int C,
+                      float eps, void* ws, cudaStream_t st) {
+  // MHC_B200_BULK32=0 keeps the per-thread cp.async backward (A/B measurement)
+  if (!env_int("MHC_B200_BULK32", 1) || !env_int("MHC_B200_FULL", 1)) return -1;
+  if (!(aligned16(x) && aligned16(d) && aligned16(dx) && aligned16(w))) return -1;
+  switch (C) {
+    case 1024: return launch_bwd_rows32<128>(x, d, M, hpre, hpost, w, dx, T_, eps, ws, st);
+    case 2048: return launch_bwd_rows32<256>(x, d, M, hpre, hpost, w, dx, T_, eps, ws, st);
+    case 4096: return launch_bwd_rows32<512>(x, d, M, hpre, hpost, w, dx, T_, eps, ws, st);
+    default: return -1;
+  }
+}
+
 template <int N, typename T>
 static int bwd_rows(const T* x, const T* d, const float* M, const float* hpre, const float* hpost,
                     const float* w, T* dx, int64_t T_, int C, float eps, void* ws,
@@ -1730,6 +1987,11 @@ static int bwd_fast(const XT* x, const DT* d, const float* M, const float* hpre,
   if constexpr (sizeof(XT) == 2 && std::is_same<XT, DT>::value && std::is_same<XT, DXT>::value &&
                 N <= 4) {
     const int r = bwd_rows<N, XT>(x, d, M, hpre, hpost, w, dx, T, C, eps, ws, st);
+    if (r >= 0) return r;
+  }
+  if constexpr (N == 4 && std::is_same<XT, float>::value && std::is_same<DT, float>::value &&
+                std::is_same<DXT, float>::value) {
+    const int r = bwd_rows32(x, d, M, hpre, hpost, w, dx, T, C, eps, ws, st);
     if (r >= 0) return r;
   }
   if constexpr (VX == VD && VecOf<DXT>::value == VX) {

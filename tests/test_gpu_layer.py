@@ -158,7 +158,8 @@ def _layer_grads(x, params, d_out, iters, eps, return_dtype=None):
 
 GRAD_SHAPES = [(1, 4, 16, 5), (2, 4, 128, 20), (3, 4, 129, 20), (2, 1, 64, 3), (2, 2, 100, 20),
                (2, 8, 128, 20), (2, 3, 40, 20), (2, 16, 256, 20), (1, 32, 256, 20),
-               (1, 64, 96, 20), (5, 4, 4096, 20), (4, 4, 2048, 20), (2, 8, 4096, 10),
+               (1, 64, 96, 20), (5, 4, 4096, 20), (4, 4, 2048, 20), (3, 4, 1024, 20),
+               (300, 4, 4096, 20), (2, 8, 4096, 10),
                # cluster-split generic backward: column slices of a token over 2-8 CTAs
                (2, 32, 4096, 20), (3, 16, 2048, 20), (2, 32, 1000, 20), (1, 64, 1024, 10)]
 
