@@ -846,7 +846,12 @@ k_bwd_rows32(const float* __restrict__ x, const float* __restrict__ dout,
   bool aborted = false;
   int64_t t = blockIdx.x;
   for (; t < T_; t += G) {
+    // each half's first-pass sums are taken as soon as it lands, so the
+    // wait for the second half (requested later) overlaps that arithmetic;
+    // y and dyn are recomputed in the second pass (fp32 has issue slots to
+    // spare; keeping them would spill at 128 registers)
     float xr[N][8], dr[N][8];
+    float ss = 0.f, pd = 0.f;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int slot = (int)(use % NS);
@@ -860,15 +865,10 @@ k_bwd_rows32(const float* __restrict__ x, const float* __restrict__ dout,
         dr[i][4 * h] = b.x; dr[i][4 * h + 1] = b.y; dr[i][4 * h + 2] = b.z; dr[i][4 * h + 3] = b.w;
       }
       ++use;
-    }
-    // y and dyn are recomputed in the second pass (fp32 has issue slots to
-    // spare; keeping them would spill at 128 registers)
-    float ss = 0.f, pd = 0.f;
-    {
-      float wv[8];
-      load_w(wv);
+      const float4 w4 = s_w[h * BD + tid];
+      const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-      for (int v = 0; v < 8; ++v) {
+      for (int v = 4 * h; v < 4 * h + 4; ++v) {
         float y = 0.f, dyn = 0.f;
 #pragma unroll
         for (int i = 0; i < N; ++i) {
@@ -876,7 +876,7 @@ k_bwd_rows32(const float* __restrict__ x, const float* __restrict__ dout,
           dyn = fmaf(hpost[i], dr[i][v], dyn);
         }
         ss = fmaf(y, y, ss);
-        pd = fmaf(dyn * wv[v], y, pd);
+        pd = fmaf(dyn * wv[v - 4 * h], y, pd);
       }
     }
     const float2 red2 = block_sum2_bfly<NW>(ss, pd, red[par]);
