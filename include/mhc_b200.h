@@ -292,6 +292,18 @@ MHC_API int mhc_qlinear_bwd_dx(const void* dy, int dy_dtype, const uint32_t* w_p
                                void* dx, int64_t M, int N, int K, int group_size, int bits,
                                void* stream);
 
+/* The same input gradient from the transposed layouts of the frozen weight
+ * (no counterpart in the reference: a derived, cacheable copy for the
+ * backward), which let the dequantised rows of W^T live in tensor memory:
+ *   wt_packed  [K][N/8] 32-bit words, code n%8 of row k in bits
+ *              [4(n%8), 4(n%8)+4) of word n/8 (the codes of W^T);
+ *   scales_t, biases_t  [K/64][N] in dy's dtype (scales[n][g] at [g][n]).
+ * Same coverage as mhc_qlinear_bwd_dx; scales_t / biases_t 16-byte aligned. */
+MHC_API int mhc_qlinear_bwd_dx_t(const void* dy, int dy_dtype, const uint32_t* wt_packed,
+                                 const void* scales_t, const void* biases_t, void* dx,
+                                 int64_t M, int N, int K, int group_size, int bits,
+                                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

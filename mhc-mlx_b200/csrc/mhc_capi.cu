@@ -424,6 +424,15 @@ int mhc_qlinear_bwd_dx(const void* dy, int dy_dtype, const uint32_t* w_packed,
   MHC_TRY_END
 }
 
+int mhc_qlinear_bwd_dx_t(const void* dy, int dy_dtype, const uint32_t* wt_packed,
+                         const void* scales_t, const void* biases_t, void* dx, int64_t M, int N,
+                         int K, int group_size, int bits, void* stream) {
+  MHC_TRY_BEGIN
+  return launch_qlinear_bwd_dx_t(dy, dy_dtype, wt_packed, scales_t, biases_t, dx, M, N, K,
+                                 group_size, bits, as_stream(stream));
+  MHC_TRY_END
+}
+
 int mhc_residual_add_agg(const void* x, int x_dtype, const void* res, int res_dtype,
                          const float* H_pre, void* out, int out_dtype, float* y_agg, int64_t T,
                          int n, int C, void* stream) {

@@ -441,12 +441,22 @@ k_qlinear(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CU
 //               they read y^T back and write y (32 consecutive features per
 //               warp store: 64 contiguous bytes).
 // TMEM columns: [0, 256) accumulators, [256, 384) four A stages of 32.
+//
+// BWD = true computes the input gradient the same way, dx^T[k, m] =
+// sum_n W[n, k] dy[m, n]: the A rows are rows of W^T, so it reads the
+// transposed packing of the weight (codes of W^T, eight consecutive n per
+// word) and, since a row of W^T crosses N different groups, one scale and
+// one bias per element: the transposed scales / biases ([K/64][N], already in
+// the activations' dtype) of the slice's 64 n and the tile's two groups are
+// staged with the words.
 constexpr int kTmTok = 256, kTmFeat = 128, kTmSX = 5, kTmSA = 4;
 
+template <bool BWD>
 struct TmLayout {
-  static constexpr int kX = kTmTok * kBK * 2;         // 32 KB activation slice
-  static constexpr int kW = kTmFeat * 8 * 4;          // 4 KB of packed words
-  static constexpr int kStage = kX + kW;
+  static constexpr int kX = kTmTok * kBK * 2;                   // 32 KB activation slice
+  static constexpr int kW = kTmFeat * 8 * 4;                    // 4 KB of packed words
+  static constexpr int kSB = BWD ? 2 * (2 * kBK * 2) : 0;       // scale + bias boxes
+  static constexpr int kStage = (kX + kW + kSB + 1023) / 1024 * 1024;  // swizzle alignment
   static constexpr int kBytes = kTmSX * kStage + 1024;
   static_assert(kBytes <= 226 * 1024, "shared memory");
 };
@@ -470,13 +480,34 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
       : "memory");
 }
 
-template <typename XT, typename ST>
+// Eight codes of one word with a scale and a bias per pair of values (two
+// consecutive codes): four XT pairs of each in s4 / b4.
+template <typename XT>
+__device__ __forceinline__ uint4 dequant8_pairs(uint32_t w, uint4 s4, uint4 b4) {
+  using PX = typename Pair<XT>::P;
+  const uint32_t w4 = w >> 4;
+  const uint32_t sc[4] = {s4.x, s4.y, s4.z, s4.w}, bc[4] = {b4.x, b4.y, b4.z, b4.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t t = __byte_perm(w, w4, 0x4400u + 0x1111u * (uint32_t)p);
+    uint32_t m;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(m) : "r"(t), "r"(0x000F000Fu), "r"(Pair<XT>::kMagic));
+    const PX v = __hsub2(of_bits<PX>(m), Pair<XT>::offset());
+    o[p] = bits_of(__hfma2(v, of_bits<PX>(sc[p]), of_bits<PX>(bc[p])));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+template <bool BWD, typename XT, typename ST>
 __global__ void __launch_bounds__(kThreads, 1)
-k_qlinear_fwd_tm(const __grid_constant__ CUtensorMap tmap_x,
-                 const __grid_constant__ CUtensorMap tmap_w, const ST* __restrict__ scales,
-                 const ST* __restrict__ biases, const XT* __restrict__ bias,
-                 XT* __restrict__ out, int M, int N, int K) {
-  using L = TmLayout;
+k_qlinear_tm(const __grid_constant__ CUtensorMap tmap_x,
+             const __grid_constant__ CUtensorMap tmap_w,
+             const __grid_constant__ CUtensorMap tmap_st,
+             const __grid_constant__ CUtensorMap tmap_bt, const ST* __restrict__ scales,
+             const ST* __restrict__ biases, const XT* __restrict__ bias,
+             XT* __restrict__ out, int M, int N, int K) {
+  using L = TmLayout<BWD>;
   using PX = typename Pair<XT>::P;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t x_full[kTmSX], x_empty[kTmSX], a_full[kTmSA], a_empty[kTmSA],
@@ -487,10 +518,14 @@ k_qlinear_fwd_tm(const __grid_constant__ CUtensorMap tmap_x,
                                              ~uintptr_t(1023));
   auto sX = [&](int s) { return smem + s * L::kStage; };
   auto sW = [&](int s, int h) { return smem + s * L::kStage + L::kX + h * (L::kW / 2); };
+  auto sS = [&](int s) { return smem + s * L::kStage + L::kX + L::kW; };  // [2][64] scales
+  auto sBi = [&](int s) { return sS(s) + 2 * kBK * 2; };                  // [2][64] biases
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int f0 = blockIdx.x * kTmFeat, m0 = blockIdx.y * kTmTok;  // features, tokens
-  const int KT = K / kBK;
+  // features (rows of W, or of W^T for BWD) and tokens of this tile
+  const int f0 = blockIdx.x * kTmFeat, m0 = blockIdx.y * kTmTok;
+  const int F = BWD ? K : N;                 // output row length
+  const int KT = (BWD ? N : K) / kBK;        // reduction slices
   volatile int* abort_flag = &s_abort;
 
   if (threadIdx.x == 0) {
@@ -525,10 +560,14 @@ k_qlinear_fwd_tm(const __grid_constant__ CUtensorMap tmap_x,
           s_abort = 1;
           break;
         }
-        mbar_arrive_expect_tx(&x_full[s], (unsigned)L::kStage);
+        mbar_arrive_expect_tx(&x_full[s], (unsigned)(L::kX + L::kW + L::kSB));
         tma_2d(sX(s), &tmap_x, it * kBK, m0, &x_full[s]);
         tma_2d(sW(s, 0), &tmap_w, it * 8, f0, &x_full[s]);
         tma_2d(sW(s, 1), &tmap_w, it * 8 + 4, f0, &x_full[s]);
+        if constexpr (BWD) {
+          tma_2d(sS(s), &tmap_st, it * kBK, f0 / kGroup, &x_full[s]);
+          tma_2d(sBi(s), &tmap_bt, it * kBK, f0 / kGroup, &x_full[s]);
+        }
         issued = it + 1;
       }
       if (*abort_flag)
@@ -567,9 +606,11 @@ k_qlinear_fwd_tm(const __grid_constant__ CUtensorMap tmap_x,
     ST sv[kPre], bv[kPre];
 #pragma unroll
     for (int u = 0; u < kPre; ++u) {
-      const size_t i = (size_t)(f0 + f) * G + (u < KT ? u : 0);
-      sv[u] = scales[i];
-      bv[u] = biases[i];
+      if constexpr (!BWD) {
+        const size_t i = (size_t)(f0 + f) * G + (u < KT ? u : 0);
+        sv[u] = scales[i];
+        bv[u] = biases[i];
+      }
     }
     bool stop = false;
     for (int it0 = 0; it0 < KT && !stop; it0 += kPre) {
@@ -578,12 +619,15 @@ k_qlinear_fwd_tm(const __grid_constant__ CUtensorMap tmap_x,
         const int it = it0 + u;
         if (it >= KT) break;
         const int sx = it % kTmSX, sa = it % kTmSA;
-        const PX s2 = Pair<XT>::dup(from_f<XT>(to_f(sv[u])));
-        const PX b2 = Pair<XT>::dup(from_f<XT>(to_f(bv[u])));
-        if (it + kPre < KT) {
-          const size_t i = (size_t)(f0 + f) * G + it + kPre;
-          sv[u] = scales[i];
-          bv[u] = biases[i];
+        PX s2, b2;
+        if constexpr (!BWD) {
+          s2 = Pair<XT>::dup(from_f<XT>(to_f(sv[u])));
+          b2 = Pair<XT>::dup(from_f<XT>(to_f(bv[u])));
+          if (it + kPre < KT) {
+            const size_t i = (size_t)(f0 + f) * G + it + kPre;
+            sv[u] = scales[i];
+            bv[u] = biases[i];
+          }
         }
         if (!wait_or_abort(&x_full[sx], (unsigned)(it / kTmSX) & 1u, abort_flag) ||
             !wait_or_abort(&a_empty[sa], ((unsigned)(it / kTmSA) & 1u) ^ 1u, abort_flag)) {
@@ -598,7 +642,15 @@ k_qlinear_fwd_tm(const __grid_constant__ CUtensorMap tmap_x,
         uint32_t v[16];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const uint4 o = dequant8<XT>(wd[q], s2, b2);
+          uint4 o;
+          if constexpr (BWD) {
+            // scales / biases of n = 32 half + 8 q .. + 7 in this row's group
+            const int ofs = ((f >> 6) * kBK + 32 * half + 8 * q) * 2;
+            o = dequant8_pairs<XT>(wd[q], *reinterpret_cast<const uint4*>(sS(sx) + ofs),
+                                   *reinterpret_cast<const uint4*>(sBi(sx) + ofs));
+          } else {
+            o = dequant8<XT>(wd[q], s2, b2);
+          }
           v[4 * q] = o.x; v[4 * q + 1] = o.y; v[4 * q + 2] = o.z; v[4 * q + 3] = o.w;
         }
         tmem_st16(tmem_a + lane_base + (uint32_t)(sa * 32 + half * 16), v);
@@ -613,7 +665,8 @@ k_qlinear_fwd_tm(const __grid_constant__ CUtensorMap tmap_x,
     // ---- epilogue: y[m, f0 + f] for the warp's 128 tokens
     const bool ok = wait_or_abort(&acc_full, 0u, abort_flag) && !*abort_flag;
     tc_fence_after();
-    const float bf = bias ? to_f(bias[f0 + f]) : 0.f;
+    const bool has_bias = !BWD && bias != nullptr;
+    const float bf = has_bias ? to_f(bias[f0 + f]) : 0.f;
     for (int c0 = half * (kTmTok / 2); c0 < (half + 1) * (kTmTok / 2); c0 += 32) {
       uint32_t r[32];
       tmem_ld32(tmem + lane_base + (uint32_t)c0, r);
@@ -623,8 +676,8 @@ k_qlinear_fwd_tm(const __grid_constant__ CUtensorMap tmap_x,
         if (m < M) {
           float y = ok ? __uint_as_float(r[t]) : __int_as_float(0x7fc00000);
           XT yv = from_f<XT>(y);
-          if (bias) yv = from_f<XT>(to_f(yv) + bf);
-          out[(size_t)m * N + f0 + f] = yv;
+          if (has_bias) yv = from_f<XT>(to_f(yv) + bf);
+          out[(size_t)m * F + f0 + f] = yv;
         }
       }
     }
@@ -714,15 +767,46 @@ int run_qlinear_fwd_tm(const void* x, const uint32_t* wq, const void* scales, co
   r = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, wq, (uint64_t)K / 8, (uint64_t)N,
                (uint64_t)K / 2, 4, kTmFeat, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (r != MHC_OK) return r;
-  auto kern = k_qlinear_fwd_tm<XT, ST>;
-  const size_t smem = TmLayout::kBytes;
+  auto kern = k_qlinear_tm<false, XT, ST>;
+  const size_t smem = TmLayout<false>::kBytes;
   const cudaError_t e = allow_dyn_smem(kern, smem);
   if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "qlinear: %s", cudaGetErrorString(e));
   const dim3 grid(N / kTmFeat, (unsigned)((M + kTmTok - 1) / kTmTok));
-  kern<<<grid, kThreads, smem, st>>>(mx, mw, static_cast<const ST*>(scales),
+  // the scale / bias maps are not read by the forward: pass the weight map
+  kern<<<grid, kThreads, smem, st>>>(mx, mw, mw, mw, static_cast<const ST*>(scales),
                                      static_cast<const ST*>(biases), static_cast<const XT*>(bias),
                                      static_cast<XT*>(out), (int)M, N, K);
   return check_launch("qlinear_fwd");
+}
+
+template <typename XT>
+int run_qlinear_bwd_tm(const void* dy, const uint32_t* wt, const void* scales_t,
+                       const void* biases_t, void* dx, int64_t M, int N, int K, cudaStream_t st) {
+  CUtensorMap md, mw, ms, mb;
+  const CUtensorMapDataType xdt =
+      std::is_same<XT, bf16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  int r = make_map(&md, xdt, dy, (uint64_t)N, (uint64_t)M, (uint64_t)N * 2, kBK, kTmTok,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+  if (r != MHC_OK) return r;
+  // codes of W^T: [K rows][N / 8 words]
+  r = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, wt, (uint64_t)N / 8, (uint64_t)K,
+               (uint64_t)N / 2, 4, kTmFeat, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (r != MHC_OK) return r;
+  // scales / biases of W^T: [K / 64][N] in the activations' dtype
+  r = make_map(&ms, xdt, scales_t, (uint64_t)N, (uint64_t)K / kGroup, (uint64_t)N * 2, kBK, 2,
+               CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (r != MHC_OK) return r;
+  r = make_map(&mb, xdt, biases_t, (uint64_t)N, (uint64_t)K / kGroup, (uint64_t)N * 2, kBK, 2,
+               CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (r != MHC_OK) return r;
+  auto kern = k_qlinear_tm<true, XT, XT>;
+  const size_t smem = TmLayout<true>::kBytes;
+  const cudaError_t e = allow_dyn_smem(kern, smem);
+  if (e != cudaSuccess) return set_error(MHC_ERR_CUDA, "qlinear: %s", cudaGetErrorString(e));
+  const dim3 grid(K / kTmFeat, (unsigned)((M + kTmTok - 1) / kTmTok));
+  kern<<<grid, kThreads, smem, st>>>(md, mw, ms, mb, nullptr, nullptr, nullptr,
+                                     static_cast<XT*>(dx), (int)M, N, K);
+  return check_launch("qlinear_bwd_dx_t");
 }
 
 template <bool BWD, typename XT, typename ST>
@@ -779,6 +863,18 @@ int launch_qlinear_fwd(const void* x, int xdt, const uint32_t* wq, const void* s
   int r = check_args("mhc_qlinear_fwd", x, xdt, wq, scales, biases, sdt, y, M, N, K, group_size, bits);
   if (r != MHC_OK || M == 0) return r;
   return dispatch<false>(x, xdt, wq, scales, biases, sdt, bias, y, M, N, K, st);
+}
+
+int launch_qlinear_bwd_dx_t(const void* dy, int dydt, const uint32_t* wt, const void* scales_t,
+                            const void* biases_t, void* dx, int64_t M, int N, int K,
+                            int group_size, int bits, cudaStream_t st) {
+  int r = check_args("mhc_qlinear_bwd_dx_t", dy, dydt, wt, scales_t, biases_t, dydt, dx, M, N, K,
+                     group_size, bits);
+  if (r != MHC_OK || M == 0) return r;
+  if (!aligned16(scales_t) || !aligned16(biases_t))
+    return set_error(MHC_ERR_INVALID, "mhc_qlinear_bwd_dx_t: scales_t / biases_t must be 16-byte aligned");
+  if (dydt == MHC_BF16) return run_qlinear_bwd_tm<bf16>(dy, wt, scales_t, biases_t, dx, M, N, K, st);
+  return run_qlinear_bwd_tm<f16>(dy, wt, scales_t, biases_t, dx, M, N, K, st);
 }
 
 int launch_qlinear_bwd_dx(const void* dy, int dydt, const uint32_t* wq, const void* scales,

@@ -404,3 +404,18 @@ def qlinear_bwd_dx(dy2, w_packed, scales, biases, in_dims: int, group_size: int,
               C.ptr(_c(scales)), C.ptr(_c(biases)), C.dtype_code(scales.dtype), C.ptr(dx), M, N,
               in_dims, int(group_size), int(bits), C.stream_of(dc))
     return dx
+
+
+def qlinear_bwd_dx_t(dy2, wt_packed, scales_t, biases_t, in_dims: int, group_size: int,
+                     bits: int):
+    """dx[M, K] = dy2[M, N] W from the transposed layouts of the weight (codes
+    of W^T, scales / biases [K/64][N] in dy's dtype): mhc_qlinear_bwd_dx_t."""
+    dev = C.require_cuda(dy2, wt_packed, scales_t, biases_t)
+    M, N = dy2.shape
+    with _on(dev):
+        dc = _c(dy2)
+        dx = torch.empty(M, in_dims, dtype=dc.dtype, device=dev)
+        _call("mhc_qlinear_bwd_dx_t", dc, C.ptr(dc), C.dtype_code(dc.dtype), C.ptr(_c(wt_packed)),
+              C.ptr(_c(scales_t)), C.ptr(_c(biases_t)), C.ptr(dx), M, N, in_dims,
+              int(group_size), int(bits), C.stream_of(dc))
+    return dx

@@ -32,12 +32,13 @@ class _QLinearFn(torch.autograd.Function):
     gives the input gradient only (codes, scales and biases are frozen)."""
 
     @staticmethod
-    def forward(ctx, x, weight, scales, biases, bias, group_size, bits):
+    def forward(ctx, x, weight, scales, biases, bias, group_size, bits, module=None):
         shape = x.shape
         y = K.qlinear_fwd(x.reshape(-1, shape[-1]), weight, scales, biases, bias, group_size,
                           bits)
         ctx.save_for_backward(weight, scales, biases)
         ctx.meta = (shape, x.dtype, group_size, bits)
+        ctx.module = module
         return y.reshape(*shape[:-1], y.shape[-1])
 
     @staticmethod
@@ -47,9 +48,13 @@ class _QLinearFn(torch.autograd.Function):
         dx = None
         if ctx.needs_input_grad[0]:
             dy2 = dy.reshape(-1, dy.shape[-1]).to(dtype)
-            dx = K.qlinear_bwd_dx(dy2, weight, scales, biases, shape[-1], group_size, bits)
+            if ctx.module is not None:
+                wt, st, bt = ctx.module.transposed(dtype)
+                dx = K.qlinear_bwd_dx_t(dy2, wt, st, bt, shape[-1], group_size, bits)
+            else:
+                dx = K.qlinear_bwd_dx(dy2, weight, scales, biases, shape[-1], group_size, bits)
             dx = dx.reshape(shape)
-        return dx, None, None, None, None, None, None
+        return dx, None, None, None, None, None, None, None
 
 
 class QuantizedLinear(nn.Module):
@@ -147,10 +152,30 @@ class QuantizedLinear(nn.Module):
                 and self.output_dims % 128 == 0
                 and self.scales.dtype in (torch.bfloat16, torch.float16))
 
+    def transposed(self, dtype: torch.dtype):
+        """Transposed layouts of the frozen weight for the input-gradient GEMM,
+        built once per activation dtype and cached (rebuilt if a buffer is
+        replaced or modified): the codes of W^T packed like `weight`
+        ([in, out/8] words, eight consecutive output rows per word) and the
+        scales / biases as [in/group, out] in `dtype`.  4-bit codes take
+        in*out/2 bytes: a copy of the packed weight, not a dequantised one."""
+        key = (dtype, self.weight.data_ptr(), self.weight._version, self.scales._version,
+               self.biases._version)
+        cache = getattr(self, "_t_cache", None)
+        if cache is not None and cache[0] == key:
+            return cache[1]
+        with torch.no_grad():
+            q = self.codes().to(torch.uint8)               # [out, in]
+            wt = self.pack(q.t().contiguous(), self.bits)  # [in, out/8]
+            st = self.scales.t().contiguous().to(dtype)    # [in/group, out]
+            bt = self.biases.t().contiguous().to(dtype)
+        self._t_cache = (key, (wt, st, bt))
+        return wt, st, bt
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self._in_kernel(x):
             return _QLinearFn.apply(x, self.weight, self.scales, self.biases, self.bias,
-                                    self.group_size, self.bits)
+                                    self.group_size, self.bits, self)
         w = self.dequantize(dtype=x.dtype)
         y = torch.matmul(x, w.t())
         if self.bias is not None:

@@ -238,7 +238,10 @@ def test_qlinear_kernels_match_dequantized_gemm(M, N, Kd, xdt, sdt):
     W = ql.dequantize(xdt).double()
     y = K.qlinear_fwd(x, ql.weight, ql.scales, ql.biases, None, 64, 4)
     dx = K.qlinear_bwd_dx(dy, ql.weight, ql.scales, ql.biases, Kd, 64, 4)
-    assert y.dtype == xdt and dx.dtype == xdt
+    # the same gradient from the transposed layouts (weights in tensor memory)
+    dx_t = K.qlinear_bwd_dx_t(dy, *ql.transposed(xdt), Kd, 64, 4)
+    assert y.dtype == xdt and dx.dtype == xdt and dx_t.dtype == xdt
+    assert rel_err(dx_t, dy.double() @ W) < (1e-2 if xdt == torch.bfloat16 else 2e-3)
     y_ref = x.double() @ W.T
     dx_ref = dy.double() @ W
     tol = 1e-2 if xdt == torch.bfloat16 else 2e-3
