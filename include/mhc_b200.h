@@ -299,6 +299,11 @@ MHC_API int mhc_qlinear_bwd_dx(const void* dy, int dy_dtype, const uint32_t* w_p
  *              [4(n%8), 4(n%8)+4) of word n/8 (the codes of W^T);
  *   scales_t, biases_t  [K/64][N] in dy's dtype (scales[n][g] at [g][n]).
  * Same coverage as mhc_qlinear_bwd_dx; scales_t / biases_t 16-byte aligned. */
+/* Builds wt_packed ([K][N/8]) from w_packed ([N][K/8]) on the device: the
+ * one-time layout step of mhc_qlinear_bwd_dx_t (no counterpart in the
+ * reference).  N and K multiples of 8. */
+MHC_API int mhc_qlinear_transpose_pack(const uint32_t* w_packed, uint32_t* wt_packed, int N,
+                                       int K, void* stream);
 MHC_API int mhc_qlinear_bwd_dx_t(const void* dy, int dy_dtype, const uint32_t* wt_packed,
                                  const void* scales_t, const void* biases_t, void* dx,
                                  int64_t M, int N, int K, int group_size, int bits,

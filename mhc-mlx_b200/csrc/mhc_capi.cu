@@ -424,6 +424,13 @@ int mhc_qlinear_bwd_dx(const void* dy, int dy_dtype, const uint32_t* w_packed,
   MHC_TRY_END
 }
 
+int mhc_qlinear_transpose_pack(const uint32_t* w_packed, uint32_t* wt_packed, int N, int K,
+                               void* stream) {
+  MHC_TRY_BEGIN
+  return launch_qlinear_transpose_pack(w_packed, wt_packed, N, K, as_stream(stream));
+  MHC_TRY_END
+}
+
 int mhc_qlinear_bwd_dx_t(const void* dy, int dy_dtype, const uint32_t* wt_packed,
                          const void* scales_t, const void* biases_t, void* dx, int64_t M, int N,
                          int K, int group_size, int bits, void* stream) {

@@ -131,6 +131,7 @@ int launch_residual_add_agg_bwd(const void* out, int odt, const void* dout, int 
 int launch_qlinear_fwd(const void* x, int xdt, const uint32_t* wq, const void* scales,
                        const void* biases, int sdt, const void* bias, void* y, int64_t M, int N,
                        int K, int group_size, int bits, cudaStream_t st);
+int launch_qlinear_transpose_pack(const uint32_t* w, uint32_t* wt, int N, int K, cudaStream_t st);
 int launch_qlinear_bwd_dx_t(const void* dy, int dydt, const uint32_t* wt, const void* scales_t,
                             const void* biases_t, void* dx, int64_t M, int N, int K,
                             int group_size, int bits, cudaStream_t st);

@@ -692,6 +692,27 @@ k_qlinear_tm(const __grid_constant__ CUtensorMap tmap_x,
   }
 }
 
+// Transposed packing of 4-bit codes: wt[k][n / 8] holds the codes of rows
+// n .. n + 7 at column k (code j of the word for row n + j), from
+// w[n][k / 8] (code k % 8 of row n).  One output word per thread; a one-time
+// layout build, so the eight scattered reads per word do not matter.
+__global__ void k_transpose_pack4(const uint32_t* __restrict__ w, uint32_t* __restrict__ wt,
+                                  int N, int K) {
+  const int nwords = N / 8;
+  const int64_t total = (int64_t)K * nwords;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int k = (int)(idx / nwords), nw = (int)(idx - (int64_t)k * nwords);
+    uint32_t o = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t word = w[(size_t)(nw * 8 + j) * (K / 8) + k / 8];
+      o |= ((word >> (4 * (k & 7))) & 0xFu) << (4 * j);
+    }
+    wt[idx] = o;
+  }
+}
+
 // ------------------------------------------------------------------ host --
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -863,6 +884,18 @@ int launch_qlinear_fwd(const void* x, int xdt, const uint32_t* wq, const void* s
   int r = check_args("mhc_qlinear_fwd", x, xdt, wq, scales, biases, sdt, y, M, N, K, group_size, bits);
   if (r != MHC_OK || M == 0) return r;
   return dispatch<false>(x, xdt, wq, scales, biases, sdt, bias, y, M, N, K, st);
+}
+
+int launch_qlinear_transpose_pack(const uint32_t* w, uint32_t* wt, int N, int K,
+                                  cudaStream_t st) {
+  if (N < 8 || K < 8 || N % 8 || K % 8)
+    return set_error(MHC_ERR_INVALID, "mhc_qlinear_transpose_pack: N and K must be multiples of 8");
+  if (!w || !wt) return set_error(MHC_ERR_INVALID, "mhc_qlinear_transpose_pack: NULL pointer");
+  const int64_t total = (int64_t)K * (N / 8);
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
+  k_transpose_pack4<<<(int)blocks, 256, 0, st>>>(w, wt, N, K);
+  return check_launch("qlinear_transpose_pack");
 }
 
 int launch_qlinear_bwd_dx_t(const void* dy, int dydt, const uint32_t* wt, const void* scales_t,

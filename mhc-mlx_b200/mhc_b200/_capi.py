@@ -64,6 +64,7 @@ SIGNATURES: dict[str, tuple] = {
                                 c_int, _P]),
     "mhc_qlinear_bwd_dx": (c_int, [_P, c_int, _P, _P, _P, c_int, _P, c_int64, c_int, c_int, c_int,
                                    c_int, _P]),
+    "mhc_qlinear_transpose_pack": (c_int, [_P, _P, c_int, c_int, _P]),
     "mhc_qlinear_bwd_dx_t": (c_int, [_P, c_int, _P, _P, _P, _P, c_int64, c_int, c_int, c_int,
                                      c_int, _P]),
     "mhc_residual_add_agg": (c_int, [_P, c_int, _P, c_int, _P, _P, c_int, _P, c_int64, c_int, c_int,

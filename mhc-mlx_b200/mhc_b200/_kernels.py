@@ -419,3 +419,15 @@ def qlinear_bwd_dx_t(dy2, wt_packed, scales_t, biases_t, in_dims: int, group_siz
               C.ptr(_c(scales_t)), C.ptr(_c(biases_t)), C.ptr(dx), M, N, in_dims,
               int(group_size), int(bits), C.stream_of(dc))
     return dx
+
+
+def qlinear_transpose_pack(w_packed, in_dims: int):
+    """Codes of W^T packed eight per word ([in, out/8] int32) from the layer's
+    [out, in/8] words, on the device (mhc_qlinear_transpose_pack)."""
+    dev = C.require_cuda(w_packed)
+    N = w_packed.shape[0]
+    with _on(dev):
+        wc = _c(w_packed)
+        wt = torch.empty(in_dims, N // 8, dtype=torch.int32, device=dev)
+        _call("mhc_qlinear_transpose_pack", wc, C.ptr(wc), C.ptr(wt), N, in_dims, C.stream_of(wc))
+    return wt

@@ -165,9 +165,8 @@ class QuantizedLinear(nn.Module):
         if cache is not None and cache[0] == key:
             return cache[1]
         with torch.no_grad():
-            q = self.codes().to(torch.uint8)               # [out, in]
-            wt = self.pack(q.t().contiguous(), self.bits)  # [in, out/8]
-            st = self.scales.t().contiguous().to(dtype)    # [in/group, out]
+            wt = K.qlinear_transpose_pack(self.weight, self.input_dims)  # [in, out/8]
+            st = self.scales.t().contiguous().to(dtype)                   # [in/group, out]
             bt = self.biases.t().contiguous().to(dtype)
         self._t_cache = (key, (wt, st, bt))
         return wt, st, bt
