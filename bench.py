@@ -57,7 +57,8 @@ def parse():
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the compact BASELINE config 1-5 records of the default run")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--workload", choices=["layer", "sweep", "sinkhorn", "rewire", "llama", "all"],
+    ap.add_argument("--workload", choices=["layer", "sweep", "sinkhorn", "rewire", "llama", "qmm",
+                                           "all"],
                     default="layer",
                     help="layer = the headline (BASELINE target); the others measure BASELINE "
                          "configs 1-4 and print one JSON line each (1 GPU)")
@@ -849,6 +850,36 @@ def llama_measure(dev, rank, world, steps, warmup):
                                       "all-reduce of the mHC gradients per step"}}
 
 
+def qmm_measure(dev, M, iters=20):
+    """The wrapped 4-bit QuantizedLinear's two GEMMs at BASELINE config 4's
+    shape (4096 -> 4096, group 64, fp16 scales, bf16 activations, M rows):
+    forward and input gradient, weights dequantised inside the kernels."""
+    import mhc_b200
+    from mhc_b200 import _kernels as K
+
+    peak = 1590.0
+    if (ROOT / "MEASURED_PEAKS.json").exists():
+        peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("bf16_tflops", peak)
+    g = torch.Generator().manual_seed(4)
+    ql = mhc_b200.QuantizedLinear.random(4096, 4096, group_size=64, bits=4, dtype=torch.float16,
+                                         generator=g).to(dev)
+    x = torch.randn(M, 4096, device=dev).to(torch.bfloat16)
+    dy = torch.randn(M, 4096, device=dev).to(torch.bfloat16)
+    wt, st, bt = ql.transposed(torch.bfloat16)
+    flops = 2 * M * 4096 * 4096
+    fwd = _median_us(lambda: K.qlinear_fwd(x, ql.weight, ql.scales, ql.biases, None, 64, 4), dev,
+                     iters, 3)
+    bwd = _median_us(lambda: K.qlinear_bwd_dx_t(dy, wt, st, bt, 4096, 64, 4), dev, iters, 3)
+    return {"metric": "QuantizedLinear 4096x4096 4-bit GEMMs, weight dequantised in-kernel",
+            "unit": "us", "higher_is_better": False, "M": M,
+            "fwd_us": fwd, "fwd_tflops": flops / (fwd * 1e-6) / 1e12,
+            "bwd_dx_us": bwd, "bwd_dx_tflops": flops / (bwd * 1e-6) / 1e12,
+            "peak_bf16_tflops": peak,
+            "config": {"workload": "BASELINE config 4 wrapped layer: group 64, fp16 scales / "
+                                   "biases, bf16 activations, random codes",
+                       "note": "median of CUDA-event times per call"}}
+
+
 def run_configs(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -874,6 +905,8 @@ def run_configs(args):
     if w in ("rewire", "all"):
         out.append(config1_quickstart(dev))
         out.append(config4_rewire(dev, peak, peak_kind))
+    if w in ("qmm", "all"):
+        out.append(qmm_measure(dev, args.tokens if args.tokens != 65536 else 8192))
     for r in out:
         print(json.dumps(r), flush=True)
 
