@@ -88,6 +88,21 @@ __device__ __forceinline__ void load_vec(const T* __restrict__ p, float (&o)[V])
   }
 }
 
+// Two fp32 values rounded to nearest-even into one packed pair of 16-bit T
+// (one paired conversion instead of two single ones; the same bits).
+template <typename T>
+__device__ __forceinline__ unsigned pack2_16(float a, float b) {
+  unsigned u;
+  if constexpr (std::is_same<T, bf16>::value) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    u = *reinterpret_cast<unsigned*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(a, b);
+    u = *reinterpret_cast<unsigned*>(&h);
+  }
+  return u;
+}
+
 // Store V fp32 values as T.  For T = float with V = 8 (half input, fp32
 // output) two float4 stores are issued.
 template <typename T, int V, bool Stream = true>
@@ -110,16 +125,16 @@ __device__ __forceinline__ void store_vec(T* __restrict__ p, const float (&v)[V]
     *reinterpret_cast<unsigned*>(p) = u;  // 4-byte aligned
   } else if constexpr (V == 4) {
     uint2 u;
-    T* h = reinterpret_cast<T*>(&u);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) h[k] = from_f<T>(v[k]);
+    u.x = pack2_16<T>(v[0], v[1]);
+    u.y = pack2_16<T>(v[2], v[3]);
     *reinterpret_cast<uint2*>(p) = u;
   } else {
     static_assert(V == 8, "16-bit store width is 2, 4 or 8");
     uint4 u;
-    T* h = reinterpret_cast<T*>(&u);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) h[k] = from_f<T>(v[k]);
+    u.x = pack2_16<T>(v[0], v[1]);
+    u.y = pack2_16<T>(v[2], v[3]);
+    u.z = pack2_16<T>(v[4], v[5]);
+    u.w = pack2_16<T>(v[6], v[7]);
     if constexpr (Stream) __stcs(reinterpret_cast<uint4*>(p), u);
     else *reinterpret_cast<uint4*>(p) = u;
   }

@@ -417,50 +417,54 @@ k_rewire_bwd_x_fast(const XT* __restrict__ x, const DT* __restrict__ dout,
 #pragma unroll
     for (int j = 0; j < N; ++j) aQ[i][j] = 0.f;
   }
+  // (token, column group) of linear item q = thread + k * stride, stepped
+  // incrementally: no per-item 64-bit division
   const int groups = C / VEC;
-  const int64_t items = T * groups;
-  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < items;
-       q += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = q / groups;
-    const int col = (int)(q - t * groups) * VEC;
-    const int64_t base = t * (int64_t)N * C + col;
-    float xr[N][VEC], o[N][VEC];
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t q0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t t = q0 / groups;
+  int g = (int)(q0 - t * groups);
+  const int64_t dt = stride / groups;
+  const int dg = (int)(stride - dt * groups);
+  for (; t < T;) {
+    const int64_t base = t * (int64_t)N * C + (int64_t)g * VEC;
+    // every load of the item first, then the arithmetic
+    float xr[N][VEC], dr[N][VEC], pv[N][VEC];
 #pragma unroll
-    for (int j = 0; j < N; ++j) {
-      load_vec<XT, VEC>(x + base + (int64_t)j * C, xr[j]);
+    for (int j = 0; j < N; ++j) load_vec<XT, VEC>(x + base + (int64_t)j * C, xr[j]);
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) o[j][v] = 0.f;
-    }
+    for (int i = 0; i < N; ++i) load_vec<DT, VEC>(dout + base + (int64_t)i * C, dr[i]);
+    if (dp) {
 #pragma unroll
-    for (int i = 0; i < N; ++i) {
-      float dr[VEC];
-      load_vec<DT, VEC>(dout + base + (int64_t)i * C, dr);
+      for (int j = 0; j < N; ++j) load_vec<PT, VEC>(dp + base + (int64_t)j * C, pv[j]);
+    } else {
 #pragma unroll
       for (int j = 0; j < N; ++j)
 #pragma unroll
-        for (int v = 0; v < VEC; ++v) aQ[i][j] = fmaf(dr[v], xr[j][v], aQ[i][j]);
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        const float z = hpost[i] * dr[v];
-#pragma unroll
-        for (int j = 0; j < N; ++j) o[j][v] = fmaf(sM[i * N + j], z, o[j][v]);
-      }
+        for (int v = 0; v < VEC; ++v) pv[j][v] = 0.f;
     }
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+#pragma unroll
+      for (int j = 0; j < N; ++j)
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) aQ[i][j] = fmaf(dr[i][v], xr[j][v], aQ[i][j]);
 #pragma unroll
     for (int j = 0; j < N; ++j) {
-      if (dp) {
-        float pv[VEC];
-        load_vec<PT, VEC>(dp + base + (int64_t)j * C, pv);
+      float o[VEC];
 #pragma unroll
-        for (int v = 0; v < VEC; ++v) {
-          aS[j] = fmaf(pv[v], xr[j][v], aS[j]);
-          o[j][v] += pv[v];
-        }
+      for (int v = 0; v < VEC; ++v) {
+        aS[j] = fmaf(pv[j][v], xr[j][v], aS[j]);
+        float a = pv[j][v];
+#pragma unroll
+        for (int i = 0; i < N; ++i) a = fmaf(sM[i * N + j] * hpost[i], dr[i][v], a);
+        o[v] = a * hpre[j];
       }
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) o[j][v] *= hpre[j];
-      if (dx) store_vec<XT, VEC>(dx + base + (int64_t)j * C, o[j]);
+      if (dx) store_vec<XT, VEC>(dx + base + (int64_t)j * C, o);
     }
+    g += dg;
+    t += dt;
+    if (g >= groups) { g -= groups; ++t; }
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
 #pragma unroll
@@ -979,6 +983,8 @@ static int rewire_x_t(const void* xv, const void* dv, const void* pv, const floa
                       const float* hpre, const float* hpost, void* dxv, int64_t T, int n, int C,
                       void* ws, cudaStream_t st) {
   constexpr int VX = VecOf<XT>::value;
+  // 4 columns per item: all of an item's loads fit in registers at once
+  constexpr int V4 = 4;
   const XT* x = static_cast<const XT*>(xv);
   const DT* d = static_cast<const DT*>(dv);
   const PT* p = static_cast<const PT*>(pv);
@@ -989,9 +995,9 @@ static int rewire_x_t(const void* xv, const void* dv, const void* pv, const floa
   const int cap = mix_rows_cap();
   const bool vec = (C % VX == 0) && all_aligned({xv, dv, pv, dxv});
   if (vec && (n == 1 || n == 2 || n == 4)) {
-    const int G = elem_grid(T * (C / VX), cap);
+    const int G = elem_grid(T * (C / V4), cap);
 #define MHC_RX(NN) \
-  k_rewire_bwd_x_fast<NN, XT, DT, PT, VX><<<G, kMixBD, 0, st>>>(x, d, p, M, hpre, hpost, dx, T, C, wp, hdr)
+  k_rewire_bwd_x_fast<NN, XT, DT, PT, V4><<<G, kMixBD, 0, st>>>(x, d, p, M, hpre, hpost, dx, T, C, wp, hdr)
     if (n == 1) MHC_RX(1);
     else if (n == 2) MHC_RX(2);
     else MHC_RX(4);
