@@ -62,7 +62,7 @@ def _worker_equivalence(rank, world, port, q):
         for p, gr in zip(mhc_parameters(layer), grads):
             p.grad = gr.float()
         allreduce_grads(mhc_parameters(layer))
-        q.put((rank, xs.shape[0], [p.grad.clone() for p in mhc_parameters(layer)]))
+        q.put((rank, xs.shape[0], [p.grad.tolist() for p in mhc_parameters(layer)]))
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:  # report instead of hanging the parent
@@ -89,7 +89,7 @@ def test_sharded_allreduce_matches_full_batch():
     full = O.layer_grads(x, *params, d, 20, 1e-5, dtype=torch.float64)[2:]
     for r in res:
         for a, b in zip(r[2], full):
-            assert torch.allclose(a.double(), b, rtol=1e-5, atol=1e-6)
+            assert torch.allclose(torch.tensor(a).double(), b, rtol=1e-5, atol=1e-6)
 
 
 def _worker_bucket(rank, world, port, q):
@@ -119,7 +119,9 @@ def _worker_bucket(rank, world, port, q):
         want[3] = torch.zeros_like(want[3])
         got = [p.grad.clone() for p in ps]
         views_ok = all(p.grad.data_ptr() == v.data_ptr() for p, v in zip(ps, bucket.views))
-        q.put((rank, views_ok, got, want))
+        # plain lists: a worker's tensors would be shared by file descriptor and
+        # the worker may exit before the parent reads them
+        q.put((rank, views_ok, [g.tolist() for g in got], [w.tolist() for w in want]))
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:  # report instead of hanging the parent
@@ -141,7 +143,7 @@ def test_grad_bucket_allreduce_matches_gather_scatter():
         assert views_ok, got
         # parameter 3 has no gradient on either rank in the bucket run: zeros
         for k, (a, b) in enumerate(zip(got, want)):
-            assert torch.allclose(a, b), k
+            assert torch.allclose(torch.tensor(a), torch.tensor(b)), k
 
 
 def _worker_dead_peer(rank, world, port, q):
