@@ -767,6 +767,29 @@ def config4_rewire(dev, peak, peak_kind):
     gemm = {k: v for k, v in per4.items() if k.startswith("mhc_qlinear")}
     per4 = {k: v for k, v in per4.items() if k not in gemm}
     mk4 = sum(per4.values())
+    # the same mHC kernel sequence of one step (parameter kernel, pre-scale,
+    # combine, dy side, x side + finalize, parameter backward) on the same
+    # shapes and dtypes, replayed from a CUDA graph: device time without the
+    # host gaps of eager launches (the inner GEMM's output and input gradient
+    # are stand-in tensors of its shapes)
+    from mhc_b200 import _kernels as K
+
+    mh = model4.mhc
+    x3 = x4.detach().view(8192, 4, 1024)
+    y3 = torch.randn(8192, 4, 1024, device=dev).to(torch.bfloat16)
+    p3 = torch.randn(8192, 4, 1024, device=dev).to(torch.bfloat16)
+    d3 = d4.view(8192, 4, 1024)
+
+    def mhc_only():
+        hpre, hpost, M, tape = K.params_fwd(mh.H_pre_raw, mh.H_post_raw, mh.H_res_raw, 20, 1e-5,
+                                            want_tape=True)
+        K.prescale_fwd(x3, hpre)
+        K.rewire_fwd(x3, y3, M, hpre, hpost, torch.float32)
+        _, state = K.rewire_bwd_dy(y3, d3, hpost)
+        _, dM, dpre, dpost = K.rewire_bwd_dx(x3, p3, M, hpre, hpost, state)
+        K.params_bwd(mh.H_pre_raw, mh.H_post_raw, mh.H_res_raw, tape, 20, 1e-5, dpre, dpost, dM)
+
+    mk4_graph = _graph_us(mhc_only, dev)
     step_us = _median_us(fb4, dev, iters=30, warm=3)
     gemm_flops = 2 * 8192 * 4096 * 4096
     # algorithmic bytes of the mHC kernels per step (bf16 x / y_inner / dy / d_xpre /
@@ -777,11 +800,13 @@ def config4_rewire(dev, peak, peak_kind):
     mbytes = elems * ((2 + 2) + (2 + 2 + 4) + (2 + 4 + 2) + (2 + 4 + 2 + 2))
     return {"metric": "MHCRewire(QuantizedLinear 4096, n=4) mHC fwd+bwd tokens/s, GEMM "
                       "excluded (BASELINE config 4)",
-            "value": 8192 / (mk4 * 1e-6), "unit": "tokens/s", "higher_is_better": True,
+            "value": 8192 / (mk4_graph * 1e-6), "unit": "tokens/s", "higher_is_better": True,
+            "mhc_kernels_graph_us": mk4_graph,
             "mhc_kernels_us": mk4, "mhc_kernels": per4,
             "mhc_algorithmic_bytes": mbytes,
-            "mhc_achieved_gbs": mbytes / (mk4 * 1e-6) / 1e9, "peak": peak,
-            "frac": mbytes / (mk4 * 1e-6) / 1e9 / peak,
+            "mhc_achieved_gbs": mbytes / (mk4_graph * 1e-6) / 1e9, "peak": peak,
+            "frac": mbytes / (mk4_graph * 1e-6) / 1e9 / peak,
+            "frac_eager_events": mbytes / (mk4 * 1e-6) / 1e9 / peak,
             "whole_step_us_incl_gemm": step_us,
             "gemm_in_kernel_dequant": {
                 k: {"us": v, "tflops": gemm_flops / (v * 1e-6) / 1e12,
@@ -790,8 +815,10 @@ def config4_rewire(dev, peak, peak_kind):
             "config": {"workload": "8192 bf16 tokens, 4-bit affine QuantizedLinear "
                                    "(group 64, fp16 scales / biases), random codes",
                        "peak_source": f"{peak_kind} hbm_gbs",
-                       "note": "mhc_kernels_us = sum of CUDA-event durations around each "
-                               "mHC C-ABI call (the two Sinkhorn parameter kernels included)"}}
+                       "note": "mhc_kernels_graph_us = one step's mHC kernels (the two "
+                               "Sinkhorn parameter kernels included) replayed from a CUDA "
+                               "graph; mhc_kernels_us = CUDA events around each eager C-ABI "
+                               "call of the real step (includes host gaps)"}}
 
 
 def llama_measure(dev, rank, world, steps, warmup):
@@ -952,7 +979,8 @@ def secondary_configs(dev, rank, world, peak, peak_kind, llama_steps=3):
                                              ("value", "unit", "fwd_us", "bwd_us")}
         c4 = config4_rewire(dev, peak, peak_kind)
         out["secondary_config4_rewire_q4"] = {
-            k: c4[k] for k in ("value", "unit", "mhc_kernels_us", "mhc_achieved_gbs", "frac",
+            k: c4[k] for k in ("value", "unit", "mhc_kernels_graph_us", "mhc_kernels_us",
+                               "mhc_achieved_gbs", "frac", "frac_eager_events",
                                "whole_step_us_incl_gemm", "mhc_kernels",
                                "gemm_in_kernel_dequant")}
         torch.cuda.empty_cache()
