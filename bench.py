@@ -767,11 +767,11 @@ def config4_rewire(dev, peak, peak_kind):
     gemm = {k: v for k, v in per4.items() if k.startswith("mhc_qlinear")}
     per4 = {k: v for k, v in per4.items() if k not in gemm}
     mk4 = sum(per4.values())
-    # the same mHC kernel sequence of one step (parameter kernel, pre-scale,
-    # combine, dy side, x side + finalize, parameter backward) on the same
-    # shapes and dtypes, replayed from a CUDA graph: device time without the
-    # host gaps of eager launches (the inner GEMM's output and input gradient
-    # are stand-in tensors of its shapes)
+    # the same mHC kernel sequence of one step (parameters + pre-scale,
+    # combine, dy side, x side + finalize with the parameter backward) on the
+    # same shapes and dtypes, replayed from a CUDA graph: device time without
+    # the host gaps of eager launches (the inner GEMM's output and input
+    # gradient are stand-in tensors of its shapes)
     from mhc_b200 import _kernels as K
 
     mh = model4.mhc
@@ -781,13 +781,11 @@ def config4_rewire(dev, peak, peak_kind):
     d3 = d4.view(8192, 4, 1024)
 
     def mhc_only():
-        hpre, hpost, M, tape = K.params_fwd(mh.H_pre_raw, mh.H_post_raw, mh.H_res_raw, 20, 1e-5,
-                                            want_tape=True)
-        K.prescale_fwd(x3, hpre)
+        _, hpre, hpost, M, raw = K.rewire_in_fwd(x3, mh.H_pre_raw, mh.H_post_raw, mh.H_res_raw,
+                                                 mh.sinkhorn_iters, mh.eps)
         K.rewire_fwd(x3, y3, M, hpre, hpost, torch.float32)
         _, state = K.rewire_bwd_dy(y3, d3, hpost)
-        _, dM, dpre, dpost = K.rewire_bwd_dx(x3, p3, M, hpre, hpost, state)
-        K.params_bwd(mh.H_pre_raw, mh.H_post_raw, mh.H_res_raw, tape, 20, 1e-5, dpre, dpost, dM)
+        K.rewire_bwd_dx(x3, p3, M, hpre, hpost, state, raw=raw)
 
     mk4_graph = _graph_us(mhc_only, dev)
     step_us = _median_us(fb4, dev, iters=30, warm=3)
@@ -815,9 +813,9 @@ def config4_rewire(dev, peak, peak_kind):
             "config": {"workload": "8192 bf16 tokens, 4-bit affine QuantizedLinear "
                                    "(group 64, fp16 scales / biases), random codes",
                        "peak_source": f"{peak_kind} hbm_gbs",
-                       "note": "mhc_kernels_graph_us = one step's mHC kernels (the two "
-                               "Sinkhorn parameter kernels included) replayed from a CUDA "
-                               "graph; mhc_kernels_us = CUDA events around each eager C-ABI "
+                       "note": "mhc_kernels_graph_us = one step's mHC kernels (the "
+                               "Sinkhorn parameter forward and backward included) replayed "
+                               "from a CUDA graph; mhc_kernels_us = CUDA events around each eager C-ABI "
                                "call of the real step (includes host gaps)"}}
 
 

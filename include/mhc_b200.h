@@ -231,8 +231,35 @@ MHC_API int mhc_rewire_bwd_dx(const void* x, int x_dtype, const void* d_out, int
                               const void* d_xpre, int dxpre_dtype, const float* M,
                               const float* H_pre_act, const float* H_post_act, void* dx,
                               int dx_dtype, float* dM, float* dH_pre_act, float* dH_post_act,
-                              int64_t T, int n, int C, void* workspace,
-                              size_t workspace_bytes, void* stream);
+                              const float* H_pre_raw, const float* H_post_raw,
+                              const float* H_res_raw, const float* tape,
+                              const float* jacobian, int iters, float eps, float* dH_pre_raw,
+                              float* dH_post_raw, float* dH_res_raw, int64_t T, int n, int C,
+                              void* workspace, size_t workspace_bytes, void* stream);
+/* The raw-parameter arguments of mhc_rewire_bwd_dx carry the chain rule on
+ * to H_pre_raw / H_post_raw / H_res_raw (what mhc_params_bwd does with the
+ * activation gradients) in the same finalize launch: pass the raw parameters,
+ * the tape of mhc_rewire_in_fwd or mhc_params_fwd, the forward's iters and
+ * eps, and three outputs; all NULL to stop at the activation gradients.
+ * jacobian (nullable, n <= 4): the one mhc_rewire_in_fwd wrote, turning the
+ * Sinkhorn backward into n^2 dot products. */
+
+/* ---- MHCRewire input side ----------------------------------------------------
+ * layer.py:474-480 (MHCRewire.__call__: the wrapped MHCLayer's activations,
+ * then x * H_pre_act) in one call:
+ *   H_pre_act, H_post_act, M and the tape exactly as mhc_params_fwd;
+ *   x_pre[t,i,c] = x[t,i,c] * H_pre_act[i]  (as mhc_prescale_fwd).
+ * For n in {1, 2, 4, 8} this is one launch: one block runs the parameter chain
+ * while the others pre-scale.  Otherwise the parameter kernel, then the
+ * pre-scale.  jacobian (nullable; n in {1, 2, 4} only,
+ * mhc_rewire_jacobian_floats(n) floats) receives the transposed Jacobian
+ * dM/dH_res_raw for mhc_rewire_bwd_dx; tape is required when iters > 0. */
+MHC_API size_t mhc_rewire_jacobian_floats(int n);
+MHC_API int mhc_rewire_in_fwd(const void* x, int x_dtype, const float* H_pre_raw,
+                              const float* H_post_raw, const float* H_res_raw, int iters,
+                              float eps, float* H_pre_act, float* H_post_act, float* M,
+                              float* tape, float* jacobian, void* x_pre, int out_dtype,
+                              int64_t T, int n, int C, void* stream);
 
 /* ---- stream pre-scale (MHCRewire input side) ------------------------------
  * layer.py:478-480: x_pre[t,i,c] = x[t,i,c] * H_pre_act[i].  Backward:

@@ -11,6 +11,7 @@
 #include <tuple>
 
 #include "mhc_internal.h"
+#include "mhc_sinkhorn.cuh"
 
 namespace mhc {
 
@@ -362,7 +363,10 @@ int mhc_rewire_bwd_dy(const void* y_inner, int y_dtype, const void* d_out, int d
 int mhc_rewire_bwd_dx(const void* x, int x_dtype, const void* d_out, int dout_dtype,
                       const void* d_xpre, int dxpre_dtype, const float* M, const float* H_pre_act,
                       const float* H_post_act, void* dx, int dx_dtype, float* dM,
-                      float* dH_pre_act, float* dH_post_act, int64_t T, int n, int C,
+                      float* dH_pre_act, float* dH_post_act, const float* H_pre_raw,
+                      const float* H_post_raw, const float* H_res_raw, const float* tape,
+                      const float* jacobian, int iters, float eps, float* dH_pre_raw,
+                      float* dH_post_raw, float* dH_res_raw, int64_t T, int n, int C,
                       void* workspace, size_t workspace_bytes, void* stream) {
   MHC_TRY_BEGIN
   MHC_CHK(check_common(__func__, T, n, C));
@@ -373,9 +377,44 @@ int mhc_rewire_bwd_dx(const void* x, int x_dtype, const void* d_out, int dout_dt
   MHC_REQ(M && H_pre_act && H_post_act, "%s: NULL parameter pointer", __func__);
   MHC_REQ(dM && dH_pre_act && dH_post_act, "%s: NULL gradient pointer", __func__);
   MHC_REQ(T == 0 || (x && d_out), "%s: NULL tensor pointer", __func__);
+  MHC_REQ(!H_pre_raw == !dH_pre_raw, "%s: H_pre_raw and dH_pre_raw must both be given or both NULL", __func__);
+  MHC_REQ(!H_post_raw == !dH_post_raw, "%s: H_post_raw and dH_post_raw must both be given or both NULL", __func__);
+  MHC_REQ(!H_res_raw == !dH_res_raw, "%s: H_res_raw and dH_res_raw must both be given or both NULL", __func__);
+  if (H_res_raw) {
+    MHC_REQ(iters >= 0, "%s: iters=%d must be >= 0", __func__, iters);
+    MHC_REQ(tape || jacobian || iters == 0, "%s: tape is NULL (record it with mhc_rewire_in_fwd)", __func__);
+  }
+  MHC_REQ(!jacobian || sk_lane_ok(n), "%s: a Jacobian exists for n in {1, 2, 4} only (n=%d)", __func__, n);
+  const ParamsBwd pb{H_pre_raw, H_post_raw, H_res_raw, tape, jacobian, iters, eps,
+                     dH_pre_raw, dH_post_raw, dH_res_raw};
   return launch_rewire_bwd_dx(x, x_dtype, d_out, dout_dtype, d_xpre, dxpre_dtype, M, H_pre_act,
-                              H_post_act, dx, dx_dtype, dM, dH_pre_act, dH_post_act, T, n, C,
+                              H_post_act, dx, dx_dtype, dM, dH_pre_act, dH_post_act, pb, T, n, C,
                               workspace, workspace_bytes, as_stream(stream));
+  MHC_TRY_END
+}
+
+size_t mhc_rewire_jacobian_floats(int n) {
+  if (n < 1 || n > 64) return 0;
+  return sk_jacobian_floats(n);
+}
+
+int mhc_rewire_in_fwd(const void* x, int x_dtype, const float* H_pre_raw, const float* H_post_raw,
+                      const float* H_res_raw, int iters, float eps, float* H_pre_act,
+                      float* H_post_act, float* M, float* tape, float* jacobian, void* x_pre,
+                      int out_dtype, int64_t T, int n, int C, void* stream) {
+  MHC_TRY_BEGIN
+  MHC_CHK(check_common(__func__, T, n, C));
+  MHC_CHK(check_dtype(__func__, "x", x_dtype));
+  MHC_CHK(check_dtype(__func__, "x_pre", out_dtype));
+  MHC_REQ(iters >= 0, "%s: iters=%d must be >= 0", __func__, iters);
+  MHC_REQ(H_pre_raw && H_post_raw && H_res_raw, "%s: NULL raw parameter pointer", __func__);
+  MHC_REQ(H_pre_act && H_post_act && M, "%s: NULL activation pointer", __func__);
+  MHC_REQ(tape || iters == 0, "%s: tape is NULL", __func__);
+  MHC_REQ(!jacobian || sk_lane_ok(n), "%s: a Jacobian exists for n in {1, 2, 4} only (n=%d)", __func__, n);
+  MHC_REQ(T == 0 || (x && x_pre), "%s: NULL tensor pointer", __func__);
+  const ParamsFwd pf{H_pre_raw, H_post_raw, H_res_raw, iters, eps, H_pre_act, H_post_act, M,
+                     tape, jacobian};
+  return launch_rewire_in_fwd(x, x_dtype, pf, x_pre, out_dtype, T, n, C, as_stream(stream));
   MHC_TRY_END
 }
 

@@ -64,6 +64,36 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 int max_partial_rows(int64_t T);
 
 // ---- Sinkhorn / parameters (mhc_sinkhorn.cu) ----------------------------
+// The parameter forward folded into another launch: raw parameters in, the
+// activations, M, the Sinkhorn tape and (nullable, n <= 4) the transposed
+// Jacobian of M out.
+struct ParamsFwd {
+  const float* hpre_raw;
+  const float* hpost_raw;
+  const float* hres_raw;
+  int iters;
+  float eps;
+  float* hpre;
+  float* hpost;
+  float* M;
+  float* tape;
+  float* jac;
+};
+// The parameter backward folded into a finalize: raw parameters, the
+// forward's tape / Jacobian, and the raw gradients (all null: not folded).
+struct ParamsBwd {
+  const float* hpre_raw;
+  const float* hpost_raw;
+  const float* hres_raw;
+  const float* tape;
+  const float* jac;
+  int iters;
+  float eps;
+  float* dhpre_raw;
+  float* dhpost_raw;
+  float* dhres_raw;
+  __host__ __device__ bool any() const { return dhpre_raw || dhpost_raw || dhres_raw; }
+};
 size_t sk_tape_floats(int n, int iters);
 int launch_selftest_reciprocal(const float* x, float* y, int64_t count, cudaStream_t st);
 int launch_params_fwd(const float* hpre_raw, const float* hpost_raw, const float* hres_raw,
@@ -112,10 +142,12 @@ int launch_rewire_bwd_dy(const void* y, int ydt, const void* d, int ddt, const f
                          cudaStream_t st);
 int launch_rewire_bwd_dx(const void* x, int xdt, const void* d, int ddt, const void* p, int pdt,
                          const float* M, const float* hpre, const float* hpost, void* dx, int dxdt,
-                         float* dM, float* dhpre, float* dhpost, int64_t T, int n, int C, void* ws,
-                         size_t ws_bytes, cudaStream_t st);
+                         float* dM, float* dhpre, float* dhpost, const ParamsBwd& pb, int64_t T,
+                         int n, int C, void* ws, size_t ws_bytes, cudaStream_t st);
 int launch_prescale_fwd(const void* x, int xdt, const float* hpre, void* xo, int odt, int64_t T,
                         int n, int C, cudaStream_t st);
+int launch_rewire_in_fwd(const void* x, int xdt, const ParamsFwd& pf, void* xo, int odt, int64_t T,
+                         int n, int C, cudaStream_t st);
 int launch_prescale_bwd(const void* x, int xdt, const void* d, int ddt, const float* hpre,
                         void* dx, int dxdt, float* dhpre, int64_t T, int n, int C, void* ws,
                         size_t ws_bytes, cudaStream_t st);

@@ -1556,76 +1556,8 @@ k_finalize(const char* __restrict__ ws, int n, int C, float* __restrict__ dM,
     }
     __syncthreads();
   }
-  if (tid < n) {
-    if (hpre_raw && dhpre_raw) {
-      const float s = sigmoidf_(hpre_raw[tid]);
-      dhpre_raw[tid] = sP[n * n + tid] * (1.0f - s) * s;
-    }
-    if (hpost_raw && dhpost_raw) {
-      const float s = sigmoidf_(hpost_raw[tid]);
-      dhpost_raw[tid] = (2.0f * sP[n * n + n + tid]) * (1.0f - s) * s;
-    }
-  }
-  if (hres_raw && dhres_raw && (tape || iters == 0)) {
-    if (sk_warp_ok(n)) {
-      // one call site per address space of the tape (shared when staged,
-      // global otherwise), so its loads are not generic
-      auto run = [&](const float* Hs, const float* Ts) {
-        if (sk_lane_ok(n)) {
-          if (tid < 32) {
-            MHC_SK_LANE_SWITCH(n, ({
-              const bool act = tid < SK_N * SK_N;
-              const float d = sk_backward_lane<SK_N>(Hs, Ts, iters, eps, act ? sP[tid] : 0.f);
-              if (act) dhres_raw[tid] = d;
-            }))
-          }
-          return;
-        }
-        if (tid < 32) {
-          const int row = tid % n;
-          MHC_SK_WARP_SWITCH(n, ({
-            float d[SK_N];
-            for (int j = 0; j < SK_N; ++j) d[j] = sP[row * SK_N + j];
-            sk_backward_warp<SK_N>(Hs, Ts, iters, eps, d);
-            if (tid < SK_N)
-              for (int j = 0; j < SK_N; ++j) dhres_raw[row * SK_N + j] = d[j];
-          }))
-        }
-      };
-      if (stage_sk) {  // dynamic shared memory holds [tape | logits]
-        const size_t tf = (size_t)iters * sk_tape_stride(n);
-#pragma unroll 8
-        for (size_t e = tid; e < tf; e += BD) s_fin[e] = tape[e];
-        for (int e = tid; e < n * n; e += BD) s_fin[tf + e] = hres_raw[e];
-        __syncthreads();
-        run(s_fin + tf, s_fin);
-      } else {
-        run(hres_raw, tape);
-      }
-      return;
-    }
-    if (sk_elem_ok(n)) {  // BD threads: n^2 / BD entries per thread
-      MHC_SK_ELEM_SWITCH(n, ({
-        if constexpr (SK_N * SK_N >= BD) {  // the launcher pairs BD = 1024 with n = 32 only
-          if (stage_sk) {
-            const SkTape tp = sk_stage_tape_fixed<SK_N>(tape, iters, s_fin);
-            __syncthreads();  // staged tape complete
-            sk_backward_elem<SK_N, BD>(hres_raw, tp, iters, eps, sP, D, dhres_raw);
-          } else {
-            sk_backward_elem<SK_N, BD>(hres_raw, SkTape{tape, SK_N, sk_tape_stride(SK_N)},
-                                       iters, eps, sP, D, dhres_raw);
-          }
-        }
-      }))
-      return;
-    }
-    const SkTape tp = stage_sk ? sk_stage_tape(tape, n, iters, s_fin)
-                               : SkTape{tape, n, sk_tape_stride(n)};
-    const int ld = sk_ld(n);
-    for (int e = tid; e < n * n; e += BD) D[(e / n) * ld + e % n] = sP[e];
-    __syncthreads();
-    sk_backward_block(hres_raw, tp, n, iters, eps, D, dhres_raw);
-  }
+  sk_params_bwd_tail<BD>(sP, n, hpre_raw, hpost_raw, hres_raw, tape, nullptr, iters, eps,
+                         stage_sk, s_fin, D, dhpre_raw, dhpost_raw, dhres_raw);
 }
 
 // ================================================================= launch ==

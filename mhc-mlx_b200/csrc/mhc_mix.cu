@@ -34,6 +34,7 @@
 
 #include "mhc_common.cuh"
 #include "mhc_internal.h"
+#include "mhc_sinkhorn.cuh"
 
 namespace mhc {
 
@@ -98,18 +99,49 @@ k_combine_fwd(const XT* __restrict__ x, const YT* __restrict__ y, const float* _
 }
 
 // ----------------------------------------------------------- prescale fwd --
-template <int MAXN, bool EXACT, typename XT, typename OT, int VEC>
-__global__ void __launch_bounds__(kMixBD)
+// PARAMS (MHCRewire's input side, n in {1, 2, 4, 8}): the parameter kernel
+// rides along as block 0 -- sigmoids, the Sinkhorn forward with its tape and,
+// for n <= 4, the transposed Jacobian of M (sk_jacobian_lane) -- while blocks
+// 1.. pre-scale with H_pre_act = sigmoid(H_pre_raw) evaluated in-block by the
+// same function (the same bits block 0 stores).  The one-warp latency chain
+// of the Sinkhorn iterations then overlaps the streaming instead of
+// preceding it.
+template <int MAXN, bool EXACT, typename XT, typename OT, int VEC, bool PARAMS = false>
+__global__ void __launch_bounds__(kMixBD, PARAMS ? 8 : 1)  // PARAMS: keep 8 blocks per SM
 k_prescale_fwd(const XT* __restrict__ x, const float* __restrict__ hpre_g, OT* __restrict__ xo,
-               int64_t T, int n, int C) {
+               int64_t T, int n, int C, ParamsFwd pf) {
   __shared__ float shpre[MAXN];
   const int nr = EXACT ? MAXN : n;
-  for (int e = threadIdx.x; e < nr; e += blockDim.x) shpre[e] = hpre_g[e];
+  int b0 = 0;
+  if constexpr (PARAMS) {
+    static_assert(EXACT && MAXN <= 8, "the parameter block runs the one-warp Sinkhorn paths");
+    if (blockIdx.x == 0) {
+      const int tid = threadIdx.x;
+      if (tid < MAXN) {
+        pf.hpre[tid] = sigmoidf_(pf.hpre_raw[tid]);
+        pf.hpost[tid] = 2.0f * sigmoidf_(pf.hpost_raw[tid]);
+      }
+      if constexpr (MAXN <= 4) {
+        if (tid < 32) sk_forward_lane<MAXN>(pf.hres_raw, pf.iters, pf.eps, pf.tape, pf.M);
+        if (pf.jac) {  // kernel argument: uniform over the block
+          __syncthreads();  // tape stored
+          sk_jacobian_lane<MAXN>(pf.hres_raw, pf.tape, pf.iters, pf.eps, pf.jac);
+        }
+      } else {
+        if (tid < 32) sk_forward_warp<MAXN>(pf.hres_raw, pf.iters, pf.eps, pf.tape, pf.M);
+      }
+      return;
+    }
+    b0 = 1;
+    for (int e = threadIdx.x; e < nr; e += blockDim.x) shpre[e] = sigmoidf_(pf.hpre_raw[e]);
+  } else {
+    for (int e = threadIdx.x; e < nr; e += blockDim.x) shpre[e] = hpre_g[e];
+  }
   __syncthreads();
   const int groups = (C + VEC - 1) / VEC;
   const int64_t items = T * groups;
-  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < items;
-       q += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t q = (int64_t)(blockIdx.x - b0) * blockDim.x + threadIdx.x; q < items;
+       q += (int64_t)(gridDim.x - b0) * blockDim.x) {
     const int64_t t = q / groups;
     const int col = (int)(q - t * groups) * VEC;
     const int64_t base = t * (int64_t)nr * C + col;
@@ -609,6 +641,10 @@ k_residual_bwd(const OT* __restrict__ out, const DT* __restrict__ dout,
 //   mode 2 (prescale): dhpre = R
 //   mode 3 (rewire end to end): as mode 1 with dhpre_j += S_j; the rows of
 //                      both passes are summed (header words 0 and 2)
+// and, in modes 1 and 3 with pb.any(), carries on to the raw-parameter
+// gradients (sigmoid chain rule, Sinkhorn backward: sk_params_bwd_tail) in
+// the same launch.  Dynamic shared memory: [D (n * sk_ld(n)) | staged tape],
+// D only for n > 8 without a Jacobian, the staged tape only when stage_sk.
 // Thread t sums entry e = t % EW of a block of EW consecutive entries over the
 // interleaved row slice t / EW (slice r takes rows r, r + S, ...; S = 1024 /
 // EW slices), then the slices are added in order: a fixed order for a given
@@ -621,9 +657,12 @@ constexpr int kCFinBD = 1024;
 __global__ void __launch_bounds__(kCFinBD)
 k_combine_finalize(const char* __restrict__ ws, int n, const float* __restrict__ M,
                    const float* __restrict__ hpre, const float* __restrict__ hpost, int mode,
-                   float* __restrict__ dM, float* __restrict__ dhpre, float* __restrict__ dhpost) {
+                   float* __restrict__ dM, float* __restrict__ dhpre, float* __restrict__ dhpost,
+                   ParamsBwd pb, int stage_sk) {
   __shared__ float sQ[kMaxN * kMaxN + 2 * kMaxN];
+  __shared__ float sA[kMaxN * kMaxN + 2 * kMaxN];  // [dM | dhpre | dhpost] for the tail
   __shared__ float part[kCFinBD];
+  extern __shared__ float s_dyn[];
   const int* hdr = reinterpret_cast<const int*>(ws);
   const int G = mode == 3 ? hdr[0] + hdr[2] : hdr[0];
   const int P = n * n + 2 * n;
@@ -636,7 +675,7 @@ k_combine_finalize(const char* __restrict__ ws, int n, const float* __restrict__
     const int e = e0 + el;
     float s = 0.f;
     if (e < E && r0 < S) {
-#pragma unroll 4
+#pragma unroll 8
       for (int g = r0; g < G; g += S) s += wp[(size_t)g * P + e];
     }
     part[threadIdx.x] = s;
@@ -651,25 +690,37 @@ k_combine_finalize(const char* __restrict__ ws, int n, const float* __restrict__
   const float* sR = sQ + n * n;
   if (mode == 0) {
     for (int e = threadIdx.x; e < n * n; e += blockDim.x) dM[e] = sQ[e];
-  } else if (mode == 2) {
-    for (int e = threadIdx.x; e < n; e += blockDim.x) dhpre[e] = sR[e];
-  } else {
-    for (int e = threadIdx.x; e < n * n; e += blockDim.x) {
-      const int i = e / n, j = e % n;
-      if (dM) dM[e] = (hpost[i] * hpre[j]) * sQ[e];
-    }
-    for (int j = threadIdx.x; j < n; j += blockDim.x) {
-      float s = 0.f;
-      for (int i = 0; i < n; ++i) s = fmaf(hpost[i] * M[i * n + j], sQ[i * n + j], s);
-      if (mode == 3) s += sR[n + j];
-      if (dhpre) dhpre[j] = s;
-    }
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      float s = sR[i];
-      for (int j = 0; j < n; ++j) s = fmaf(M[i * n + j] * hpre[j], sQ[i * n + j], s);
-      if (dhpost) dhpost[i] = s;
-    }
+    return;
   }
+  if (mode == 2) {
+    for (int e = threadIdx.x; e < n; e += blockDim.x) dhpre[e] = sR[e];
+    return;
+  }
+  for (int e = threadIdx.x; e < n * n; e += blockDim.x) {
+    const int i = e / n, j = e % n;
+    const float v = (hpost[i] * hpre[j]) * sQ[e];
+    sA[e] = v;
+    if (dM) dM[e] = v;
+  }
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    float s = 0.f;
+    for (int i = 0; i < n; ++i) s = fmaf(hpost[i] * M[i * n + j], sQ[i * n + j], s);
+    if (mode == 3) s += sR[n + j];
+    sA[n * n + j] = s;
+    if (dhpre) dhpre[j] = s;
+  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float s = sR[i];
+    for (int j = 0; j < n; ++j) s = fmaf(M[i * n + j] * hpre[j], sQ[i * n + j], s);
+    sA[n * n + n + i] = s;
+    if (dhpost) dhpost[i] = s;
+  }
+  if (!pb.any()) return;  // kernel argument: uniform over the block
+  __syncthreads();        // sA complete
+  const bool dreg = !sk_warp_ok(n) && !pb.jac;
+  sk_params_bwd_tail<kCFinBD>(sA, n, pb.hpre_raw, pb.hpost_raw, pb.hres_raw, pb.tape, pb.jac,
+                              pb.iters, pb.eps, stage_sk, s_dyn + (dreg ? n * sk_ld(n) : 0), s_dyn,
+                              pb.dhpre_raw, pb.dhpost_raw, pb.dhres_raw);
 }
 
 // ================================================================= launch ==
@@ -834,7 +885,7 @@ static int combine_bwd(const void* x, int xdt, const void* y, int ydt, const voi
   }
   if (r != MHC_OK) return r;
   k_combine_finalize<<<1, kCFinBD, 0, st>>>(static_cast<const char*>(ws), n, M, hpre, hpost, mode,
-                                        dM, dhpre, dhpost);
+                                            dM, dhpre, dhpost, ParamsBwd{}, 0);
   return check_launch("combine_finalize");
 }
 
@@ -856,15 +907,27 @@ int launch_rewire_bwd(const void* x, int xdt, const void* y, int ydt, const void
 // ---- pre-scale -----------------------------------------------------------------
 template <typename XT, typename OT>
 static int prescale_fwd_t(const void* xv, const float* hpre, void* ov, int64_t T, int n, int C,
-                          cudaStream_t st) {
+                          const ParamsFwd* pf, cudaStream_t st) {
   constexpr int VX = VecOf<XT>::value;
   const XT* x = static_cast<const XT*>(xv);
   OT* o = static_cast<OT*>(ov);
   const bool vec = (C % VX == 0) && all_aligned({xv, ov});
   const int cap = sm_count() * 8;
   const int gv = elem_grid(T * (C / VX), cap), g1 = elem_grid(T * C, cap);
+  if (pf) {  // n in {1, 2, 4, 8}: one more block for the parameters
+#define MHC_PP(NN, V, G) \
+  k_prescale_fwd<NN, true, XT, OT, V, true><<<G + 1, kMixBD, 0, st>>>(x, nullptr, o, T, n, C, *pf)
+    switch (n) {
+      case 1: if (vec) MHC_PP(1, VX, gv); else MHC_PP(1, 1, g1); break;
+      case 2: if (vec) MHC_PP(2, VX, gv); else MHC_PP(2, 1, g1); break;
+      case 4: if (vec) MHC_PP(4, VX, gv); else MHC_PP(4, 1, g1); break;
+      default: if (vec) MHC_PP(8, VX, gv); else MHC_PP(8, 1, g1); break;
+    }
+#undef MHC_PP
+    return check_launch("rewire_in_fwd");
+  }
 #define MHC_PF(NN, EX, V, G) \
-  k_prescale_fwd<NN, EX, XT, OT, V><<<G, kMixBD, 0, st>>>(x, hpre, o, T, n, C)
+  k_prescale_fwd<NN, EX, XT, OT, V><<<G, kMixBD, 0, st>>>(x, hpre, o, T, n, C, ParamsFwd{})
   switch (n) {
     case 1: if (vec) MHC_PF(1, true, VX, gv); else MHC_PF(1, true, 1, g1); break;
     case 2: if (vec) MHC_PF(2, true, VX, gv); else MHC_PF(2, true, 1, g1); break;
@@ -878,20 +941,38 @@ static int prescale_fwd_t(const void* xv, const float* hpre, void* ov, int64_t T
   return check_launch("prescale_fwd");
 }
 
-int launch_prescale_fwd(const void* x, int xdt, const float* hpre, void* xo, int odt, int64_t T,
-                        int n, int C, cudaStream_t st) {
-  if (T == 0) return MHC_OK;
+static int prescale_fwd_any(const void* x, int xdt, const float* hpre, void* xo, int odt,
+                            int64_t T, int n, int C, const ParamsFwd* pf, cudaStream_t st) {
   if (odt != xdt && odt != MHC_F32)
     return set_error(MHC_ERR_UNSUPPORTED, "prescale: out dtype must be fp32 or x's dtype");
   switch (xdt) {
-    case MHC_F32: return prescale_fwd_t<float, float>(x, hpre, xo, T, n, C, st);
+    case MHC_F32: return prescale_fwd_t<float, float>(x, hpre, xo, T, n, C, pf, st);
     case MHC_BF16:
-      return odt == MHC_F32 ? prescale_fwd_t<bf16, float>(x, hpre, xo, T, n, C, st)
-                            : prescale_fwd_t<bf16, bf16>(x, hpre, xo, T, n, C, st);
+      return odt == MHC_F32 ? prescale_fwd_t<bf16, float>(x, hpre, xo, T, n, C, pf, st)
+                            : prescale_fwd_t<bf16, bf16>(x, hpre, xo, T, n, C, pf, st);
     default:
-      return odt == MHC_F32 ? prescale_fwd_t<f16, float>(x, hpre, xo, T, n, C, st)
-                            : prescale_fwd_t<f16, f16>(x, hpre, xo, T, n, C, st);
+      return odt == MHC_F32 ? prescale_fwd_t<f16, float>(x, hpre, xo, T, n, C, pf, st)
+                            : prescale_fwd_t<f16, f16>(x, hpre, xo, T, n, C, pf, st);
   }
+}
+
+int launch_prescale_fwd(const void* x, int xdt, const float* hpre, void* xo, int odt, int64_t T,
+                        int n, int C, cudaStream_t st) {
+  if (T == 0) return MHC_OK;
+  return prescale_fwd_any(x, xdt, hpre, xo, odt, T, n, C, nullptr, st);
+}
+
+// MHCRewire's input side: parameters + pre-scale in one launch for n <= 8
+// (the one-warp Sinkhorn paths), else the parameter kernel and then the
+// pre-scale.  The Jacobian is written for n <= 4 when pf.jac is given.
+int launch_rewire_in_fwd(const void* x, int xdt, const ParamsFwd& pf, void* xo, int odt, int64_t T,
+                         int n, int C, cudaStream_t st) {
+  if (sk_warp_ok(n))  // T = 0 too: the parameter block still runs
+    return prescale_fwd_any(x, xdt, nullptr, xo, odt, T, n, C, &pf, st);
+  int r = launch_params_fwd(pf.hpre_raw, pf.hpost_raw, pf.hres_raw, n, pf.iters, pf.eps, pf.hpre,
+                            pf.hpost, pf.M, pf.tape, st);
+  if (r != MHC_OK || T == 0) return r;
+  return prescale_fwd_any(x, xdt, pf.hpre, xo, odt, T, n, C, nullptr, st);
 }
 
 template <typename XT, typename DT>
@@ -944,8 +1025,8 @@ int launch_prescale_bwd(const void* x, int xdt, const void* d, int ddt, const fl
       break;
   }
   if (r != MHC_OK) return r;
-  k_combine_finalize<<<1, kCFinBD, 0, st>>>(static_cast<const char*>(ws), n, nullptr, nullptr, nullptr,
-                                        2, nullptr, dhpre, nullptr);
+  k_combine_finalize<<<1, kCFinBD, 0, st>>>(static_cast<const char*>(ws), n, nullptr, nullptr,
+                                            nullptr, 2, nullptr, dhpre, nullptr, ParamsBwd{}, 0);
   return check_launch("prescale_finalize");
 }
 
@@ -1031,8 +1112,8 @@ static int rewire_x_x(const void* x, int xdt, const void* d, int ddt, const void
 
 int launch_rewire_bwd_dx(const void* x, int xdt, const void* d, int ddt, const void* p, int pdt,
                          const float* M, const float* hpre, const float* hpost, void* dx, int dxdt,
-                         float* dM, float* dhpre, float* dhpost, int64_t T, int n, int C, void* ws,
-                         size_t ws_bytes, cudaStream_t st) {
+                         float* dM, float* dhpre, float* dhpost, const ParamsBwd& pb, int64_t T,
+                         int n, int C, void* ws, size_t ws_bytes, cudaStream_t st) {
   const size_t need = rewire_fused_ws_bytes(T, n, C);
   if (!ws || ws_bytes < need)
     return set_error(MHC_ERR_WORKSPACE, "rewire bwd: workspace %zu < %zu bytes", ws_bytes, need);
@@ -1044,9 +1125,33 @@ int launch_rewire_bwd_dx(const void* x, int xdt, const void* d, int ddt, const v
     default: r = rewire_x_x<f16>(x, xdt, d, ddt, p, pdt, M, hpre, hpost, dx, T, n, C, ws, st); break;
   }
   if (r != MHC_OK) return r;
-  k_combine_finalize<<<1, kCFinBD, 0, st>>>(static_cast<const char*>(ws), n, M, hpre, hpost, 3,
-                                            dM, dhpre, dhpost);
-  return check_launch("rewire_bwd_finalize");
+  // The raw-parameter chain rule runs in the finalize when its thread count
+  // suits the Sinkhorn path of n, else as the separate parameter kernel on
+  // the activation gradients the finalize wrote.
+  const bool fold = pb.any() && sk_tail_ok(n, kCFinBD);
+  size_t dyn = 0;
+  int stage = 0;
+  if (fold && !pb.jac && pb.hres_raw && pb.dhres_raw && pb.tape) {
+    if (!sk_warp_ok(n)) dyn += (size_t)n * sk_ld(n) * sizeof(float);
+    const size_t sb = sk_stage_floats(n, pb.iters) * sizeof(float);
+    if (dyn + sb <= 150 * 1024) {
+      dyn += sb;
+      stage = 1;
+    }
+  } else if (fold && !pb.jac && !sk_warp_ok(n)) {
+    dyn = (size_t)n * sk_ld(n) * sizeof(float);
+  }
+  {
+    const cudaError_t e = allow_dyn_smem(k_combine_finalize, dyn);
+    if (e != cudaSuccess)
+      return set_error(MHC_ERR_CUDA, "rewire_bwd_finalize: %s", cudaGetErrorString(e));
+  }
+  k_combine_finalize<<<1, kCFinBD, dyn, st>>>(static_cast<const char*>(ws), n, M, hpre, hpost, 3,
+                                              dM, dhpre, dhpost, fold ? pb : ParamsBwd{}, stage);
+  r = check_launch("rewire_bwd_finalize");
+  if (r != MHC_OK || !pb.any() || fold) return r;
+  return launch_params_bwd(pb.hpre_raw, pb.hpost_raw, pb.hres_raw, pb.tape, n, pb.iters, pb.eps,
+                           dhpre, dhpost, dM, pb.dhpre_raw, pb.dhpost_raw, pb.dhres_raw, st);
 }
 
 // ---- residual add + aggregate ----------------------------------------------------
@@ -1152,8 +1257,8 @@ int launch_residual_add_agg_bwd(const void* out, int odt, const void* dout, int 
     default: r = residual_bwd_o<f16>(out, dout, ddt, dy, hpre, dx, dxdt, T, n, C, ws, st, odt); break;
   }
   if (r != MHC_OK) return r;
-  k_combine_finalize<<<1, kCFinBD, 0, st>>>(static_cast<const char*>(ws), n, nullptr, nullptr, nullptr,
-                                        2, nullptr, dhpre, nullptr);
+  k_combine_finalize<<<1, kCFinBD, 0, st>>>(static_cast<const char*>(ws), n, nullptr, nullptr,
+                                            nullptr, 2, nullptr, dhpre, nullptr, ParamsBwd{}, 0);
   return check_launch("residual_add_agg_bwd_finalize");
 }
 

@@ -306,19 +306,29 @@ __device__ __forceinline__ void sk_forward_lane(const float* __restrict__ H, int
 
 // d: this lane's entry of dM on entry, of dH_res on exit.  The next
 // iteration's tape entries are loaded before the current one is processed.
-template <int N>
+// PACKED: every lane group of NN lanes runs its own cotangent on entry le =
+// lane % NN (the reductions already stay inside a group), and the tape is
+// read through L2 because the same kernel wrote it (sk_jacobian_lane).
+template <int N, bool PACKED = false>
 __device__ __forceinline__ float sk_backward_lane(const float* __restrict__ H,
                                                   const float* __restrict__ tape, int iters,
                                                   float eps, float d) {
   constexpr int NN = N * N, TS = NN + 2 * N;
   const int lane = threadIdx.x & 31;
-  const bool act = lane < NN;
+  const int le = PACKED ? lane % NN : lane;
+  const bool act = PACKED || lane < NN;
   const int i = (lane / N) % N, j = lane % N;
   auto ld = [&](int k, float& pa, float& r, float& c) {
     const float* tk = tape + (size_t)k * TS;
-    pa = act ? tk[lane] : 0.f;
-    r = tk[NN + i];
-    c = tk[NN + N + j];
+    if constexpr (PACKED) {
+      pa = __ldcg(tk + le);
+      r = __ldcg(tk + NN + i);
+      c = __ldcg(tk + NN + N + j);
+    } else {
+      pa = act ? tk[lane] : 0.f;
+      r = tk[NN + i];
+      c = tk[NN + N + j];
+    }
   };
   float pa = 0.f, r = 0.f, c = 0.f;
   if (iters > 0) ld(iters - 1, pa, r, c);
@@ -335,12 +345,35 @@ __device__ __forceinline__ float sk_backward_lane(const float* __restrict__ H,
     c = cn;
   }
   // exp and the row-max shift (the max's gradient is split over ties)
-  const float h = act ? H[lane] : 0.f;
+  const float h = act ? H[le] : 0.f;
   const float m = sk_row_max<N>(h);
   d *= expf(h - m);
   const float S = group_sum<N>(d);
   const float cnt = group_sum<N>(h == m ? 1.f : 0.f);
   return d - (h == m ? S / cnt : 0.f);
+}
+
+// Transposed Jacobian of the lane-path Sinkhorn at H (n in {1, 2, 4}), from
+// the tape this kernel wrote (visible to the block: the caller syncs first).
+// The backward is linear in dM, so running it on the unit cotangents e_u
+// gives A[u][e] = d(M_u)/d(H_e) and, later, dH_res = sum_u dM[u] A[u][:] as
+// a dot product instead of a reverse sweep (a latency chain of 2 iters
+// dependent reductions).  Lane group g of warp w takes u = w (32 / NN) + g:
+// for n = 4 the 16 cotangents are one pass of 8 warps.
+template <int N>
+__device__ __forceinline__ void sk_jacobian_lane(const float* __restrict__ H,
+                                                 const float* tape, int iters, float eps,
+                                                 float* __restrict__ A) {
+  constexpr int NN = N * N, GPW = 32 / NN;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int u0 = warp * GPW; u0 < NN; u0 += nw * GPW) {  // warp-uniform
+    const int u = u0 + lane / NN, le = lane % NN;
+    const float d = sk_backward_lane<N, true>(H, tape, iters, eps, le == u ? 1.f : 0.f);
+    if (u < NN) A[u * NN + le] = d;
+  }
+}
+__host__ __device__ inline size_t sk_jacobian_floats(int n) {
+  return sk_lane_ok(n) ? (size_t)n * n * n * n : 0;
 }
 
 // Expand BODY with SK_N = n for the element-per-lane path (n in {1, 2, 4}).
@@ -535,6 +568,114 @@ __host__ __device__ inline size_t sk_stage_floats(int n, int iters) {
 }
 __host__ __device__ inline int sk_threads(int n) {
   return sk_warp_ok(n) ? 32 : sk_elem_ok(n) ? n * n : 32 * (n < 32 ? n : 32);
+}
+
+// ---------------------------------------------------------------------------
+// Raw-parameter gradients at the end of a one-CTA backward finalize, from the
+// activation gradients G = [dM (n*n) | dH_pre_act (n) | dH_post_act (n)] in
+// shared memory (filled and synced by the caller):
+//   dH_pre_raw  = dH_pre_act sigma' (H_pre_act = sigmoid(H_pre_raw))
+//   dH_post_raw = 2 dH_post_act sigma' (H_post_act = 2 sigmoid(H_post_raw))
+//   dH_res_raw  = Sinkhorn backward of dM: with jac (n <= 4, written by
+//                 sk_jacobian_lane) the dot products sum_u dM[u] jac[u][:],
+//                 else the reverse sweep through the tape.
+// Every one of the BD threads calls it (the sweeps synchronise the block);
+// sk_tail_ok(n, BD) must hold.  stage_sk: copy [tape | logits] into s_fin
+// (dynamic shared memory of sk_stage_floats(n, iters) floats) first.  D:
+// shared [n][sk_ld(n)] scratch.  Null outputs are skipped.
+__host__ __device__ inline bool sk_tail_ok(int n, int bd) { return !sk_elem_ok(n) || n * n >= bd; }
+
+template <int BD>
+__device__ inline void sk_params_bwd_tail(const float* G, int n, const float* __restrict__ hpre_raw,
+                                          const float* __restrict__ hpost_raw,
+                                          const float* __restrict__ hres_raw,
+                                          const float* __restrict__ tape,
+                                          const float* __restrict__ jac, int iters, float eps,
+                                          int stage_sk, float* s_fin, float* D,
+                                          float* __restrict__ dhpre_raw,
+                                          float* __restrict__ dhpost_raw,
+                                          float* __restrict__ dhres_raw) {
+  const int tid = threadIdx.x;
+  if (tid < n) {
+    // d/da sigmoid(a) = s (1 - s)
+    if (hpre_raw && dhpre_raw) {
+      const float s = sigmoidf_(hpre_raw[tid]);
+      dhpre_raw[tid] = G[n * n + tid] * (1.0f - s) * s;
+    }
+    if (hpost_raw && dhpost_raw) {
+      const float s = sigmoidf_(hpost_raw[tid]);
+      dhpost_raw[tid] = (2.0f * G[n * n + n + tid]) * (1.0f - s) * s;
+    }
+  }
+  if (!hres_raw || !dhres_raw) return;
+  if (jac) {
+    const int nn = n * n;
+    for (int e = tid; e < nn; e += BD) {
+      float s = 0.f;
+      for (int u = 0; u < nn; ++u) s = fmaf(G[u], jac[u * nn + e], s);
+      dhres_raw[e] = s;
+    }
+    return;
+  }
+  if (!tape && iters > 0) return;
+  if (sk_warp_ok(n)) {
+    // one call site per address space of the tape (shared when staged,
+    // global otherwise), so its loads are not generic
+    auto run = [&](const float* Hs, const float* Ts) {
+      if (sk_lane_ok(n)) {
+        if (tid < 32) {
+          MHC_SK_LANE_SWITCH(n, ({
+            const bool act = tid < SK_N * SK_N;
+            const float d = sk_backward_lane<SK_N>(Hs, Ts, iters, eps, act ? G[tid] : 0.f);
+            if (act) dhres_raw[tid] = d;
+          }))
+        }
+        return;
+      }
+      if (tid < 32) {
+        const int row = tid % n;
+        MHC_SK_WARP_SWITCH(n, ({
+          float d[SK_N];
+          for (int j = 0; j < SK_N; ++j) d[j] = G[row * SK_N + j];
+          sk_backward_warp<SK_N>(Hs, Ts, iters, eps, d);
+          if (tid < SK_N)
+            for (int j = 0; j < SK_N; ++j) dhres_raw[row * SK_N + j] = d[j];
+        }))
+      }
+    };
+    if (stage_sk) {  // s_fin holds [tape | logits]
+      const size_t tf = (size_t)iters * sk_tape_stride(n);
+#pragma unroll 8
+      for (size_t e = tid; e < tf; e += BD) s_fin[e] = tape[e];
+      for (int e = tid; e < n * n; e += BD) s_fin[tf + e] = hres_raw[e];
+      __syncthreads();
+      run(s_fin + tf, s_fin);
+    } else {
+      run(hres_raw, tape);
+    }
+    return;
+  }
+  if (sk_elem_ok(n)) {  // BD threads: n^2 / BD entries per thread
+    MHC_SK_ELEM_SWITCH(n, ({
+      if constexpr (SK_N * SK_N >= BD) {
+        if (stage_sk) {
+          const SkTape tp = sk_stage_tape_fixed<SK_N>(tape, iters, s_fin);
+          __syncthreads();  // staged tape complete
+          sk_backward_elem<SK_N, BD>(hres_raw, tp, iters, eps, G, D, dhres_raw);
+        } else {
+          sk_backward_elem<SK_N, BD>(hres_raw, SkTape{tape, SK_N, sk_tape_stride(SK_N)}, iters,
+                                     eps, G, D, dhres_raw);
+        }
+      }
+    }))
+    return;
+  }
+  const SkTape tp = stage_sk ? sk_stage_tape(tape, n, iters, s_fin)
+                             : SkTape{tape, n, sk_tape_stride(n)};
+  const int ld = sk_ld(n);
+  for (int e = tid; e < n * n; e += BD) D[(e / n) * ld + e % n] = G[e];
+  __syncthreads();
+  sk_backward_block(hres_raw, tp, n, iters, eps, D, dhres_raw);
 }
 
 }  // namespace mhc

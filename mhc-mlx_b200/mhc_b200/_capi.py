@@ -56,7 +56,11 @@ SIGNATURES: dict[str, tuple] = {
     "mhc_rewire_bwd_dy": (c_int, [_P, c_int, _P, c_int, _P, _P, c_int, c_int64, c_int, c_int, _P,
                                   c_size_t, _P]),
     "mhc_rewire_bwd_dx": (c_int, [_P, c_int, _P, c_int, _P, c_int, _P, _P, _P, _P, c_int, _P, _P,
-                                  _P, c_int64, c_int, c_int, _P, c_size_t, _P]),
+                                  _P, _P, _P, _P, _P, _P, c_int, c_float, _P, _P, _P, c_int64,
+                                  c_int, c_int, _P, c_size_t, _P]),
+    "mhc_rewire_jacobian_floats": (c_size_t, [c_int]),
+    "mhc_rewire_in_fwd": (c_int, [_P, c_int, _P, _P, _P, c_int, c_float, _P, _P, _P, _P, _P, _P,
+                                  c_int, c_int64, c_int, c_int, _P]),
     "mhc_prescale_fwd": (c_int, [_P, c_int, _P, _P, c_int, c_int64, c_int, c_int, _P]),
     "mhc_prescale_bwd": (c_int, [_P, c_int, _P, c_int, _P, _P, c_int, _P, c_int64, c_int, c_int, _P,
                                  c_size_t, _P]),

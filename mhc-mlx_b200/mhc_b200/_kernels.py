@@ -291,10 +291,15 @@ def rewire_bwd_dy(y, dout, hpost):
     return dy, (ws, nb, dc)
 
 
-def rewire_bwd_dx(x, d_xpre, M, hpre, hpost, state, want_dx: bool = True):
+def rewire_bwd_dx(x, d_xpre, M, hpre, hpost, state, want_dx: bool = True, raw=None):
     """Second half (after the inner module's backward gave d_xpre, or None):
     dx written once, and dM, dH_pre_act (both branches), dH_post_act from one
-    reduction.  `state` is what rewire_bwd_dy returned."""
+    reduction.  `state` is what rewire_bwd_dy returned.
+
+    raw = (H_pre_raw, H_post_raw, H_res_raw, tape, jacobian, iters, eps), as
+    rewire_in_fwd returned them: the same launch carries on to the raw
+    gradients, and (dx, dH_pre_raw, dH_post_raw, dH_res_raw) is returned
+    instead of (dx, dM, dH_pre_act, dH_post_act)."""
     ws, nb, dc = state
     dev = C.require_cuda(x, d_xpre, M, hpre, hpost)
     T, n, Cc = x.shape
@@ -304,15 +309,55 @@ def rewire_bwd_dx(x, d_xpre, M, hpre, hpost, state, want_dx: bool = True):
         if d_xpre is not None:
             pc = _c(d_xpre) if d_xpre.dtype in (F32, xc.dtype) else d_xpre.float().contiguous()
         dx = torch.empty(T, n, Cc, dtype=xc.dtype, device=dev) if want_dx else None
-        dM = torch.empty(n, n, dtype=F32, device=dev)
-        dpre = torch.empty(n, dtype=F32, device=dev)
-        dpost = torch.empty(n, dtype=F32, device=dev)
+        nn = n * n
+        # one buffer for the activation gradients [dM | dpre | dpost] and one
+        # for the raw gradients [dres | dpre_raw | dpost_raw]
+        act = torch.empty(nn + 2 * n, dtype=F32, device=dev)
+        dM, dpre, dpost = act[:nn].view(n, n), act[nn:nn + n], act[nn + n:]
+        rargs = (None,) * 5 + (0, 0.0) + (None,) * 3
+        if raw is not None:
+            pre, post, res, tape, jac, iters, eps = raw
+            g = torch.empty(nn + 2 * n, dtype=F32, device=dev)
+            gres, gpre, gpost = g[:nn].view(n, n), g[nn:nn + n], g[nn + n:]
+            rargs = (C.ptr(pre), C.ptr(post), C.ptr(res), C.ptr(tape), C.ptr(jac), int(iters),
+                     float(eps), C.ptr(gpre), C.ptr(gpost), C.ptr(gres))
         _call("mhc_rewire_bwd_dx", xc, C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(dc),
               C.dtype_code(dc.dtype), C.ptr(pc), C.dtype_code(pc.dtype if pc is not None else F32),
               C.ptr(_f32(M)), C.ptr(_f32(hpre)), C.ptr(_f32(hpost)), C.ptr(dx),
-              C.dtype_code(xc.dtype), C.ptr(dM), C.ptr(dpre), C.ptr(dpost), T, n, Cc, C.ptr(ws), nb,
-              C.stream_of(xc))
+              C.dtype_code(xc.dtype), C.ptr(dM), C.ptr(dpre), C.ptr(dpost), *rargs, T, n, Cc,
+              C.ptr(ws), nb, C.stream_of(xc))
+    if raw is not None:
+        return dx, gpre, gpost, gres
     return dx, dM, dpre, dpost
+
+
+@functools.lru_cache(maxsize=64)
+def jacobian_floats(n: int) -> int:
+    return int(C.query("mhc_rewire_jacobian_floats", n))
+
+
+def rewire_in_fwd(x, H_pre_raw, H_post_raw, H_res_raw, iters: int, eps: float, out_dtype=None):
+    """MHCRewire's input side in one launch for n <= 8: the activations, M,
+    the Sinkhorn tape and (n <= 4) the Jacobian of M, and x_pre = x * H_pre_act.
+    Returns (x_pre, hpre, hpost, M, raw) with raw the tuple rewire_bwd_dx takes."""
+    dev = C.require_cuda(x, H_pre_raw, H_post_raw, H_res_raw)
+    T, n, Cc = x.shape
+    with _on(dev):
+        xc = _io(x)
+        odt = out_dtype or xc.dtype
+        pre, post, res = _f32(H_pre_raw), _f32(H_post_raw), _f32(H_res_raw)
+        nn, tf, jf = n * n, tape_floats(n, iters), jacobian_floats(n)
+        # one buffer: [M | hpre | hpost | tape | jacobian]
+        buf = torch.empty(nn + 2 * n + tf + jf, dtype=F32, device=dev)
+        M, hpre, hpost = buf[:nn].view(n, n), buf[nn:nn + n], buf[nn + n:nn + 2 * n]
+        o = nn + 2 * n
+        tape = buf[o:o + tf] if tf else None
+        jac = buf[o + tf:o + tf + jf] if jf else None
+        out = torch.empty(T, n, Cc, dtype=odt, device=dev)
+        _call("mhc_rewire_in_fwd", xc, C.ptr(xc), C.dtype_code(xc.dtype), C.ptr(pre), C.ptr(post),
+              C.ptr(res), int(iters), float(eps), C.ptr(hpre), C.ptr(hpost), C.ptr(M),
+              C.ptr(tape), C.ptr(jac), C.ptr(out), C.dtype_code(odt), T, n, Cc, C.stream_of(xc))
+    return out, hpre, hpost, M, (pre, post, res, tape, jac, int(iters), float(eps))
 
 
 def prescale_fwd(x, hpre, out_dtype=None) -> torch.Tensor:

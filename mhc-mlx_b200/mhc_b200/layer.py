@@ -102,31 +102,57 @@ class _RewireLink:
         self.state = None
 
 
-class _PrescaleFn(torch.autograd.Function):
-    """x_pre[t, i, c] = x[t, i, c] * H_pre_act[i]  (reference layer.py:478-480).
+class _RewireInputFn(torch.autograd.Function):
+    """MHCRewire's input side (reference layer.py:474-480): the wrapped
+    MHCLayer's activations from its raw parameters, then
+    x_pre[t, i, c] = x[t, i, c] * H_pre_act[i] -- one launch for n <= 8.
 
-    M and H_post_act are inputs too (unused by the forward): when the
-    post-combine's backward has handed over d_out through `link`, this
-    backward is the x side of MHCRewire's end-to-end backward and returns
-    the gradients of x, M, H_pre_act and H_post_act of the whole layer."""
+    Outputs (x_pre, H_pre_act, H_post_act, M); the last three feed the
+    post-combine.  When the post-combine's backward has handed over d_out
+    through `link`, this backward is the x side of MHCRewire's end-to-end
+    backward and returns the raw-parameter gradients of the whole layer from
+    the same finalize launch (the Sinkhorn / sigmoid chain rule folded in).
+    Otherwise the post-combine returned its own activation gradients, and
+    they are added to the pre-scale's before the parameter backward."""
 
     @staticmethod
-    def forward(ctx, x, M, hpre, hpost, link=None):
-        ctx.save_for_backward(x, M, hpre, hpost)
-        ctx.link = link
-        return K.prescale_fwd(x, hpre)
+    def forward(ctx, x, H_pre_raw, H_post_raw, H_res_raw, iters, eps, link):
+        ctx.set_materialize_grads(False)
+        x_pre, hpre, hpost, M, raw = K.rewire_in_fwd(x, H_pre_raw, H_post_raw, H_res_raw,
+                                                     iters, eps)
+        pre, post, res, tape, jac, _, _ = raw
+        z = M.new_empty(0)
+        ctx.save_for_backward(x, pre, post, res, hpre, hpost, M,
+                              tape if tape is not None else z, jac if jac is not None else z)
+        ctx.iters, ctx.eps, ctx.link = iters, eps, link
+        return x_pre, hpre, hpost, M
 
     @staticmethod
-    def backward(ctx, d):
-        x, M, hpre, hpost = ctx.saved_tensors
+    def backward(ctx, d, dhpre, dhpost, dM):
+        x, pre, post, res, hpre, hpost, M, tape, jac = ctx.saved_tensors
+        tape = tape if tape.numel() else None
+        jac = jac if jac.numel() else None
         link = ctx.link
-        if link is not None and link.state is not None:
+        want_dx = ctx.needs_input_grad[0]
+        if link.state is not None:
             state, link.state = link.state, None
-            dx, dM, dpre, dpost = K.rewire_bwd_dx(x, d, M, hpre, hpost, state,
-                                                  want_dx=ctx.needs_input_grad[0])
-            return dx, dM, dpre, dpost, None
-        dx, dpre = K.prescale_bwd(x, d, hpre)
-        return dx, None, dpre, None, None
+            dx, gpre, gpost, gres = K.rewire_bwd_dx(
+                x, d, M, hpre, hpost, state, want_dx=want_dx,
+                raw=(pre, post, res, tape, jac, ctx.iters, ctx.eps))
+            return dx, gpre, gpost, gres, None, None, None
+        dx = None
+        if d is not None:
+            dx, dpre_x = K.prescale_bwd(x, d, hpre)
+            dhpre = dpre_x if dhpre is None else dhpre + dpre_x
+        if dhpre is None and dhpost is None and dM is None:
+            return dx, None, None, None, None, None, None
+        z = pre.new_zeros
+        gpre, gpost, gres = K.params_bwd(
+            pre, post, res, tape, ctx.iters, ctx.eps,
+            dhpre if dhpre is not None else z(pre.shape),
+            dhpost if dhpost is not None else z(post.shape),
+            dM if dM is not None else z(res.shape))
+        return dx, gpre, gpost, gres, None, None, None
 
 
 def _engine_will_run(node) -> bool:
@@ -360,10 +386,12 @@ class MHCRewire(nn.Module):
         C = dims // self.n
         B = x.numel() // dims if dims else 0
         self.mhc._require_cuda_path(B, self.n, C)
-        hpre, hpost, M = self.mhc.activations()
+        _validate_n(self.n)
         x3 = x.reshape(-1, self.n, C)
         link = _RewireLink()
-        x_pre3 = _PrescaleFn.apply(x3, M, hpre, hpost, link)
+        mh = self.mhc
+        x_pre3, hpre, hpost, M = _RewireInputFn.apply(
+            x3, mh.H_pre_raw, mh.H_post_raw, mh.H_res_raw, mh.sinkhorn_iters, mh.eps, link)
         y_inner = self.inner(x_pre3.reshape(x.shape))
         if tuple(y_inner.shape) != tuple(x.shape):
             raise ValueError(

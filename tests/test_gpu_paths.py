@@ -365,6 +365,80 @@ def test_rewire_split_backward_kernels_match_oracle(B, n, C, dt, with_p):
         assert rel_err(a, b) < 1e-5, (name, rel_err(a, b))
 
 
+@pytest.mark.parametrize("T,n,C,dt,iters", [(6, 4, 1024, torch.bfloat16, 20),
+                                             (5, 4, 129, torch.float32, 20),
+                                             (0, 4, 64, torch.float32, 20),
+                                             (3, 1, 64, torch.float16, 20),
+                                             (3, 2, 64, torch.float32, 7),
+                                             (3, 8, 128, torch.bfloat16, 20),
+                                             (2, 3, 40, torch.float32, 20),
+                                             (2, 16, 64, torch.float32, 20),
+                                             (2, 32, 64, torch.bfloat16, 20),
+                                             (2, 4, 64, torch.float32, 0)])
+def test_rewire_in_fwd_matches_parameter_and_prescale_kernels(T, n, C, dt, iters):
+    """mhc_rewire_in_fwd (one launch for n <= 8: the parameter chain in one
+    block beside the pre-scale) writes the same bits as mhc_params_fwd then
+    mhc_prescale_fwd; for n <= 4 its Jacobian row u equals the parameter
+    backward of the unit cotangent dM = e_u."""
+    from mhc_b200 import _kernels as K
+
+    g = torch.Generator().manual_seed(97 * n + T + iters)
+    x = cu(torch.randn(T, n, C, generator=g).to(dt), dt)
+    pre, post = cu(torch.randn(n, generator=g)), cu(torch.randn(n, generator=g))
+    res = cu(3 * torch.randn(n, n, generator=g))
+    xp, hpre, hpost, M, raw = K.rewire_in_fwd(x, pre, post, res, iters, 1e-5)
+    hpre2, hpost2, M2, tape2 = K.params_fwd(pre, post, res, iters, 1e-5, want_tape=True)
+    xp2 = K.prescale_fwd(x, hpre2)
+    assert torch.equal(hpre, hpre2) and torch.equal(hpost, hpost2) and torch.equal(M, M2)
+    assert torch.equal(xp, xp2) and xp.dtype == dt
+    tape, jac = raw[3], raw[4]
+    if iters:
+        assert torch.equal(tape, tape2)
+    if n not in (1, 2, 4):
+        assert jac is None
+        return
+    assert jac is not None and jac.numel() == n ** 4
+    eye = torch.eye(n * n, device=DEV)
+    for u in range(n * n):
+        _, _, gres = K.params_bwd(pre, post, res, tape2, iters, 1e-5, torch.zeros_like(hpre),
+                                  torch.zeros_like(hpost), eye[u].view(n, n))
+        assert torch.allclose(jac.view(n * n, n * n)[u], gres.flatten(), rtol=1e-6, atol=1e-7), u
+
+
+@pytest.mark.parametrize("T,n,C,dt", [(5, 4, 1024, torch.bfloat16), (4, 4, 129, torch.float32),
+                                      (3, 1, 64, torch.float32), (3, 2, 64, torch.float32),
+                                      (3, 8, 64, torch.float32), (2, 3, 40, torch.float32),
+                                      (2, 16, 64, torch.float32), (2, 32, 64, torch.float32),
+                                      (0, 4, 64, torch.float32)])
+def test_rewire_bwd_dx_raw_gradients_match_parameter_kernel(T, n, C, dt):
+    """mhc_rewire_bwd_dx with the raw parameters: the finalize carries the
+    chain rule on to dH_pre_raw / dH_post_raw / dH_res_raw (the Jacobian's
+    dot products for n <= 4, the reverse sweep in the finalize for n != 16,
+    the parameter kernel after it for n = 16) and matches mhc_params_bwd on
+    the activation gradients of the same call; dx is unchanged."""
+    from mhc_b200 import _kernels as K
+
+    g = torch.Generator().manual_seed(13 * n + C + T)
+    x = cu(torch.randn(T, n, C, generator=g).to(dt), dt)
+    y = cu(torch.randn(T, n, C, generator=g).to(dt), dt)
+    d = cu(torch.randn(T, n, C, generator=g))
+    p = cu(torch.randn(T, n, C, generator=g).to(dt), dt)
+    pre, post = cu(torch.randn(n, generator=g)), cu(torch.randn(n, generator=g))
+    res = cu(3 * torch.randn(n, n, generator=g))
+    _, hpre, hpost, M, raw = K.rewire_in_fwd(x, pre, post, res, 20, 1e-5)
+    _, state = K.rewire_bwd_dy(y, d, hpost)
+    dx, dM, dpre, dpost = K.rewire_bwd_dx(x, p, M, hpre, hpost, state)
+    _, state = K.rewire_bwd_dy(y, d, hpost)
+    dx2, gpre, gpost, gres = K.rewire_bwd_dx(x, p, M, hpre, hpost, state, raw=raw)
+    assert torch.equal(dx, dx2)
+    rpre, rpost, rres = K.params_bwd(pre, post, res, raw[3], 20, 1e-5, dpre, dpost, dM)
+    assert torch.equal(gpre, rpre) and torch.equal(gpost, rpost)
+    assert gres.shape == (n, n)
+    assert torch.allclose(gres, rres, rtol=1e-5, atol=1e-6 * float(rres.abs().max()) + 1e-30)
+    if T == 0:
+        assert torch.all(gres == 0) and torch.all(gpre == 0) and torch.all(gpost == 0)
+
+
 def test_rewire_backward_runs_no_torch_elementwise_kernel():
     """MHCRewire's backward around a frozen bias-free Linear (BASELINE config 4
     layout, bf16): the GPU kernels it launches are this library's and the
