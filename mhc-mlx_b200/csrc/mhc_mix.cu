@@ -419,17 +419,127 @@ k_combine_bwd_generic(const XT* __restrict__ x, const YT* __restrict__ y,
 }
 
 // ------------------------------------------- rewire backward, x side (fast) --
+// The finalize of MHCRewire's end-to-end backward when the x side's last CTA
+// runs it (on = 1): the activation gradients (each nullable) and the
+// raw-parameter chain rule of pb.
+struct RewireFin {
+  float* dM;
+  float* dhpre;
+  float* dhpost;
+  ParamsBwd pb;
+  int on;
+};
+
+// Run by the last CTA of the x side (n in {1, 2, 4}) once every CTA's row
+// is visible: sums the G rows of P floats -- each already holding its share
+// of the dy side's rows -- in a fixed order (16-byte columns of a row over S
+// interleaved row slices, then the slices of an entry by a warp butterfly),
+// so the result does not depend on which CTA came last.  Then the mode-3
+// finalize of k_combine_finalize and the raw-parameter tail: sigmoid chain
+// rule, and dH_res from the Jacobian's dot products or the lane-path
+// reverse sweep.  The rows were written in this launch: L2 loads.
+template <int N>
+__device__ __forceinline__ void rewire_fin_last(const float* rows, int G, const float* sM,
+                                                const float* __restrict__ hpre_g,
+                                                const float* __restrict__ hpost_g,
+                                                const RewireFin& fin) {
+  constexpr int NN = N * N, P = NN + 2 * N;
+  constexpr int W = (P % 4 == 0) ? 4 : 1;  // floats per load
+  constexpr int CW = P / W;                // loads per row
+  constexpr int S = kMixBD / CW;           // row slices
+  __shared__ float red[S * P];
+  __shared__ float fq[P], fa[P];
+  const int tid = threadIdx.x, c = tid % CW, r = tid / CW;
+  if (r < S) {
+    float a[W];
+#pragma unroll
+    for (int k = 0; k < W; ++k) a[k] = 0.f;
+#pragma unroll 8
+    for (int g = r; g < G; g += S) {
+      const float* src = rows + (size_t)g * P + c * W;
+      if constexpr (W == 4) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(src));
+        a[0] += v.x; a[1] += v.y; a[2] += v.z; a[3] += v.w;
+      } else {
+        a[0] += __ldcg(src);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < W; ++k) red[r * P + c * W + k] = a[k];
+  }
+  __syncthreads();
+  const int lane = tid & 31, warp = tid >> 5;
+  for (int e = warp; e < P; e += kMixBD / 32) {
+    float s = 0.f;
+    for (int q = lane; q < S; q += 32) s += red[q * P + e];
+    s = warp_sum(s);
+    if (lane == 0) fq[e] = s;
+  }
+  __syncthreads();
+  // Q = fq[0, NN), R = fq[NN, NN + N), S = fq[NN + N, P)
+  if (tid < NN) {
+    const int i = tid / N, j = tid % N;
+    const float v = (hpost_g[i] * hpre_g[j]) * fq[tid];
+    fa[tid] = v;
+    if (fin.dM) fin.dM[tid] = v;
+  } else if (tid < NN + N) {
+    const int j = tid - NN;
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) s = fmaf(hpost_g[i] * sM[i * N + j], fq[i * N + j], s);
+    s += fq[NN + N + j];
+    fa[tid] = s;
+    if (fin.dhpre) fin.dhpre[j] = s;
+  } else if (tid < P) {
+    const int i = tid - NN - N;
+    float s = fq[NN + i];
+#pragma unroll
+    for (int j = 0; j < N; ++j) s = fmaf(sM[i * N + j] * hpre_g[j], fq[i * N + j], s);
+    fa[tid] = s;
+    if (fin.dhpost) fin.dhpost[i] = s;
+  }
+  const ParamsBwd& pb = fin.pb;
+  if (!pb.any()) return;
+  __syncthreads();  // fa complete
+  if (tid < N) {
+    if (pb.dhpre_raw) {
+      const float sg = sigmoidf_(pb.hpre_raw[tid]);
+      pb.dhpre_raw[tid] = fa[NN + tid] * (1.0f - sg) * sg;
+    }
+    if (pb.dhpost_raw) {
+      const float sg = sigmoidf_(pb.hpost_raw[tid]);
+      pb.dhpost_raw[tid] = (2.0f * fa[NN + N + tid]) * (1.0f - sg) * sg;
+    }
+  }
+  if (!pb.dhres_raw) return;
+  if (pb.jac) {
+    if (tid < NN) {
+      float s = 0.f;
+#pragma unroll
+      for (int u = 0; u < NN; ++u) s = fmaf(fa[u], pb.jac[u * NN + tid], s);
+      pb.dhres_raw[tid] = s;
+    }
+  } else if (tid < 32 && (pb.tape || pb.iters == 0)) {
+    const bool act = tid < NN;
+    const float d = sk_backward_lane<N>(pb.hres_raw, pb.tape, pb.iters, pb.eps, act ? fa[tid] : 0.f);
+    if (act) pb.dhres_raw[tid] = d;
+  }
+}
+
 // n in {1, 2, 4}, 16-byte vectors: thread = (token, VEC columns) with the
 // x rows and the dx accumulators of all n streams in registers, Q and S in
 // registers across the thread's items.  p (d_xpre) may be NULL (zero), dx
-// may be NULL (only the parameter partials are wanted).
+// may be NULL (only the parameter partials are wanted).  With fin.on each
+// CTA folds the dy side's rows b, b + G2, ... into its own row and the last
+// CTA to finish (a ticket in header word 3, zeroed by the dy side) runs
+// the finalize: no separate finalize launch.
 template <int N, typename XT, typename DT, typename PT, int VEC>
 __global__ void __launch_bounds__(kMixBD, 2)
 k_rewire_bwd_x_fast(const XT* __restrict__ x, const DT* __restrict__ dout,
                     const PT* __restrict__ dp, const float* __restrict__ Mg,
                     const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
                     XT* __restrict__ dx, int64_t T, int C, float* __restrict__ ws_p,
-                    int* __restrict__ ws_hdr) {
+                    int* __restrict__ ws_hdr, RewireFin fin) {
   constexpr int P = N * N + 2 * N;
   __shared__ float sM[N * N];
   __shared__ float sacc[(kMixBD / 32) * P];
@@ -513,9 +623,23 @@ k_rewire_bwd_x_fast(const XT* __restrict__ x, const DT* __restrict__ dout,
   for (int e = threadIdx.x; e < P; e += blockDim.x) {
     float s = 0.f;
     for (int w = 0; w < nw; ++w) s += sacc[w * P + e];
+    if (fin.on)  // this CTA's share of the dy side's rows (written by the previous launch)
+      for (int r = blockIdx.x; r < row0; r += gridDim.x) s += ws_p[(size_t)r * P + e];
     ws_p[(size_t)(row0 + blockIdx.x) * P + e] = s;
   }
-  if (blockIdx.x == 0 && threadIdx.x == 0) ws_hdr[2] = gridDim.x;
+  if (!fin.on) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) ws_hdr[2] = gridDim.x;
+    return;
+  }
+  __shared__ int s_last;
+  __threadfence();  // this CTA's row is visible device-wide before its ticket
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(ws_hdr + 3, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  rewire_fin_last<N>(ws_p + (size_t)row0 * P, (int)gridDim.x, sM, hpre_g, hpost_g, fin);
+  if (threadIdx.x == 0) ws_hdr[3] = 0;  // the workspace may be finalized again
 }
 
 // ----------------------------------------------------------- prescale bwd --
@@ -566,7 +690,10 @@ k_prescale_bwd(const XT* __restrict__ x, const DT* __restrict__ dout,
       for (int w = 0; w < nw; ++w) s += sacc[w * MAXN + (e - nr * nr)];
     pr[e] = s;
   }
-  if (blockIdx.x == 0 && threadIdx.x == 0) ws_hdr[0] = gridDim.x;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    ws_hdr[0] = gridDim.x;
+    ws_hdr[3] = 0;  // ticket of the rewire x side's last-CTA finalize
+  }
 }
 
 // ------------------------------------------------- residual add agg bwd --
@@ -1059,10 +1186,11 @@ int launch_rewire_bwd_dy(const void* y, int ydt, const void* d, int ddt, const f
   }
 }
 
+// *finished: the x side's last CTA ran the finalize (fast path, fin.on).
 template <typename XT, typename DT, typename PT>
 static int rewire_x_t(const void* xv, const void* dv, const void* pv, const float* M,
                       const float* hpre, const float* hpost, void* dxv, int64_t T, int n, int C,
-                      void* ws, cudaStream_t st) {
+                      void* ws, RewireFin fin, bool* finished, cudaStream_t st) {
   constexpr int VX = VecOf<XT>::value;
   // 4 columns per item: all of an item's loads fit in registers at once
   constexpr int V4 = 4;
@@ -1077,8 +1205,10 @@ static int rewire_x_t(const void* xv, const void* dv, const void* pv, const floa
   const bool vec = (C % VX == 0) && all_aligned({xv, dv, pv, dxv});
   if (vec && (n == 1 || n == 2 || n == 4)) {
     const int G = elem_grid(T * (C / V4), cap);
+    fin.on = aligned16(ws) ? 1 : 0;  // the last CTA's 16-byte row loads
+    *finished = fin.on != 0;
 #define MHC_RX(NN) \
-  k_rewire_bwd_x_fast<NN, XT, DT, PT, V4><<<G, kMixBD, 0, st>>>(x, d, p, M, hpre, hpost, dx, T, C, wp, hdr)
+  k_rewire_bwd_x_fast<NN, XT, DT, PT, V4><<<G, kMixBD, 0, st>>>(x, d, p, M, hpre, hpost, dx, T, C, wp, hdr, fin)
     if (n == 1) MHC_RX(1);
     else if (n == 2) MHC_RX(2);
     else MHC_RX(4);
@@ -1100,14 +1230,14 @@ static int rewire_x_t(const void* xv, const void* dv, const void* pv, const floa
 template <typename XT>
 static int rewire_x_x(const void* x, int xdt, const void* d, int ddt, const void* p, int pdt,
                       const float* M, const float* hpre, const float* hpost, void* dx, int64_t T,
-                      int n, int C, void* ws, cudaStream_t st) {
+                      int n, int C, void* ws, const RewireFin& fin, bool* fd, cudaStream_t st) {
   const bool d32 = ddt == MHC_F32, p32 = (p == nullptr) || pdt == MHC_F32;
   if (!d32 && ddt != xdt) return set_error(MHC_ERR_UNSUPPORTED, "rewire bwd: d_out dtype must be fp32 or x's dtype");
   if (!p32 && pdt != xdt) return set_error(MHC_ERR_UNSUPPORTED, "rewire bwd: d_xpre dtype must be fp32 or x's dtype");
-  if (d32 && p32) return rewire_x_t<XT, float, float>(x, d, p, M, hpre, hpost, dx, T, n, C, ws, st);
-  if (d32) return rewire_x_t<XT, float, XT>(x, d, p, M, hpre, hpost, dx, T, n, C, ws, st);
-  if (p32) return rewire_x_t<XT, XT, float>(x, d, p, M, hpre, hpost, dx, T, n, C, ws, st);
-  return rewire_x_t<XT, XT, XT>(x, d, p, M, hpre, hpost, dx, T, n, C, ws, st);
+  if (d32 && p32) return rewire_x_t<XT, float, float>(x, d, p, M, hpre, hpost, dx, T, n, C, ws, fin, fd, st);
+  if (d32) return rewire_x_t<XT, float, XT>(x, d, p, M, hpre, hpost, dx, T, n, C, ws, fin, fd, st);
+  if (p32) return rewire_x_t<XT, XT, float>(x, d, p, M, hpre, hpost, dx, T, n, C, ws, fin, fd, st);
+  return rewire_x_t<XT, XT, XT>(x, d, p, M, hpre, hpost, dx, T, n, C, ws, fin, fd, st);
 }
 
 int launch_rewire_bwd_dx(const void* x, int xdt, const void* d, int ddt, const void* p, int pdt,
@@ -1118,13 +1248,17 @@ int launch_rewire_bwd_dx(const void* x, int xdt, const void* d, int ddt, const v
   if (!ws || ws_bytes < need)
     return set_error(MHC_ERR_WORKSPACE, "rewire bwd: workspace %zu < %zu bytes", ws_bytes, need);
   if (dx && dxdt != xdt) return set_error(MHC_ERR_UNSUPPORTED, "rewire bwd: dx dtype must equal x dtype");
+  // The fast x side (n <= 4) finalizes in its last CTA, the Jacobian or the
+  // lane-path sweep included; otherwise the one-CTA finalize kernel follows.
+  const RewireFin fin{dM, dhpre, dhpost, pb, 0};
+  bool finished = false;
   int r;
   switch (xdt) {
-    case MHC_F32: r = rewire_x_x<float>(x, xdt, d, ddt, p, pdt, M, hpre, hpost, dx, T, n, C, ws, st); break;
-    case MHC_BF16: r = rewire_x_x<bf16>(x, xdt, d, ddt, p, pdt, M, hpre, hpost, dx, T, n, C, ws, st); break;
-    default: r = rewire_x_x<f16>(x, xdt, d, ddt, p, pdt, M, hpre, hpost, dx, T, n, C, ws, st); break;
+    case MHC_F32: r = rewire_x_x<float>(x, xdt, d, ddt, p, pdt, M, hpre, hpost, dx, T, n, C, ws, fin, &finished, st); break;
+    case MHC_BF16: r = rewire_x_x<bf16>(x, xdt, d, ddt, p, pdt, M, hpre, hpost, dx, T, n, C, ws, fin, &finished, st); break;
+    default: r = rewire_x_x<f16>(x, xdt, d, ddt, p, pdt, M, hpre, hpost, dx, T, n, C, ws, fin, &finished, st); break;
   }
-  if (r != MHC_OK) return r;
+  if (r != MHC_OK || finished) return r;
   // The raw-parameter chain rule runs in the finalize when its thread count
   // suits the Sinkhorn path of n, else as the separate parameter kernel on
   // the activation gradients the finalize wrote.

@@ -437,6 +437,11 @@ def test_rewire_bwd_dx_raw_gradients_match_parameter_kernel(T, n, C, dt):
     assert torch.allclose(gres, rres, rtol=1e-5, atol=1e-6 * float(rres.abs().max()) + 1e-30)
     if T == 0:
         assert torch.all(gres == 0) and torch.all(gpre == 0) and torch.all(gpost == 0)
+    # run to run the same bits (fixed-order reductions whichever CTA finishes
+    # last), also when one dy workspace is finalized twice
+    again = K.rewire_bwd_dx(x, p, M, hpre, hpost, state, raw=raw)
+    for a, b in zip((dx2, gpre, gpost, gres), again):
+        assert torch.equal(a, b)
 
 
 def test_rewire_backward_runs_no_torch_elementwise_kernel():
