@@ -58,10 +58,11 @@ def parse():
                     help="skip the compact BASELINE config 1-5 records of the default run")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--workload", choices=["layer", "sweep", "sinkhorn", "rewire", "llama", "qmm",
-                                           "all"],
+                                           "rewire_step", "all"],
                     default="layer",
                     help="layer = the headline (BASELINE target); the others measure BASELINE "
-                         "configs 1-4 and print one JSON line each (1 GPU)")
+                         "configs 1-4 and print one JSON line each (1 GPU); rewire_step runs "
+                         "config 4's step --warmup + --steps times (for profilers)")
     return ap.parse_args()
 
 
@@ -742,16 +743,14 @@ def config3_sinkhorn(dev):
                        "iterations and reverses them)"}}
 
 
-def config4_rewire(dev, peak, peak_kind):
-    """BASELINE config 4: MHCRewire n=4 around a 4-bit QuantizedLinear 4096 ->
-    4096, 8192 bf16 tokens; mHC kernels timed, the GEMM excluded."""
+def _config4_step(dev):
+    """Config 4's model (MHCRewire n=4 around a 4-bit QuantizedLinear 4096 ->
+    4096), inputs (8192 bf16 tokens, fp32 d_out) and one fwd+bwd step."""
     import mhc_b200
 
     g = torch.Generator().manual_seed(4)
     ql = mhc_b200.QuantizedLinear.random(4096, 4096, group_size=64, bits=4,
                                          dtype=torch.float16, generator=g).to(dev)
-    bf16_peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("bf16_tflops", 1590.0) \
-        if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
     model4 = mhc_b200.MHCRewire(ql, dims=4096, n=4).to(dev)
     x4 = torch.randn(8192, 4096, device=dev).to(torch.bfloat16).requires_grad_(True)
     d4 = torch.randn(8192, 4096, device=dev)
@@ -761,6 +760,35 @@ def config4_rewire(dev, peak, peak_kind):
         for p_ in model4.parameters():
             p_.grad = None
         model4(x4).backward(d4)
+
+    return model4, x4, d4, fb4
+
+
+def rewire_step_only(dev, steps, warmup):
+    """Config 4's eager fwd+bwd step, W + K times, nothing else: the command
+    that per-launch profiles of the MHCRewire kernels capture."""
+    _, _, _, fb4 = _config4_step(dev)
+    for _ in range(warmup):
+        fb4()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fb4()
+    b.record()
+    torch.cuda.synchronize(dev)
+    return {"metric": "MHCRewire config 4 eager fwd+bwd step (profiling entry)", "unit": "us",
+            "higher_is_better": False, "value": 1e3 * a.elapsed_time(b) / max(steps, 1),
+            "steps": steps, "warmup": warmup,
+            "config": {"workload": "BASELINE config 4 step, GEMMs included"}}
+
+
+def config4_rewire(dev, peak, peak_kind):
+    """BASELINE config 4: MHCRewire n=4 around a 4-bit QuantizedLinear 4096 ->
+    4096, 8192 bf16 tokens; mHC kernels timed, the GEMM excluded."""
+    bf16_peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("bf16_tflops", 1590.0) \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
+    model4, x4, d4, fb4 = _config4_step(dev)
 
     _, per4 = _kernel_us_per_step(fb4, dev)
     # the wrapped layer's two GEMMs (forward, input gradient) are timed apart
@@ -932,6 +960,8 @@ def run_configs(args):
         out.append(config4_rewire(dev, peak, peak_kind))
     if w in ("qmm", "all"):
         out.append(qmm_measure(dev, args.tokens if args.tokens != 65536 else 8192))
+    if w == "rewire_step":
+        out.append(rewire_step_only(dev, args.steps, args.warmup))
     for r in out:
         print(json.dumps(r), flush=True)
 

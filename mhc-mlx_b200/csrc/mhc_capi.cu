@@ -6,6 +6,7 @@
 // metal.py:1610-1616).
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -59,6 +60,14 @@ int max_smem_optin() {
   const int d = current_device();
   std::call_once(g_once[d], query, d);
   return g_smem[d];
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("MHC_B200_PDL");
+    return !(v && *v == '0');
+  }();
+  return on;
 }
 
 // Launch-attribute caches keyed on (kernel, device[, block, shared bytes]).
@@ -413,7 +422,7 @@ int mhc_rewire_in_fwd(const void* x, int x_dtype, const float* H_pre_raw, const 
   MHC_REQ(!jacobian || sk_lane_ok(n), "%s: a Jacobian exists for n in {1, 2, 4} only (n=%d)", __func__, n);
   MHC_REQ(T == 0 || (x && x_pre), "%s: NULL tensor pointer", __func__);
   const ParamsFwd pf{H_pre_raw, H_post_raw, H_res_raw, iters, eps, H_pre_act, H_post_act, M,
-                     tape, jacobian};
+                     tape, jacobian, 0};
   return launch_rewire_in_fwd(x, x_dtype, pf, x_pre, out_dtype, T, n, C, as_stream(stream));
   MHC_TRY_END
 }

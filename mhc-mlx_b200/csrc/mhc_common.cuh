@@ -156,6 +156,18 @@ __device__ __forceinline__ void cp_async_wait_group() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(K) : "memory");
 }
 
+// ------------------------------------------- programmatic dependent launch --
+// A kernel launched with the PDL attribute (launch_pdl) may become resident
+// while the previous kernel of the stream drains.  pdl_wait() blocks until
+// that kernel has completed and its writes are visible, so it precedes every
+// access to memory the previous kernel may touch; pdl_trigger() lets the next
+// kernel's CTAs launch (they wait in their own pdl_wait()).  Both are no-ops
+// for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
 // ------------------------------------------------- mbarrier + bulk copies --
 // 1-D bulk copies (cp.async.bulk: the TMA unit without a tensor map) from
 // this GPU's own global memory into the CTA's shared memory, completing on an

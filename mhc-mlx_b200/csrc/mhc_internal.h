@@ -56,6 +56,26 @@ inline int blocks_per_sm(K kernel, int threads, size_t smem) {
   return per_sm;
 }
 
+// Launch with programmatic stream serialisation: the kernel may start while
+// the previous kernel of the stream finishes (it calls pdl_wait() before
+// touching memory).  MHC_B200_PDL=0 launches without the attribute.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 inline int dtype_size(int dt) { return dt == MHC_F32 ? 4 : 2; }
 inline bool dtype_ok(int dt) { return dt == MHC_F32 || dt == MHC_F16 || dt == MHC_BF16; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -78,6 +98,7 @@ struct ParamsFwd {
   float* M;
   float* tape;
   float* jac;
+  int stage;  // set by the launcher: the block keeps the tape in dynamic shared memory
 };
 // The parameter backward folded into a finalize: raw parameters, the
 // forward's tape / Jacobian, and the raw gradients (all null: not folded).

@@ -30,6 +30,7 @@
 // The two passes write their partial rows into one workspace: the dy side
 // rows [0, G1) (header word 0 = G1), the x side rows [G1, G1 + G2) (word 2 =
 // G2); a row is [Q (n*n) | R (n) | S (n)] with the other side's slots zero.
+#include <algorithm>
 #include <cstdlib>
 
 #include "mhc_common.cuh"
@@ -59,6 +60,8 @@ __global__ void __launch_bounds__(kMixBD)
 k_combine_fwd(const XT* __restrict__ x, const YT* __restrict__ y, const float* __restrict__ Mg,
               const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
               OT* __restrict__ out, int64_t T, int n, int C) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sM[MAXN * MAXN];
   __shared__ float shpre[MAXN], shpost[MAXN];
   const int nr = EXACT ? MAXN : n;
@@ -110,6 +113,8 @@ template <int MAXN, bool EXACT, typename XT, typename OT, int VEC, bool PARAMS =
 __global__ void __launch_bounds__(kMixBD, PARAMS ? 8 : 1)  // PARAMS: keep 8 blocks per SM
 k_prescale_fwd(const XT* __restrict__ x, const float* __restrict__ hpre_g, OT* __restrict__ xo,
                int64_t T, int n, int C, ParamsFwd pf) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float shpre[MAXN];
   const int nr = EXACT ? MAXN : n;
   int b0 = 0;
@@ -122,10 +127,18 @@ k_prescale_fwd(const XT* __restrict__ x, const float* __restrict__ hpre_g, OT* _
         pf.hpost[tid] = 2.0f * sigmoidf_(pf.hpost_raw[tid]);
       }
       if constexpr (MAXN <= 4) {
-        if (tid < 32) sk_forward_lane<MAXN>(pf.hres_raw, pf.iters, pf.eps, pf.tape, pf.M);
-        if (pf.jac) {  // kernel argument: uniform over the block
+        // pf.stage: the tape goes to shared memory first (the Jacobian's
+        // sweep reads it there) and then to the global record
+        extern __shared__ float s_tape[];
+        float* tp = pf.stage ? s_tape : pf.tape;
+        if (tid < 32) sk_forward_lane<MAXN>(pf.hres_raw, pf.iters, pf.eps, tp, pf.M);
+        if (pf.jac || pf.stage) {  // kernel arguments: uniform over the block
           __syncthreads();  // tape stored
-          sk_jacobian_lane<MAXN>(pf.hres_raw, pf.tape, pf.iters, pf.eps, pf.jac);
+          if (pf.stage) {
+            const int tf = pf.iters * (MAXN * MAXN + 2 * MAXN);
+            for (int e = tid; e < tf; e += blockDim.x) pf.tape[e] = s_tape[e];
+          }
+          if (pf.jac) sk_jacobian_lane<MAXN>(pf.hres_raw, tp, pf.iters, pf.eps, pf.jac, !pf.stage);
         }
       } else {
         if (tid < 32) sk_forward_warp<MAXN>(pf.hres_raw, pf.iters, pf.eps, pf.tape, pf.M);
@@ -469,7 +482,7 @@ __device__ __forceinline__ void rewire_fin_last(const float* rows, int G, const 
   }
   __syncthreads();
   const int lane = tid & 31, warp = tid >> 5;
-  for (int e = warp; e < P; e += kMixBD / 32) {
+  for (int e = warp; e < P; e += (int)(blockDim.x >> 5)) {
     float s = 0.f;
     for (int q = lane; q < S; q += 32) s += red[q * P + e];
     s = warp_sum(s);
@@ -526,13 +539,58 @@ __device__ __forceinline__ void rewire_fin_last(const float* rows, int G, const 
   }
 }
 
+// End of an x-side CTA: Q and S reduced over its threads (fixed-order warp
+// butterflies, then the warps in order) into its partial row [Q | 0 | S] --
+// with fin.on plus its share of the dy side's rows b, b + G2, ... (written by
+// the previous launch) -- and, with fin.on, the last CTA to finish (a ticket
+// in header word 3, zeroed by the dy side) runs the finalize.
+template <int N>
+__device__ __forceinline__ void rewire_x_rows(float (&aQ)[N][N], float (&aS)[N], const float* sM,
+                                              const float* __restrict__ hpre_g,
+                                              const float* __restrict__ hpost_g,
+                                              float* __restrict__ ws_p, int* __restrict__ ws_hdr,
+                                              int row0, const RewireFin& fin) {
+  constexpr int P = N * N + 2 * N;
+  __shared__ float sacc[32 * P];  // up to 1,024 threads
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float v = warp_sum(aQ[i][j]);
+      if (lane == 0) sacc[warp * P + i * N + j] = v;
+    }
+    const float r = warp_sum(aS[i]);
+    if (lane == 0) { sacc[warp * P + N * N + i] = 0.f; sacc[warp * P + N * N + N + i] = r; }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < P; e += blockDim.x) {
+    float s = 0.f;
+    for (int w = 0; w < nw; ++w) s += sacc[w * P + e];
+    if (fin.on)  // this CTA's share of the dy side's rows (written by the previous launch)
+      for (int r = blockIdx.x; r < row0; r += gridDim.x) s += ws_p[(size_t)r * P + e];
+    ws_p[(size_t)(row0 + blockIdx.x) * P + e] = s;
+  }
+  if (!fin.on) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) ws_hdr[2] = gridDim.x;
+    return;
+  }
+  __shared__ int s_last;
+  __threadfence();  // this CTA's row is visible device-wide before its ticket
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(ws_hdr + 3, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  rewire_fin_last<N>(ws_p + (size_t)row0 * P, (int)gridDim.x, sM, hpre_g, hpost_g, fin);
+  if (threadIdx.x == 0) ws_hdr[3] = 0;  // the workspace may be finalized again
+}
+
 // n in {1, 2, 4}, 16-byte vectors: thread = (token, VEC columns) with the
 // x rows and the dx accumulators of all n streams in registers, Q and S in
 // registers across the thread's items.  p (d_xpre) may be NULL (zero), dx
-// may be NULL (only the parameter partials are wanted).  With fin.on each
-// CTA folds the dy side's rows b, b + G2, ... into its own row and the last
-// CTA to finish (a ticket in header word 3, zeroed by the dy side) runs
-// the finalize: no separate finalize launch.
+// may be NULL (only the parameter partials are wanted).  Ends in
+// rewire_x_rows (partial rows, and with fin.on the last-CTA finalize).
 template <int N, typename XT, typename DT, typename PT, int VEC>
 __global__ void __launch_bounds__(kMixBD, 2)
 k_rewire_bwd_x_fast(const XT* __restrict__ x, const DT* __restrict__ dout,
@@ -540,9 +598,9 @@ k_rewire_bwd_x_fast(const XT* __restrict__ x, const DT* __restrict__ dout,
                     const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
                     XT* __restrict__ dx, int64_t T, int C, float* __restrict__ ws_p,
                     int* __restrict__ ws_hdr, RewireFin fin) {
-  constexpr int P = N * N + 2 * N;
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sM[N * N];
-  __shared__ float sacc[(kMixBD / 32) * P];
   const int row0 = ws_hdr[0];
   for (int e = threadIdx.x; e < N * N; e += blockDim.x) sM[e] = Mg[e];
   float hpre[N], hpost[N];
@@ -608,38 +666,175 @@ k_rewire_bwd_x_fast(const XT* __restrict__ x, const DT* __restrict__ dout,
     t += dt;
     if (g >= groups) { g -= groups; ++t; }
   }
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  rewire_x_rows<N>(aQ, aS, sM, hpre_g, hpost_g, ws_p, ws_hdr, row0, fin);
+}
+
+// Shared-memory 4-column loads of the staged rows (plain ld.shared: the
+// load_vec helpers use global-memory cache hints).
+template <typename T>
+__device__ __forceinline__ void lds4(const T* p, float (&o)[4]) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
+    o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = to_f(h[k]);
+  }
+}
+
+// x side with bulk-copy staging (n in {1, 2, 4}): one CTA of 512 threads per
+// SM takes the tokens b, b + G, ... of the sequence; a token's x, d_out and
+// d_xpre rows are each one contiguous run, so thread 0 stages a whole token
+// with three 1-D bulk copies (plain loads of this GPU's memory) into a ring
+// of NS buffers completing on mbarriers, NS tokens ahead.  The two halves of
+// the CTA take two consecutive tokens of the sequence at a time (16 warps
+// per SM to hide the shared-memory and FMA latencies of ~220 instructions per
+// 4-column group); thread t of a half owns its column groups t, t + 256, ...
+// A pair's buffers are refilled after the block barrier that follows their
+// last reads.  The loads no longer occupy registers, so the bytes in flight
+// per SM are the ring's.  Waits are bounded: a copy that never lands makes the
+// CTA wait (bounded) for its other copies in flight, write NaN into its dx
+// tokens from there on and into its partial row, so the parameter gradients
+// come out NaN.
+constexpr int kXBulkMaxStages = 8;
+constexpr int kXBulkBD = 512;
+
+template <int N, typename XT, typename DT, typename PT>
+__global__ void __launch_bounds__(kXBulkBD, 1)
+k_rewire_bwd_x_bulk(const XT* __restrict__ x, const DT* __restrict__ dout,
+                    const PT* __restrict__ dp, const float* __restrict__ Mg,
+                    const float* __restrict__ hpre_g, const float* __restrict__ hpost_g,
+                    XT* __restrict__ dx, int64_t T, int C, int NS, float* __restrict__ ws_p,
+                    int* __restrict__ ws_hdr, RewireFin fin) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr int HB = kXBulkBD / 2;  // threads per half
+  extern __shared__ __align__(16) unsigned char s_ring[];
+  __shared__ float sM[N * N];
+  __shared__ __align__(16) float sWT[N][4];  // sWT[j][i] = M_ij H_post_i
+  __shared__ __align__(8) uint64_t s_full[kXBulkMaxStages];
+  __shared__ int s_abort;
+  const int tid = threadIdx.x, hf = tid / HB, lt = tid % HB;
+  const int row0 = ws_hdr[0];
+  const int64_t G = gridDim.x, RS = (int64_t)N * C;
+  const unsigned bx = (unsigned)(RS * sizeof(XT)), bdo = (unsigned)(RS * sizeof(DT));
+  const unsigned bp = dp ? (unsigned)(RS * sizeof(PT)) : 0u;
+  const unsigned sb = bx + bdo + bp;  // bytes per stage (multiples of 16: launcher)
+  if (tid == 0) {
+    for (int b = 0; b < NS; ++b) mbar_init(&s_full[b], 1);
+    s_abort = 0;
+    mbar_init_fence();
+  }
+  for (int e = tid; e < N * N; e += blockDim.x) {
+    sM[e] = Mg[e];
+    sWT[e % N][e / N] = Mg[e] * __ldg(hpost_g + e / N);
+  }
+  float hpre[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) hpre[i] = __ldg(hpre_g + i);
+  __syncthreads();
+  const int64_t ntok = (int64_t)blockIdx.x < T ? (T - 1 - blockIdx.x) / G + 1 : 0;
+  auto issue = [&](int64_t k) {  // thread 0: token k of this CTA's sequence
+    const int64_t tok = blockIdx.x + k * G;
+    const int slot = (int)(k % NS);
+    unsigned char* dst = s_ring + (size_t)slot * sb;
+    mbar_arrive_expect_tx(&s_full[slot], sb);
+    bulk_g2s(dst, x + tok * RS, bx, &s_full[slot]);
+    bulk_g2s(dst + bx, dout + tok * RS, bdo, &s_full[slot]);
+    if (dp) bulk_g2s(dst + bx + bdo, dp + tok * RS, bp, &s_full[slot]);
+  };
+  int64_t issued = 0;  // meaningful in thread 0
+  if (tid == 0)
+    for (; issued < NS && issued < ntok; ++issued) issue(issued);
+
+  float aQ[N][N], aS[N];
 #pragma unroll
   for (int i = 0; i < N; ++i) {
+    aS[i] = 0.f;
 #pragma unroll
-    for (int j = 0; j < N; ++j) {
-      const float v = warp_sum(aQ[i][j]);
-      if (lane == 0) sacc[warp * P + i * N + j] = v;
+    for (int j = 0; j < N; ++j) aQ[i][j] = 0.f;
+  }
+  const int groups = C / 4;
+  int64_t k0 = 0;
+  bool aborted = false;
+  for (; k0 < ntok; k0 += 2) {
+    const int64_t k = k0 + hf;  // this half's token of the pair
+    if (k < ntok) {
+      const int slot = (int)(k % NS);
+      if (!mbar_wait(&s_full[slot], (unsigned)((k / NS) & 1))) s_abort = 1;
+      const unsigned char* src = s_ring + (size_t)slot * sb;
+      const XT* sx = reinterpret_cast<const XT*>(src);
+      const DT* sd = reinterpret_cast<const DT*>(src + bx);
+      const PT* sp = reinterpret_cast<const PT*>(src + bx + bdo);
+      XT* dxt = dx ? dx + (blockIdx.x + k * G) * RS : nullptr;
+      for (int g = lt; g < groups; g += HB) {
+        float xr[N][4], dr[N][4], pv[N][4];
+#pragma unroll
+        for (int j = 0; j < N; ++j) lds4<XT>(sx + (int64_t)j * C + 4 * g, xr[j]);
+#pragma unroll
+        for (int i = 0; i < N; ++i) lds4<DT>(sd + (int64_t)i * C + 4 * g, dr[i]);
+        if (dp) {
+#pragma unroll
+          for (int j = 0; j < N; ++j) lds4<PT>(sp + (int64_t)j * C + 4 * g, pv[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < N; ++j)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) pv[j][v] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+#pragma unroll
+          for (int j = 0; j < N; ++j)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) aQ[i][j] = fmaf(dr[i][v], xr[j][v], aQ[i][j]);
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          const float4 w4 = *reinterpret_cast<const float4*>(sWT[j]);
+          const float wj[4] = {w4.x, w4.y, w4.z, w4.w};
+          float o[4];
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            aS[j] = fmaf(pv[j][v], xr[j][v], aS[j]);
+            float a = pv[j][v];
+#pragma unroll
+            for (int i = 0; i < N; ++i) a = fmaf(wj[i], dr[i][v], a);
+            o[v] = a * hpre[j];
+          }
+          if (dxt) store_vec<XT, 4>(dxt + (int64_t)j * C + 4 * g, o);
+        }
+      }
     }
-    const float r = warp_sum(aS[i]);
-    if (lane == 0) { sacc[warp * P + N * N + i] = 0.f; sacc[warp * P + N * N + N + i] = r; }
+    __syncthreads();  // every read of the pair's buffers done; s_abort agreed
+    if (s_abort) { aborted = true; break; }
+    if (tid == 0) {
+      fence_proxy_async_smem();
+      for (; issued < ntok && issued < k0 + 2 + NS; ++issued) issue(issued);
+    }
   }
-  __syncthreads();
-  for (int e = threadIdx.x; e < P; e += blockDim.x) {
-    float s = 0.f;
-    for (int w = 0; w < nw; ++w) s += sacc[w * P + e];
-    if (fin.on)  // this CTA's share of the dy side's rows (written by the previous launch)
-      for (int r = blockIdx.x; r < row0; r += gridDim.x) s += ws_p[(size_t)r * P + e];
-    ws_p[(size_t)(row0 + blockIdx.x) * P + e] = s;
+  if (aborted) {
+    if (tid == 0)
+      for (int64_t q = k0; q < issued; ++q)
+        (void)mbar_wait(&s_full[q % NS], (unsigned)((q / NS) & 1));
+    const float nan = __int_as_float(0x7fc00000);
+    if (dx) {
+      float o[4] = {nan, nan, nan, nan};
+      for (int64_t k = k0 + hf; k < ntok; k += 2)
+        for (int g = lt; g < groups; g += HB)
+#pragma unroll
+          for (int j = 0; j < N; ++j)
+            store_vec<XT, 4>(dx + (blockIdx.x + k * G) * RS + (int64_t)j * C + 4 * g, o);
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      aS[i] = nan;
+#pragma unroll
+      for (int j = 0; j < N; ++j) aQ[i][j] = nan;
+    }
   }
-  if (!fin.on) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) ws_hdr[2] = gridDim.x;
-    return;
-  }
-  __shared__ int s_last;
-  __threadfence();  // this CTA's row is visible device-wide before its ticket
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(ws_hdr + 3, 1) == (int)gridDim.x - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  rewire_fin_last<N>(ws_p + (size_t)row0 * P, (int)gridDim.x, sM, hpre_g, hpost_g, fin);
-  if (threadIdx.x == 0) ws_hdr[3] = 0;  // the workspace may be finalized again
+  rewire_x_rows<N>(aQ, aS, sM, hpre_g, hpost_g, ws_p, ws_hdr, row0, fin);
 }
 
 // ----------------------------------------------------------- prescale bwd --
@@ -649,6 +844,8 @@ __global__ void __launch_bounds__(kMixBD)
 k_prescale_bwd(const XT* __restrict__ x, const DT* __restrict__ dout,
                const float* __restrict__ hpre_g, DXT* __restrict__ dx, int64_t T, int n, int C,
                float* __restrict__ ws_p, int* __restrict__ ws_hdr) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float shpre[MAXN];
   __shared__ float sacc[(kMixBD / 32) * MAXN];
   const int nr = EXACT ? MAXN : n;
@@ -786,6 +983,8 @@ k_combine_finalize(const char* __restrict__ ws, int n, const float* __restrict__
                    const float* __restrict__ hpre, const float* __restrict__ hpost, int mode,
                    float* __restrict__ dM, float* __restrict__ dhpre, float* __restrict__ dhpost,
                    ParamsBwd pb, int stage_sk) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sQ[kMaxN * kMaxN + 2 * kMaxN];
   __shared__ float sA[kMaxN * kMaxN + 2 * kMaxN];  // [dM | dhpre | dhpost] for the tail
   __shared__ float part[kCFinBD];
@@ -878,7 +1077,7 @@ static int combine_fwd_t(const void* xv, const void* yv, const float* M, const f
   const int cap = sm_count() * 8;
   const int gv = elem_grid(T * (C / VX), cap), g1 = elem_grid(T * C, cap);
 #define MHC_CF(NN, EX, V, G) \
-  k_combine_fwd<NN, EX, XT, YT, OT, V><<<G, kMixBD, 0, st>>>(x, y, M, hpre, hpost, o, T, n, C)
+  launch_pdl(k_combine_fwd<NN, EX, XT, YT, OT, V>, G, kMixBD, 0, st, x, y, M, hpre, hpost, o, T, n, C)
   switch (n) {
     case 1: if (vec) MHC_CF(1, true, VX, gv); else MHC_CF(1, true, 1, g1); break;
     case 2: if (vec) MHC_CF(2, true, VX, gv); else MHC_CF(2, true, 1, g1); break;
@@ -1042,8 +1241,14 @@ static int prescale_fwd_t(const void* xv, const float* hpre, void* ov, int64_t T
   const int cap = sm_count() * 8;
   const int gv = elem_grid(T * (C / VX), cap), g1 = elem_grid(T * C, cap);
   if (pf) {  // n in {1, 2, 4, 8}: one more block for the parameters
+    // with a Jacobian to compute, the tape is staged in shared memory when it
+    // is small (every block gets the allocation: at most 8 KB)
+    ParamsFwd q = *pf;
+    const size_t tb = sk_tape_floats(n, q.iters) * sizeof(float);
+    q.stage = (q.jac && sk_lane_ok(n) && q.iters > 0 && tb <= 8 * 1024) ? 1 : 0;
+    const size_t smem = q.stage ? tb : 0;
 #define MHC_PP(NN, V, G) \
-  k_prescale_fwd<NN, true, XT, OT, V, true><<<G + 1, kMixBD, 0, st>>>(x, nullptr, o, T, n, C, *pf)
+  launch_pdl(k_prescale_fwd<NN, true, XT, OT, V, true>, G + 1, kMixBD, smem, st, x, nullptr, o, T, n, C, q)
     switch (n) {
       case 1: if (vec) MHC_PP(1, VX, gv); else MHC_PP(1, 1, g1); break;
       case 2: if (vec) MHC_PP(2, VX, gv); else MHC_PP(2, 1, g1); break;
@@ -1054,7 +1259,7 @@ static int prescale_fwd_t(const void* xv, const float* hpre, void* ov, int64_t T
     return check_launch("rewire_in_fwd");
   }
 #define MHC_PF(NN, EX, V, G) \
-  k_prescale_fwd<NN, EX, XT, OT, V><<<G, kMixBD, 0, st>>>(x, hpre, o, T, n, C, ParamsFwd{})
+  launch_pdl(k_prescale_fwd<NN, EX, XT, OT, V>, G, kMixBD, 0, st, x, hpre, o, T, n, C, ParamsFwd{})
   switch (n) {
     case 1: if (vec) MHC_PF(1, true, VX, gv); else MHC_PF(1, true, 1, g1); break;
     case 2: if (vec) MHC_PF(2, true, VX, gv); else MHC_PF(2, true, 1, g1); break;
@@ -1116,7 +1321,7 @@ static int prescale_bwd_t(const void* xv, const void* dv, const float* hpre, voi
   const int cap = mix_rows_cap();
   const int gv = elem_grid(T * (C / VX), cap), g1 = elem_grid(T * C, cap);
 #define MHC_PB(NN, EX, V, G) \
-  k_prescale_bwd<NN, EX, XT, DT, XT, V><<<G, kMixBD, 0, st>>>(x, d, hpre, dx, T, n, C, wp, hdr)
+  launch_pdl(k_prescale_bwd<NN, EX, XT, DT, XT, V>, G, kMixBD, 0, st, x, d, hpre, dx, T, n, C, wp, hdr)
   switch (n) {
     case 1: if (vec) MHC_PB(1, true, VX, gv); else MHC_PB(1, true, 1, g1); break;
     case 2: if (vec) MHC_PB(2, true, VX, gv); else MHC_PB(2, true, 1, g1); break;
@@ -1204,11 +1409,42 @@ static int rewire_x_t(const void* xv, const void* dv, const void* pv, const floa
   const int cap = mix_rows_cap();
   const bool vec = (C % VX == 0) && all_aligned({xv, dv, pv, dxv});
   if (vec && (n == 1 || n == 2 || n == 4)) {
-    const int G = elem_grid(T * (C / V4), cap);
     fin.on = aligned16(ws) ? 1 : 0;  // the last CTA's 16-byte row loads
     *finished = fin.on != 0;
+    // Bulk-copy staging when a token's rows are whole 16-byte runs and at
+    // least three tokens fit in the ring (MHC_B200_XBULK=0: the register
+    // kernel below, for comparison).
+    const int64_t RS = (int64_t)n * C;
+    const bool runs16 = C % 4 == 0 && (RS * (int64_t)sizeof(XT)) % 16 == 0 &&
+                        (RS * (int64_t)sizeof(DT)) % 16 == 0 &&
+                        (!pv || (RS * (int64_t)sizeof(PT)) % 16 == 0);
+    const int64_t sb = RS * (int64_t)(sizeof(XT) + sizeof(DT) + (pv ? sizeof(PT) : 0));
+    const int64_t budget = (int64_t)max_smem_optin() - 12 * 1024;  // static shared memory aside
+    const int NS = sb > 0 ? (int)std::min<int64_t>(kXBulkMaxStages, budget / sb) : 0;
+    static const bool bulk_on = [] {
+      const char* v = getenv("MHC_B200_XBULK");
+      return !(v && *v == '0');
+    }();
+    if (bulk_on && runs16 && NS >= 3) {
+      const int G = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(), T));
+      const size_t smem = (size_t)NS * (size_t)sb;
+#define MHC_RB(NN)                                                                            \
+  do {                                                                                        \
+    auto kern = k_rewire_bwd_x_bulk<NN, XT, DT, PT>;                                          \
+    const cudaError_t e = allow_dyn_smem(kern, smem);                                         \
+    if (e != cudaSuccess)                                                                     \
+      return set_error(MHC_ERR_CUDA, "rewire_bwd_x_bulk: %s", cudaGetErrorString(e));        \
+    launch_pdl(kern, G, kXBulkBD, smem, st, x, d, p, M, hpre, hpost, dx, T, C, NS, wp, hdr, fin); \
+  } while (0)
+      if (n == 1) MHC_RB(1);
+      else if (n == 2) MHC_RB(2);
+      else MHC_RB(4);
+#undef MHC_RB
+      return check_launch("rewire_bwd_x_bulk");
+    }
+    const int G = elem_grid(T * (C / V4), cap);
 #define MHC_RX(NN) \
-  k_rewire_bwd_x_fast<NN, XT, DT, PT, V4><<<G, kMixBD, 0, st>>>(x, d, p, M, hpre, hpost, dx, T, C, wp, hdr, fin)
+  launch_pdl(k_rewire_bwd_x_fast<NN, XT, DT, PT, V4>, G, kMixBD, 0, st, x, d, p, M, hpre, hpost, dx, T, C, wp, hdr, fin)
     if (n == 1) MHC_RX(1);
     else if (n == 2) MHC_RX(2);
     else MHC_RX(4);
@@ -1280,8 +1516,8 @@ int launch_rewire_bwd_dx(const void* x, int xdt, const void* d, int ddt, const v
     if (e != cudaSuccess)
       return set_error(MHC_ERR_CUDA, "rewire_bwd_finalize: %s", cudaGetErrorString(e));
   }
-  k_combine_finalize<<<1, kCFinBD, dyn, st>>>(static_cast<const char*>(ws), n, M, hpre, hpost, 3,
-                                              dM, dhpre, dhpost, fold ? pb : ParamsBwd{}, stage);
+  launch_pdl(k_combine_finalize, 1, kCFinBD, dyn, st, static_cast<const char*>(ws), n, M, hpre,
+             hpost, 3, dM, dhpre, dhpost, fold ? pb : ParamsBwd{}, stage);
   r = check_launch("rewire_bwd_finalize");
   if (r != MHC_OK || !pb.any() || fold) return r;
   return launch_params_bwd(pb.hpre_raw, pb.hpost_raw, pb.hres_raw, pb.tape, n, pb.iters, pb.eps,

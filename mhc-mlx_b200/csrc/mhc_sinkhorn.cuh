@@ -307,12 +307,13 @@ __device__ __forceinline__ void sk_forward_lane(const float* __restrict__ H, int
 // d: this lane's entry of dM on entry, of dH_res on exit.  The next
 // iteration's tape entries are loaded before the current one is processed.
 // PACKED: every lane group of NN lanes runs its own cotangent on entry le =
-// lane % NN (the reductions already stay inside a group), and the tape is
-// read through L2 because the same kernel wrote it (sk_jacobian_lane).
+// lane % NN (the reductions already stay inside a group), and the tape was
+// written by the same kernel: l2 = read it through L2 (global memory), else
+// it is in shared memory (sk_jacobian_lane).
 template <int N, bool PACKED = false>
 __device__ __forceinline__ float sk_backward_lane(const float* __restrict__ H,
                                                   const float* __restrict__ tape, int iters,
-                                                  float eps, float d) {
+                                                  float eps, float d, bool l2 = false) {
   constexpr int NN = N * N, TS = NN + 2 * N;
   const int lane = threadIdx.x & 31;
   const int le = PACKED ? lane % NN : lane;
@@ -321,9 +322,15 @@ __device__ __forceinline__ float sk_backward_lane(const float* __restrict__ H,
   auto ld = [&](int k, float& pa, float& r, float& c) {
     const float* tk = tape + (size_t)k * TS;
     if constexpr (PACKED) {
-      pa = __ldcg(tk + le);
-      r = __ldcg(tk + NN + i);
-      c = __ldcg(tk + NN + N + j);
+      if (l2) {
+        pa = __ldcg(tk + le);
+        r = __ldcg(tk + NN + i);
+        c = __ldcg(tk + NN + N + j);
+      } else {
+        pa = tk[le];
+        r = tk[NN + i];
+        c = tk[NN + N + j];
+      }
     } else {
       pa = act ? tk[lane] : 0.f;
       r = tk[NN + i];
@@ -354,7 +361,10 @@ __device__ __forceinline__ float sk_backward_lane(const float* __restrict__ H,
 }
 
 // Transposed Jacobian of the lane-path Sinkhorn at H (n in {1, 2, 4}), from
-// the tape this kernel wrote (visible to the block: the caller syncs first).
+// the tape this kernel wrote (visible to the block: the caller syncs first;
+// l2: the tape is in global memory, else in shared memory -- the latter
+// matters when other blocks saturate DRAM, since every iteration's loads sit
+// on the chain).
 // The backward is linear in dM, so running it on the unit cotangents e_u
 // gives A[u][e] = d(M_u)/d(H_e) and, later, dH_res = sum_u dM[u] A[u][:] as
 // a dot product instead of a reverse sweep (a latency chain of 2 iters
@@ -363,12 +373,12 @@ __device__ __forceinline__ float sk_backward_lane(const float* __restrict__ H,
 template <int N>
 __device__ __forceinline__ void sk_jacobian_lane(const float* __restrict__ H,
                                                  const float* tape, int iters, float eps,
-                                                 float* __restrict__ A) {
+                                                 float* __restrict__ A, bool l2) {
   constexpr int NN = N * N, GPW = 32 / NN;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int u0 = warp * GPW; u0 < NN; u0 += nw * GPW) {  // warp-uniform
     const int u = u0 + lane / NN, le = lane % NN;
-    const float d = sk_backward_lane<N, true>(H, tape, iters, eps, le == u ? 1.f : 0.f);
+    const float d = sk_backward_lane<N, true>(H, tape, iters, eps, le == u ? 1.f : 0.f, l2);
     if (u < NN) A[u * NN + le] = d;
   }
 }
