@@ -688,12 +688,13 @@ __device__ __forceinline__ void lds4(const T* p, float (&o)[4]) {
 // SM takes the tokens b, b + G, ... of the sequence; a token's x, d_out and
 // d_xpre rows are each one contiguous run, so thread 0 stages a whole token
 // with three 1-D bulk copies (plain loads of this GPU's memory) into a ring
-// of NS buffers completing on mbarriers, NS tokens ahead.  The two halves of
-// the CTA take two consecutive tokens of the sequence at a time (16 warps
-// per SM to hide the shared-memory and FMA latencies of ~220 instructions per
-// 4-column group); thread t of a half owns its column groups t, t + 256, ...
-// A pair's buffers are refilled after the block barrier that follows their
-// last reads.  The loads no longer occupy registers, so the bytes in flight
+// of NS buffers completing on mbarriers, NS tokens ahead.  The CTA's TPI
+// parts take TPI consecutive tokens of the sequence per step (16 warps per
+// SM to hide the shared-memory and FMA latencies of ~220 instructions per
+// 4-column group; more tokens per step, fewer block barriers per token);
+// thread t of a part owns its column groups t, t + 512 / TPI, ...  A step's
+// buffers are refilled after the block barrier that follows their last
+// reads.  The loads no longer occupy registers, so the bytes in flight
 // per SM are the ring's.  Waits are bounded: a copy that never lands makes the
 // CTA wait (bounded) for its other copies in flight, write NaN into its dx
 // tokens from there on and into its partial row, so the parameter gradients
@@ -701,7 +702,7 @@ __device__ __forceinline__ void lds4(const T* p, float (&o)[4]) {
 constexpr int kXBulkMaxStages = 8;
 constexpr int kXBulkBD = 512;
 
-template <int N, typename XT, typename DT, typename PT>
+template <int N, typename XT, typename DT, typename PT, int TPI>
 __global__ void __launch_bounds__(kXBulkBD, 1)
 k_rewire_bwd_x_bulk(const XT* __restrict__ x, const DT* __restrict__ dout,
                     const PT* __restrict__ dp, const float* __restrict__ Mg,
@@ -710,7 +711,7 @@ k_rewire_bwd_x_bulk(const XT* __restrict__ x, const DT* __restrict__ dout,
                     int* __restrict__ ws_hdr, RewireFin fin) {
   pdl_wait();
   pdl_trigger();
-  constexpr int HB = kXBulkBD / 2;  // threads per half
+  constexpr int HB = kXBulkBD / TPI;  // threads per token of a step
   extern __shared__ __align__(16) unsigned char s_ring[];
   __shared__ float sM[N * N];
   __shared__ __align__(16) float sWT[N][4];  // sWT[j][i] = M_ij H_post_i
@@ -759,8 +760,8 @@ k_rewire_bwd_x_bulk(const XT* __restrict__ x, const DT* __restrict__ dout,
   const int groups = C / 4;
   int64_t k0 = 0;
   bool aborted = false;
-  for (; k0 < ntok; k0 += 2) {
-    const int64_t k = k0 + hf;  // this half's token of the pair
+  for (; k0 < ntok; k0 += TPI) {
+    const int64_t k = k0 + hf;  // this part's token of the step
     if (k < ntok) {
       const int slot = (int)(k % NS);
       if (!mbar_wait(&s_full[slot], (unsigned)((k / NS) & 1))) s_abort = 1;
@@ -811,7 +812,7 @@ k_rewire_bwd_x_bulk(const XT* __restrict__ x, const DT* __restrict__ dout,
     if (s_abort) { aborted = true; break; }
     if (tid == 0) {
       fence_proxy_async_smem();
-      for (; issued < ntok && issued < k0 + 2 + NS; ++issued) issue(issued);
+      for (; issued < ntok && issued < k0 + TPI + NS; ++issued) issue(issued);
     }
   }
   if (aborted) {
@@ -821,7 +822,7 @@ k_rewire_bwd_x_bulk(const XT* __restrict__ x, const DT* __restrict__ dout,
     const float nan = __int_as_float(0x7fc00000);
     if (dx) {
       float o[4] = {nan, nan, nan, nan};
-      for (int64_t k = k0 + hf; k < ntok; k += 2)
+      for (int64_t k = k0 + hf; k < ntok; k += TPI)
         for (int g = lt; g < groups; g += HB)
 #pragma unroll
           for (int j = 0; j < N; ++j)
@@ -1425,12 +1426,19 @@ static int rewire_x_t(const void* xv, const void* dv, const void* pv, const floa
       const char* v = getenv("MHC_B200_XBULK");
       return !(v && *v == '0');
     }();
-    if (bulk_on && runs16 && NS >= 3) {
+    // tokens per step (MHC_B200_XBULK_TPI: 2 or 4); the ring must hold a step
+    // and at least one token ahead
+    static const int tpi = [] {
+      const char* v = getenv("MHC_B200_XBULK_TPI");
+      return (v && *v == '2') ? 2 : 4;
+    }();
+    if (bulk_on && runs16 && NS >= tpi + 1) {
       const int G = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(), T));
       const size_t smem = (size_t)NS * (size_t)sb;
 #define MHC_RB(NN)                                                                            \
   do {                                                                                        \
-    auto kern = k_rewire_bwd_x_bulk<NN, XT, DT, PT>;                                          \
+    auto kern = tpi == 2 ? k_rewire_bwd_x_bulk<NN, XT, DT, PT, 2>                             \
+                         : k_rewire_bwd_x_bulk<NN, XT, DT, PT, 4>;                            \
     const cudaError_t e = allow_dyn_smem(kern, smem);                                         \
     if (e != cudaSuccess)                                                                     \
       return set_error(MHC_ERR_CUDA, "rewire_bwd_x_bulk: %s", cudaGetErrorString(e));        \
