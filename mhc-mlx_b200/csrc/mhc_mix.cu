@@ -1248,13 +1248,17 @@ static int prescale_fwd_t(const void* xv, const float* hpre, void* ov, int64_t T
     const size_t tb = sk_tape_floats(n, q.iters) * sizeof(float);
     q.stage = (q.jac && sk_lane_ok(n) && q.iters > 0 && tb <= 8 * 1024) ? 1 : 0;
     const size_t smem = q.stage ? tb : 0;
+    // the streaming blocks plus the parameter block fill one wave of 8 per SM
+    // (a streaming block beyond it would start only when the parameter block
+    // ends and finish that much later)
+    const int pv = std::max(1, std::min(gv, cap - 1)), p1 = std::max(1, std::min(g1, cap - 1));
 #define MHC_PP(NN, V, G) \
   launch_pdl(k_prescale_fwd<NN, true, XT, OT, V, true>, G + 1, kMixBD, smem, st, x, nullptr, o, T, n, C, q)
     switch (n) {
-      case 1: if (vec) MHC_PP(1, VX, gv); else MHC_PP(1, 1, g1); break;
-      case 2: if (vec) MHC_PP(2, VX, gv); else MHC_PP(2, 1, g1); break;
-      case 4: if (vec) MHC_PP(4, VX, gv); else MHC_PP(4, 1, g1); break;
-      default: if (vec) MHC_PP(8, VX, gv); else MHC_PP(8, 1, g1); break;
+      case 1: if (vec) MHC_PP(1, VX, pv); else MHC_PP(1, 1, p1); break;
+      case 2: if (vec) MHC_PP(2, VX, pv); else MHC_PP(2, 1, p1); break;
+      case 4: if (vec) MHC_PP(4, VX, pv); else MHC_PP(4, 1, p1); break;
+      default: if (vec) MHC_PP(8, VX, pv); else MHC_PP(8, 1, p1); break;
     }
 #undef MHC_PP
     return check_launch("rewire_in_fwd");
