@@ -333,6 +333,7 @@ def _fused_rewire_ref(x, y, M, hpre, hpost, d, p):
 
 @pytest.mark.parametrize("B,n,C,dt,with_p", [(5, 4, 1024, torch.float32, True),
                                              (5, 4, 1024, torch.bfloat16, True),
+                                             (3, 4, 2048, torch.bfloat16, True),
                                              (3, 4, 1024, torch.bfloat16, False),
                                              (7, 2, 64, torch.float32, True),
                                              (4, 4, 129, torch.float32, True),
@@ -343,7 +344,10 @@ def _fused_rewire_ref(x, y, M, hpre, hpost, d, p):
 def test_rewire_split_backward_kernels_match_oracle(B, n, C, dt, with_p):
     """mhc_rewire_bwd_dy + mhc_rewire_bwd_dx through the C ABI: dy, dx (both
     branches, written once) and dM / dH_pre / dH_post from one reduction,
-    against float64 autograd; d_xpre NULL counts as zero."""
+    against float64 autograd; d_xpre NULL counts as zero.  The shapes reach
+    every x-side kernel: the bulk-copy ring (n <= 4, a few tokens fit in
+    shared memory), the register kernel (n = 4, C = 2048: a 64 KB token
+    leaves room for only three), and the generic tile kernel (other n, C)."""
     from mhc_b200 import _kernels as K
 
     g = torch.Generator().manual_seed(31 * n + C + B)
@@ -406,6 +410,7 @@ def test_rewire_in_fwd_matches_parameter_and_prescale_kernels(T, n, C, dt, iters
 
 
 @pytest.mark.parametrize("T,n,C,dt", [(5, 4, 1024, torch.bfloat16), (4, 4, 129, torch.float32),
+                                      (3, 4, 2048, torch.bfloat16),
                                       (3, 1, 64, torch.float32), (3, 2, 64, torch.float32),
                                       (3, 8, 64, torch.float32), (2, 3, 40, torch.float32),
                                       (2, 16, 64, torch.float32), (2, 32, 64, torch.float32),
